@@ -1,0 +1,686 @@
+"""Benchmark of the paged-KV rollout hot path (append + paged GQA decode attention).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 4] [--impl ours|reference]
+
+One step = one decode step of every sequence through all layers: per layer,
+append one K/V token per (sequence, kv head) and attend over the sequence's
+pages (BASELINE metric: KV-read HBM GB/s and seq-steps/s). Inputs are seeded
+synthetic tensors of the BASELINE config shapes (no dataset is involved) and
+stay resident in HBM; the KV pool (~130 GB per GPU for config 4) is far larger
+than the 126 MB L2, so no L2 flush is needed between steps.
+
+Multi-GPU: one process per GPU (torchrun). Sequences are independent, so the
+job is partitioned — each rank owns a seeded shard of whole sequences
+(LPT-balanced by context length), its own page pool and block tables — and no
+collective runs inside the timed region; only the start barrier and the
+max-over-ranks time reduction cross ranks. Per-GPU work is fixed as N grows
+("scaling": "weak").
+
+Rank 0 prints ONE JSON line. `--impl reference` times the CPU restatement of
+the reference algorithm (oracle/, the reference itself is Python/Triton and
+has no CPU implementation of its own) on the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "paged KV decode: KV-read HBM GB/s and seq-steps/s at 1/2/4/8 B200"
+UNIT = "seq-steps/s"
+
+
+# ----------------------------------------------------------------------------- workloads
+CONFIGS = {
+    3: dict(name="config3: 16 prompts x group 8, shared 512-token prompt pages + U{1..512} private tokens",
+            seqs=128, hq=12, hkv=2, d=128, bs=16, layers=28),
+    4: dict(name="config4: 1024 seqs, ctx U[1024,8192], 12q/2kv, D128, bf16, bs16, 28 layers",
+            seqs=1024, hq=12, hkv=2, d=128, bs=16, layers=28),
+    5: dict(name="config5: Qwen2.5-7B geometry, 64 seqs, ctx log-U[4096,32768], 28q/4kv, D128, bf16, bs16, 28 layers",
+            seqs=64, hq=28, hkv=4, d=128, bs=16, layers=28),
+}
+
+
+def global_lengths(config: int, n_total: int, seed: int = 1234) -> np.ndarray:
+    """Post-append context length of every sequence of the whole job."""
+    rs = np.random.RandomState(seed)
+    if config == 4:
+        return rs.randint(1024, 8193, size=n_total)
+    if config == 5:
+        return np.exp(rs.uniform(np.log(4096), np.log(32768), size=n_total)).astype(np.int64)
+    if config == 3:
+        return 512 + rs.randint(1, 513, size=n_total)
+    raise ValueError(config)
+
+
+class Workload:
+    """One rank's shard: page pool, block tables, per-layer q/k_new/v_new, context lengths."""
+
+    def __init__(self, config: int, rank: int, world: int, layers: int | None, device):
+        from grpo_training_engine_b200.sharding import lpt_assign
+
+        c = CONFIGS[config]
+        self.config, self.cfg = config, c
+        self.layers = layers or c["layers"]
+        hq, hkv, d, bs = c["hq"], c["hkv"], c["d"], c["bs"]
+        n_total = c["seqs"] * world
+        lens = global_lengths(config, n_total)
+        if config == 3:
+            group = 8
+            n_groups = n_total // group
+            costs = [lens[g * group:(g + 1) * group].sum() for g in range(n_groups)]
+            groups = lpt_assign(costs, world)[rank]
+            mine = [g * group + j for g in groups for j in range(group)]
+        else:
+            mine = lpt_assign(lens.tolist(), world)[rank]
+        self.ctx_post = torch.tensor([int(lens[i]) for i in mine], dtype=torch.int32)
+        B = len(mine)
+        self.B, self.hq, self.hkv, self.d, self.bs = B, hq, hkv, d, bs
+        g = torch.Generator(device="cpu").manual_seed(1000 + rank)
+        pages = [(int(n) + bs - 1) // bs for n in self.ctx_post]
+        if config == 3:
+            # each group of 8 shares its 32 full prompt pages (refcounted in a real pool)
+            prompt_pages = 512 // bs
+            tables, nxt = [], 0
+            for gi in range(B // 8):
+                shared = list(range(nxt, nxt + prompt_pages))
+                nxt += prompt_pages
+                for j in range(8):
+                    own = pages[gi * 8 + j] - prompt_pages
+                    tables.append(shared + list(range(nxt, nxt + own)))
+                    nxt += own
+            num_blocks = nxt
+            perm = torch.randperm(num_blocks, generator=g)
+            tables = [[int(perm[p]) for p in t] for t in tables]
+            self.unique_tokens = sum(512 for _ in range(B // 8)) + sum(int(n) - 512 for n in self.ctx_post)
+        else:
+            num_blocks = sum(pages)
+            perm = torch.randperm(num_blocks, generator=g).tolist()
+            tables, off = [], 0
+            for p in pages:
+                tables.append(perm[off:off + p])
+                off += p
+            self.unique_tokens = int(self.ctx_post.sum())
+        self.max_blocks = max(len(t) for t in tables)
+        bt = np.zeros((B, self.max_blocks), dtype=np.int32)
+        for i, t in enumerate(tables):
+            bt[i, : len(t)] = t
+        self.num_blocks = num_blocks
+        self.block_tables_cpu = torch.from_numpy(bt)
+        self.device = device
+        self.block_tables = self.block_tables_cpu.to(device)
+        self.ctx_pre = (self.ctx_post - 1).to(device)
+        self.ctx = self.ctx_post.to(device)
+        # the pool: [layers, pages, hkv, bs, d] bf16, N(0,1)
+        shape = (self.layers, num_blocks, hkv, bs, d)
+        self.k_pool = torch.empty(shape, dtype=torch.bfloat16, device=device)
+        self.v_pool = torch.empty(shape, dtype=torch.bfloat16, device=device)
+        gd = torch.Generator(device=device).manual_seed(77 + rank)
+        for t in (self.k_pool, self.v_pool):
+            for layer in range(self.layers):  # per layer keeps the fp32 temporaries small
+                t[layer].normal_(generator=gd)
+        self.q = torch.randn(self.layers, B, hq, d, device=device, generator=gd).to(torch.bfloat16)
+        self.k_new = torch.randn(self.layers, B, hkv, d, device=device, generator=gd).to(torch.bfloat16)
+        self.v_new = torch.randn(self.layers, B, hkv, d, device=device, generator=gd).to(torch.bfloat16)
+        self.out = torch.empty(self.layers, B, hq, d, dtype=torch.float32, device=device)
+
+    # algorithmic bytes (one layer), the roofline numerator
+    def kv_read_bytes_layer(self) -> int:
+        return int(self.ctx_post.sum()) * self.hkv * self.d * 2 * 2
+
+    def decode_bytes_layer(self) -> int:
+        pages = int(((self.ctx_post + self.bs - 1) // self.bs).sum())
+        return (self.kv_read_bytes_layer() + self.B * self.hq * self.d * (2 + 4) + pages * 4 + self.B * 4)
+
+    def append_bytes_layer(self) -> int:
+        return self.B * self.hkv * self.d * 2 * 2 * 2  # read new K,V + write into pages
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self._t:
+            self._t.join(timeout=2)
+        sm, smax, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(smax) if smax else None,
+            "power_w_max": max(power) if power else None,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+# ----------------------------------------------------------------------------- helpers
+def measured_peaks() -> tuple[float, str]:
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return 6650.0, "fallback"
+
+
+def physical_gpu(local: int) -> int:
+    """nvidia-smi index of this process's GPU (CUDA_VISIBLE_DEVICES may remap it)."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        try:
+            return int(vis.split(",")[local])
+        except (ValueError, IndexError):
+            return local
+    return local
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and args.impl == "ours":
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# ----------------------------------------------------------------------------- our arm
+def run_ours(args, rank, world, local):
+    import grpo_training_engine_b200 as pkv
+    from grpo_training_engine_b200 import ops
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    wl = Workload(args.config, rank, world, args.layers, device)
+    L, B = wl.layers, wl.B
+    stream = torch.cuda.current_stream(device)
+
+    def step(ev_pairs=None):
+        plan = ops.plan_decode(wl.ctx, wl.hq, wl.hkv, wl.d, wl.bs, wl.max_blocks,
+                               pages_per_split=args.pages_per_split)
+        for layer in range(L):
+            kc, vc = wl.k_pool[layer], wl.v_pool[layer]
+            pkv.paged_kv_append(wl.k_new[layer], wl.v_new[layer], kc, vc, wl.block_tables, wl.ctx_pre)
+            if ev_pairs is not None:
+                ev_pairs[layer][0].record(stream)
+            pkv.paged_attention_decode(wl.q[layer], kc, vc, wl.block_tables, wl.ctx, out=wl.out[layer], plan=plan)
+            if ev_pairs is not None:
+                ev_pairs[layer][1].record(stream)
+        return plan
+
+    step()
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(physical_gpu(local))
+    clocks.start()
+    time.sleep(0.3)
+    ev_all = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(L)]
+              for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for s in range(args.steps):
+        step(ev_all[s])
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    ms_local = t0.elapsed_time(t1)
+    ms = max_over_ranks(ms_local, world)
+    decode_ms = [a.elapsed_time(b) for pairs in ev_all for a, b in pairs]
+    decode_avg_ms = sum(decode_ms) / len(decode_ms)
+
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([float(B), float(wl.kv_read_bytes_layer() * L)], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        total_seqs, total_kv = int(t[0].item()), float(t[1].item())
+    else:
+        total_seqs, total_kv = B, float(wl.kv_read_bytes_layer() * L)
+    ms_per_step = ms / args.steps
+    value = total_seqs / (ms_per_step / 1e3)
+    kv_gbs = total_kv / (ms_per_step / 1e3) / 1e9
+
+    peak, peak_kind = measured_peaks()
+    dec_bytes = wl.decode_bytes_layer()
+    achieved = dec_bytes / (decode_avg_ms / 1e3) / 1e9
+    launches = args.steps * (1 + 2 * L)
+
+    # ---- end-to-end through the public ops with pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, wl, world, device)
+
+    # ---- CPU baseline (rank 0, N=1 only)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(wl, args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic: seeded N(0,1) q/K/V/new tokens, seeded context lengths and random page permutations",
+            "config": {
+                "workload": wl.cfg["name"],
+                "seqs_per_gpu": B,
+                "layers": L,
+                "q_heads": wl.hq,
+                "kv_heads": wl.hkv,
+                "head_dim": wl.d,
+                "block_size": wl.bs,
+                "pages_per_split": plan_pps(wl, args),
+                "step": "per layer: append 1 token/seq/kv-head + paged decode attention; 1 plan per step",
+                "l2": "no flush: KV pool per GPU %.1f GB >> 126 MB L2" % (2 * wl.k_pool.numel() * 2 / 1e9),
+                "parallelism": f"dp{world} (sequence shards, LPT by context length, no collective)",
+            },
+            "kv_read_GBps": round(kv_gbs, 1),
+            "kv_read_GBps_per_gpu": round(kv_gbs / world, 1),
+            "roofline": {
+                "kernel": "decode_tc_kernel (one launch = one layer of all sequences)",
+                "bound": "hbm",
+                "achieved": round(achieved, 1),
+                "peak": peak,
+                "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else peak_kind,
+                "unit": "GB/s",
+                "frac": round(achieved / peak, 4),
+                "traffic": args.traffic_bytes,
+                "algorithmic_bytes_per_launch": dec_bytes,
+                "avg_launch_ms": round(decode_avg_ms, 4),
+            },
+            "gpu_launches": launches,
+            "clocks": clk,
+        }
+        if wl.config == 3:
+            line["config"]["unique_kv_GBps"] = round(kv_gbs * wl.unique_tokens / float(wl.ctx_post.sum()), 1)
+        if e2e is not None:
+            line["e2e"] = e2e
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+
+
+def plan_pps(wl, args) -> int:
+    from grpo_training_engine_b200 import _lib
+
+    return int(_lib.load().pkv_decode_pages_per_split(wl.B, wl.hq, wl.hkv, wl.d, wl.max_blocks,
+                                                      args.pages_per_split))
+
+
+def run_e2e(args, wl, world, device):
+    """Same step through the public ops, with per-step inputs copied from pinned host
+    memory (q, k_new, v_new of every layer, context lengths) and outputs copied back
+    (fp32 attention output of every layer), inside the timed region."""
+    import grpo_training_engine_b200 as pkv
+    from grpo_training_engine_b200 import ops
+
+    L = wl.layers
+    q_h = wl.q.cpu().pin_memory()
+    kn_h = wl.k_new.cpu().pin_memory()
+    vn_h = wl.v_new.cpu().pin_memory()
+    ctx_h = wl.ctx_post.clone().pin_memory()
+    out_h = torch.empty(wl.out.shape, dtype=torch.float32).pin_memory()
+    q_d, kn_d, vn_d = torch.empty_like(wl.q), torch.empty_like(wl.k_new), torch.empty_like(wl.v_new)
+    ctx_d = [torch.empty_like(wl.ctx) for _ in range(2)]  # double-buffered across steps
+    out_d = torch.empty_like(wl.out)
+    comp = torch.cuda.current_stream(device)
+    copy = torch.cuda.Stream(device)
+    h2d = [torch.cuda.Event() for _ in range(L)]
+    done = [torch.cuda.Event() for _ in range(L)]
+    d2h = [torch.cuda.Event() for _ in range(L)]
+    ctx_ready = [torch.cuda.Event() for _ in range(2)]
+    ctx_free = [torch.cuda.Event() for _ in range(2)]
+    state = {"step": 0}
+
+    def step(first: bool):
+        s = state["step"]
+        state["step"] += 1
+        buf = s % 2
+        with torch.cuda.stream(copy):
+            if s >= 2:
+                copy.wait_event(ctx_free[buf])  # step s-2 finished reading this buffer
+            ctx_d[buf].copy_(ctx_h, non_blocking=True)
+            ctx_ready[buf].record(copy)
+            for layer in range(L):
+                if not first:
+                    copy.wait_event(done[layer])  # previous step consumed this layer's inputs
+                q_d[layer].copy_(q_h[layer], non_blocking=True)
+                kn_d[layer].copy_(kn_h[layer], non_blocking=True)
+                vn_d[layer].copy_(vn_h[layer], non_blocking=True)
+                h2d[layer].record(copy)
+        comp.wait_event(ctx_ready[buf])
+        ctx = ctx_d[buf]
+        ctx_pre = ctx - 1
+        plan = ops.plan_decode(ctx, wl.hq, wl.hkv, wl.d, wl.bs, wl.max_blocks, pages_per_split=args.pages_per_split)
+        for layer in range(L):
+            comp.wait_event(h2d[layer])
+            if not first:
+                comp.wait_event(d2h[layer])  # previous step's output left the device
+            kc, vc = wl.k_pool[layer], wl.v_pool[layer]
+            pkv.paged_kv_append(kn_d[layer], vn_d[layer], kc, vc, wl.block_tables, ctx_pre)
+            pkv.paged_attention_decode(q_d[layer], kc, vc, wl.block_tables, ctx, out=out_d[layer], plan=plan)
+            done[layer].record(comp)
+            with torch.cuda.stream(copy):
+                copy.wait_event(done[layer])
+                out_h[layer].copy_(out_d[layer], non_blocking=True)
+                d2h[layer].record(copy)
+        ctx_free[buf].record(comp)
+
+    step(True)
+    torch.cuda.synchronize()
+    for _ in range(max(1, args.warmup)):
+        step(False)
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(comp)
+    for _ in range(args.steps):
+        step(False)
+    comp.wait_stream(copy)
+    t1.record(comp)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(t0.elapsed_time(t1), world) / args.steps
+    ok = torch.allclose(out_h[0], wl.out[0].cpu())
+    total = wl.B * world
+    h2d_bytes = (q_h.numel() * 2 + kn_h.numel() * 2 + vn_h.numel() * 2 + ctx_h.numel() * 4)
+    return {
+        "value": round(total / (ms / 1e3), 2),
+        "unit": UNIT,
+        "h2d_bytes_per_step": int(h2d_bytes),
+        "d2h_bytes_per_step": int(out_h.numel() * 4),
+        "ms_per_step": round(ms, 4),
+        "api": "grpo_training_engine_b200.paged_kv_append + paged_attention_decode (C ABI pkv_append / pkv_decode_run)",
+        "output_matches_device_run": bool(ok),
+    }
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def _cpu_sample(wl, n_seqs: int, seed: int = 0):
+    """A bounded CPU copy of n_seqs sequences of one layer (pages copied into a small pool)."""
+    rs = np.random.RandomState(seed)
+    idx = rs.choice(wl.B, size=min(n_seqs, wl.B), replace=False)
+    bt = wl.block_tables_cpu[idx]
+    pages = torch.unique(bt)
+    remap = torch.full((wl.num_blocks,), -1, dtype=torch.int32)
+    remap[pages.long()] = torch.arange(len(pages), dtype=torch.int32)
+    k = wl.k_pool[0, pages.to(wl.device).long()].cpu()
+    v = wl.v_pool[0, pages.to(wl.device).long()].cpu()
+    ctx = wl.ctx_post[idx]
+    bt_small = remap[bt.long()]
+    bt_small[bt_small < 0] = 0
+    q = wl.q[0, idx.tolist()].cpu()
+    kn = wl.k_new[0, idx.tolist()].cpu()
+    vn = wl.v_new[0, idx.tolist()].cpu()
+    return q, k, v, bt_small, ctx, kn, vn
+
+
+def cpu_baseline(wl, seconds: float, nthreads: int = 0) -> dict:
+    """Time the oracle (CPU restatement of the reference kernels) on a bounded sample
+    of this workload: n sequences of one layer, append + 3-pass decode; scaled to
+    seq-steps/s over all layers."""
+    from oracle import oracle
+
+    oracle.build()
+    threads = nthreads or oracle.max_threads()
+    n = 4
+    while True:
+        q, k, v, bt, ctx, kn, vn = _cpu_sample(wl, n)
+        t = time.perf_counter()
+        oracle.append(kn, vn, k, v, bt, ctx - 1)
+        oracle.decode(q, k, v, bt, ctx, nthreads=threads)
+        dt = time.perf_counter() - t
+        if dt * 2 > seconds or n >= wl.B:
+            break
+        n = min(wl.B, max(n * 2, int(n * seconds / max(dt, 1e-3) * 0.5)))
+    per_layer = dt / len(ctx)
+    value = 1.0 / (per_layer * wl.layers)
+    return {
+        "value": round(value, 4),
+        "unit": UNIT,
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{len(ctx)} of {wl.B} sequences x 1 of {wl.layers} layers (append + 3-pass decode, "
+                  f"{dt:.1f} s), scaled linearly to all layers",
+        "cpu": _cpu_name(),
+    }
+
+
+def _cpu_name() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(args, rank, world):
+    """CPU restatement of the reference algorithm on the host cores (the reference is
+    Python/Triton and has no CPU implementation; its kernels only run in Triton's
+    interpreter, which needs the reference checkout and takes ~12 s per config-1 call)."""
+    if rank != 0:
+        return
+    from oracle import oracle
+
+    oracle.build()
+    threads = oracle.max_threads()
+    c = CONFIGS[args.config]
+    # build the same rank-0 workload lengths on the CPU without a GPU pool
+    lens = global_lengths(args.config, c["seqs"] * max(world, 1))
+    from grpo_training_engine_b200.sharding import lpt_assign
+
+    mine = lpt_assign(lens.tolist(), max(world, 1))[0]
+    layers = args.layers or c["layers"]
+    hq, hkv, d, bs = c["hq"], c["hkv"], c["d"], c["bs"]
+    rs = np.random.RandomState(5)
+
+    def sample(n):
+        idx = rs.choice(len(mine), size=min(n, len(mine)), replace=False)
+        ctx = torch.tensor([int(lens[mine[i]]) for i in idx], dtype=torch.int32)
+        pages = [(int(x) + bs - 1) // bs for x in ctx]
+        nb = sum(pages)
+        perm = torch.randperm(nb, generator=torch.Generator().manual_seed(int(rs.randint(1 << 30))))
+        mb = max(pages)
+        bt = torch.zeros(len(idx), mb, dtype=torch.int32)
+        off = 0
+        for i, p in enumerate(pages):
+            bt[i, :p] = perm[off:off + p].int()
+            off += p
+        g = torch.Generator().manual_seed(int(rs.randint(1 << 30)))
+        k = torch.randn(nb, hkv, bs, d, generator=g).to(torch.bfloat16)
+        v = torch.randn(nb, hkv, bs, d, generator=g).to(torch.bfloat16)
+        q = torch.randn(len(idx), hq, d, generator=g).to(torch.bfloat16)
+        kn = torch.randn(len(idx), hkv, d, generator=g).to(torch.bfloat16)
+        vn = torch.randn(len(idx), hkv, d, generator=g).to(torch.bfloat16)
+        return q, k, v, bt, ctx, kn, vn
+
+    def run(s):
+        q, k, v, bt, ctx, kn, vn = s
+        t = time.perf_counter()
+        oracle.append(kn, vn, k, v, bt, ctx - 1)
+        oracle.decode(q, k, v, bt, ctx, nthreads=threads)
+        return time.perf_counter() - t
+
+    # size one step's sample to ~target seconds of CPU work
+    n = max(1, threads // 2)
+    while True:
+        dt = run(sample(n))
+        if dt >= args.ref_step_seconds * 0.5 or n >= len(mine):
+            break
+        n = min(len(mine), max(n + 1, int(n * args.ref_step_seconds / max(dt, 1e-3))))
+    for _ in range(args.warmup):
+        run(sample(n))
+    times, seqs = [], 0
+    for _ in range(args.steps):
+        s = sample(n)
+        times.append(run(s))
+        seqs += len(s[4])
+    total = sum(times)
+    value = seqs / (total * layers)
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 4),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total / args.steps, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) q/K/V, seeded context lengths and page permutations",
+        "config": {"workload": c["name"], "layers": layers, "q_heads": hq, "kv_heads": hkv, "head_dim": d,
+                   "block_size": bs},
+        "cpu_baseline": {
+            "value": round(value, 4),
+            "unit": UNIT,
+            "cores": threads,
+            "kind": "port",
+            "sample": f"each step: {n} sequences of the rank-0 shard x 1 layer (append + 3-pass decode), "
+                      f"seq-steps/s scaled to {layers} layers",
+            "cpu": _cpu_name(),
+        },
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=60)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", type=int, default=4, choices=sorted(CONFIGS))
+    ap.add_argument("--layers", type=int, default=None, help="override the layer count (diagnostics only)")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--pages-per-split", type=int, default=0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--ref-step-seconds", type=float, default=1.0)
+    ap.add_argument("--traffic-bytes", type=float, default=None,
+                    help="DRAM bytes per decode launch from an ncu capture, reported as roofline.traffic")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank, world, local = dist_setup(args)
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    try:
+        run_ours(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

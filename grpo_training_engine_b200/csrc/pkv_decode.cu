@@ -1,0 +1,1075 @@
+// pkv_decode.cu — paged-KV single-query decode attention for sm_100a.
+//
+// Computes, for every sequence b and query head h,
+//     out[b, h, :] = sum_{t < ctx_b} softmax_t(scale * q[b,h] . K[t]) V[t]
+// over the pages listed in block_tables[b], with fp32 accumulation, fp32
+// output and out = acc / max(sum, 1e-6) — the arithmetic of the reference's
+// _paged_attention_decode_kernel (src/triton_kernels/paged_kv.py:63-251).
+// The reference makes three passes over K (max, sum, weighted V,
+// paged_kv.py:97-251) per query head; this file makes ONE pass with an online
+// (running max) softmax and lets one CTA serve all G = Hq / Hkv query heads
+// that share a KV head, so every K/V byte is read from HBM once.
+//
+// Work decomposition (shared by both kernels):
+//   plan kernel   : per sequence, n_b = ceil(pages_b / P) chunks of P pages
+//                   ("splits"); a flat item list (b, split) is written into the
+//                   caller's workspace together with per-sequence offsets and
+//                   zeroed arrival counters.
+//   decode kernel : persistent CTAs stride over work units
+//                   (item, kv head, head group). A unit whose sequence has one
+//                   split writes the final output; otherwise it writes a
+//                   partial (max, sum, acc) and the last unit of the sequence
+//                   to arrive (atomic counter) merges all partials.
+//
+// Two decode kernels:
+//   decode_tc_kernel      bf16/fp16 cache, block_size 16, head_dim 64/128.
+//                         One producer warp streams K and V pages with bulk
+//                         tensor copies (TMA, 128-byte swizzle) into
+//                         per-consumer-warp smem rings guarded by mbarriers;
+//                         consumer warps compute q.K^T and P.V with
+//                         m16n8k16 tensor-core MMAs (query heads on M).
+//   decode_generic_kernel any dtype (fp32/bf16/fp16), any block size,
+//                         head_dim <= 256: CUDA-core FMAs, plain coalesced
+//                         loads, per-warp online softmax.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "pkv_common.cuh"
+
+namespace pkv {
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kTcRows = 16;   // query heads per head group in the tensor-core kernel (MMA M)
+constexpr int kGenThreads = 128;
+constexpr int kGenWarps = kGenThreads / 32;
+
+// ---------------------------------------------------------------------------
+// workspace layout
+// ---------------------------------------------------------------------------
+struct WsLayout {
+  size_t hdr, seq_off, seq_nsplit, items, counters, partials, total;
+  int64_t max_items;
+  int32_t units_per_item;  // num_kv_heads * head_groups
+  int32_t group_rows;      // query heads per head group (partial row count)
+  int32_t part_floats;     // floats per partial unit
+};
+
+__host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+inline int32_t group_rows_for(int32_t G, int32_t D) {
+  // Rows per head group: 16 (one MMA M tile) in general; the CUDA-core kernel
+  // keeps G x D/32 accumulators per lane, so wide heads use groups of 8.
+  int32_t cap = D > 128 ? 8 : kTcRows;
+  return G < cap ? G : cap;
+}
+
+WsLayout ws_layout(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t max_blocks, int32_t P) {
+  WsLayout w{};
+  const int32_t G = Hq / Hkv;
+  w.group_rows = group_rows_for(G, D);
+  const int32_t HG = (G + w.group_rows - 1) / w.group_rows;
+  w.units_per_item = Hkv * HG;
+  const int64_t per_seq = max_blocks > 0 ? (max_blocks + P - 1) / P : 1;
+  w.max_items = (int64_t)B * per_seq;
+  w.part_floats = w.group_rows * (D + 2);
+  size_t off = 0;
+  w.hdr = off; off += 256;
+  w.seq_off = off; off = align_up(off + sizeof(int32_t) * (size_t)B, 256);
+  w.seq_nsplit = off; off = align_up(off + sizeof(int32_t) * (size_t)B, 256);
+  w.items = off; off = align_up(off + sizeof(int2) * (size_t)w.max_items, 256);
+  w.counters = off; off = align_up(off + sizeof(int32_t) * (size_t)B * w.units_per_item, 256);
+  w.partials = off;
+  off = align_up(off + sizeof(float) * (size_t)w.max_items * w.units_per_item * w.part_floats, 256);
+  w.total = off;
+  return w;
+}
+
+// ---------------------------------------------------------------------------
+// kernel arguments
+// ---------------------------------------------------------------------------
+struct DecodeArgs {
+  const void *q;
+  const int32_t *bt;
+  const int32_t *ctx;
+  float *out;
+  const void *kc;  // generic kernel only (the tensor-core kernel reads through TMA)
+  const void *vc;
+  int32_t B, Hq, Hkv, G, GR, HG, D, bs, num_blocks, max_blocks, P, upi, part_floats;
+  int32_t q_dtype, kv_dtype;
+  int64_t q0, q1, q2;
+  int64_t c0, c1, c2, c3;
+  int64_t bt0, bt1;
+  int64_t o0, o1, o2;
+  float scale, scale_log2;
+  const int32_t *hdr;
+  const int32_t *seq_off;
+  const int32_t *seq_nsplit;
+  const int2 *items;
+  int32_t *counters;
+  float *partials;
+  int32_t *status;
+};
+
+__device__ __forceinline__ int32_t clamp_ctx(const DecodeArgs &a, int32_t b) {
+  int32_t c = a.ctx[b];
+  const int32_t cap = a.max_blocks * a.bs;
+  return c < 0 ? 0 : (c > cap ? cap : c);
+}
+
+struct Unit {
+  int32_t b, s, kvh, hg, nsplit, ctx, p_begin, p_end, gcount, qh0;
+};
+
+__device__ __forceinline__ Unit decode_unit(const DecodeArgs &a, int32_t w) {
+  Unit u;
+  const int32_t item = w / a.upi;
+  const int32_t r = w - item * a.upi;
+  u.kvh = r / a.HG;
+  u.hg = r - u.kvh * a.HG;
+  const int2 it = a.items[item];
+  u.b = it.x;
+  u.s = it.y;
+  u.nsplit = a.seq_nsplit[u.b];
+  u.ctx = clamp_ctx(a, u.b);
+  const int32_t npages = (u.ctx + a.bs - 1) / a.bs;
+  u.p_begin = u.s * a.P;
+  u.p_end = min(u.p_begin + a.P, npages);
+  if (u.p_end < u.p_begin) u.p_end = u.p_begin;
+  const int32_t g0 = u.hg * a.GR;
+  u.gcount = min(a.GR, a.G - g0);
+  u.qh0 = u.kvh * a.G + g0;
+  return u;
+}
+
+// ---------------------------------------------------------------------------
+// plan: per-sequence split counts, prefix offsets, item list, zeroed counters
+// ---------------------------------------------------------------------------
+constexpr int kPlanThreads = 1024;
+
+__global__ void __launch_bounds__(kPlanThreads)
+plan_kernel(const int32_t *__restrict__ ctx, int32_t B, int32_t bs, int32_t max_blocks, int32_t P,
+            int32_t upi, int32_t *hdr, int32_t *seq_off, int32_t *seq_nsplit, int2 *items,
+            int32_t *counters, int32_t *status) {
+  __shared__ int32_t warp_tot[kPlanThreads / 32];
+  __shared__ int32_t carry;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t ncount = (int64_t)B * upi;
+  for (int64_t i = tid; i < ncount; i += kPlanThreads) counters[i] = 0;
+  if (tid == 0) carry = 0;
+  __syncthreads();
+  const int32_t cap = max_blocks * bs;
+  for (int32_t base = 0; base < B; base += kPlanThreads) {
+    const int32_t b = base + tid;
+    int32_t n = 0;
+    if (b < B) {
+      int32_t c = ctx[b];
+      if (c < 0 || c > cap) {
+        flag_status(status, PKV_DEV_CTX_OUT_OF_RANGE);
+        c = c < 0 ? 0 : cap;
+      }
+      const int32_t pages = (c + bs - 1) / bs;
+      n = pages > 0 ? (pages + P - 1) / P : 1;
+    }
+    // block-wide exclusive scan of n
+    int32_t x = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      int32_t t = warp_tot[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        int32_t y = __shfl_up_sync(0xffffffffu, t, o);
+        if (lane >= o) t += y;
+      }
+      warp_tot[lane] = t;  // inclusive totals per warp
+    }
+    __syncthreads();
+    const int32_t excl = carry + (warp > 0 ? warp_tot[warp - 1] : 0) + x - n;
+    if (b < B) {
+      seq_off[b] = excl;
+      seq_nsplit[b] = n;
+      for (int32_t s = 0; s < n; ++s) items[excl + s] = make_int2(b, s);
+    }
+    __syncthreads();
+    if (tid == 0) carry += warp_tot[kPlanThreads / 32 - 1];
+    __syncthreads();
+  }
+  if (tid == 0) {
+    hdr[0] = carry * upi;  // total work units
+    hdr[1] = P;
+    hdr[2] = B;
+    hdr[3] = upi;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// split-K epilogue shared by both kernels.
+// xm/xl hold each warp's running max (log2 units) and sum per head row, xo
+// each warp's unnormalised accumulator; rows are [warp][row], xo rows padded
+// to xd floats. `sync` is a barrier over the participating threads.
+// ---------------------------------------------------------------------------
+template <typename Sync>
+__device__ bool unit_epilogue(const DecodeArgs &a, const Unit &u, int nwarps, const float *xm,
+                              const float *xl, const float *xo, int xd, int tid, int nthreads,
+                              int32_t *flag_smem, Sync &sync) {
+  const int32_t D = a.D;
+  const int32_t GR = a.GR;
+  const int32_t n = u.gcount * D;
+  const int64_t unit_idx = (int64_t)(a.seq_off[u.b] + u.s) * a.upi + u.kvh * a.HG + u.hg;
+  float *part = a.partials + unit_idx * a.part_floats;
+  for (int32_t i = tid; i < n; i += nthreads) {
+    const int32_t g = i / D, d = i - g * D;
+    float M = -INFINITY;
+    for (int w = 0; w < nwarps; ++w) M = fmaxf(M, xm[w * kTcRows + g]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+      for (int w = 0; w < nwarps; ++w) {
+        const float f = exp2_or_zero(xm[w * kTcRows + g] - M);
+        L += f * xl[w * kTcRows + g];
+        O += f * xo[(w * kTcRows + g) * xd + d];
+      }
+    }
+    if (u.nsplit == 1) {
+      a.out[u.b * a.o0 + (int64_t)(u.qh0 + g) * a.o1 + d * a.o2] = O / fmaxf(L, 1e-6f);
+    } else {
+      part[2 * GR + g * D + d] = O;
+      if (d == 0) {
+        part[g] = M;
+        part[GR + g] = L;
+      }
+    }
+  }
+  if (u.nsplit == 1) return sync();
+  __threadfence();
+  if (!sync()) return false;
+  if (tid == 0) {
+    const int old = atomicAdd(&a.counters[((int64_t)u.b * a.Hkv + u.kvh) * a.HG + u.hg], 1);
+    *flag_smem = (old == u.nsplit - 1);
+  }
+  if (!sync()) return false;
+  if (*flag_smem) {
+    __threadfence();
+    const int64_t base = (int64_t)a.seq_off[u.b] * a.upi + u.kvh * a.HG + u.hg;
+    for (int32_t i = tid; i < n; i += nthreads) {
+      const int32_t g = i / D, d = i - g * D;
+      float M = -INFINITY;
+      for (int32_t s = 0; s < u.nsplit; ++s)
+        M = fmaxf(M, __ldcg(a.partials + (base + (int64_t)s * a.upi) * a.part_floats + g));
+      float L = 0.f, O = 0.f;
+      if (M != -INFINITY) {
+        for (int32_t s = 0; s < u.nsplit; ++s) {
+          const float *p = a.partials + (base + (int64_t)s * a.upi) * a.part_floats;
+          const float f = exp2_or_zero(__ldcg(p + g) - M);
+          L += f * __ldcg(p + GR + g);
+          O += f * __ldcg(p + 2 * GR + g * D + d);
+        }
+      }
+      a.out[u.b * a.o0 + (int64_t)(u.qh0 + g) * a.o1 + d * a.o2] = O / fmaxf(L, 1e-6f);
+    }
+  }
+  return sync();
+}
+
+struct CtaSync {
+  __device__ bool operator()() {
+    __syncthreads();
+    return true;
+  }
+};
+
+// Barrier over the consumer warps of the tensor-core kernel, built on an
+// mbarrier (one arrival per warp) so that every wait is bounded.
+struct GroupSync {
+  uint64_t *bar;
+  uint32_t phase;
+  int32_t *status;
+  __device__ bool operator()() {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+    const bool ok = mbar_wait_bounded(bar, phase & 1u);
+    ++phase;
+    if (!ok) flag_status(status, PKV_DEV_WAIT_TIMEOUT);
+    return ok;
+  }
+};
+
+// ---------------------------------------------------------------------------
+// CUDA-core kernel (any dtype, any block size, head_dim <= 32*DJ)
+// ---------------------------------------------------------------------------
+template <typename KT, int DJ, int GM>
+__global__ void __launch_bounds__(kGenThreads)
+decode_generic_kernel(DecodeArgs a) {
+  extern __shared__ float gsm[];
+  constexpr int DP = DJ * 32;
+  float *q_s = gsm;                          // [GM][DP]
+  float *xm = q_s + GM * DP;                 // [NW][16]
+  float *xl = xm + kGenWarps * kTcRows;      // [NW][16]
+  float *xo = xl + kGenWarps * kTcRows;      // [NW][16][DP]
+  int32_t *flag = reinterpret_cast<int32_t *>(xo + kGenWarps * kTcRows * DP);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const KT *kc = reinterpret_cast<const KT *>(a.kc);
+  const KT *vc = reinterpret_cast<const KT *>(a.vc);
+  const int32_t total = a.hdr[0];
+  CtaSync sync;
+
+  for (int32_t w = blockIdx.x; w < total; w += gridDim.x) {
+    const Unit u = decode_unit(a, w);
+    for (int i = tid; i < GM * DP; i += kGenThreads) {
+      const int g = i / DP, d = i - g * DP;
+      float v = 0.f;
+      if (g < u.gcount && d < a.D)
+        v = load_as_f32(a.q, u.b * a.q0 + (int64_t)(u.qh0 + g) * a.q1 + d * a.q2, a.q_dtype);
+      q_s[i] = v;
+    }
+    __syncthreads();
+
+    float m[GM], l[GM], acc[GM][DJ];
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+      m[g] = -INFINITY;
+      l[g] = 0.f;
+#pragma unroll
+      for (int j = 0; j < DJ; ++j) acc[g][j] = 0.f;
+    }
+
+    const int32_t t_begin = u.p_begin * a.bs;
+    const int32_t t_end = min(u.p_end * a.bs, u.ctx);
+    for (int32_t t = t_begin + warp; t < t_end; t += kGenWarps) {
+      const int32_t pg = t / a.bs;
+      const int32_t page = a.bt[u.b * a.bt0 + (int64_t)pg * a.bt1];
+      if (page < 0 || page >= a.num_blocks) {
+        if (lane == 0) flag_status(a.status, PKV_DEV_PAGE_OUT_OF_RANGE);
+        continue;
+      }
+      const int64_t base = page * a.c0 + u.kvh * a.c1 + (int64_t)(t - pg * a.bs) * a.c2;
+      float kr[DJ], vr[DJ];
+#pragma unroll
+      for (int j = 0; j < DJ; ++j) {
+        const int d = lane + 32 * j;
+        kr[j] = d < a.D ? Elem<KT>::to_f32(kc[base + d * a.c3]) : 0.f;
+        vr[j] = d < a.D ? Elem<KT>::to_f32(vc[base + d * a.c3]) : 0.f;
+      }
+#pragma unroll
+      for (int g = 0; g < GM; ++g) {
+        if (g < u.gcount) {
+          float s = 0.f;
+#pragma unroll
+          for (int j = 0; j < DJ; ++j) s = fmaf(q_s[g * DP + lane + 32 * j], kr[j], s);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+          // reference order: logits = (q . k) * scale (paged_kv.py:133-135)
+          const float x = (s * a.scale) * kLog2e;
+          const float mn = fmaxf(m[g], x);
+          const float alpha = (mn == m[g]) ? 1.f : exp2_or_zero(m[g] - mn);
+          const float p = exp2f(x - mn);
+          l[g] = l[g] * alpha + p;
+#pragma unroll
+          for (int j = 0; j < DJ; ++j) acc[g][j] = fmaf(p, vr[j], acc[g][j] * alpha);
+          m[g] = mn;
+        }
+      }
+    }
+
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+      if (g < u.gcount) {
+        if (lane == 0) {
+          xm[warp * kTcRows + g] = m[g];
+          xl[warp * kTcRows + g] = l[g];
+        }
+#pragma unroll
+        for (int j = 0; j < DJ; ++j) xo[(warp * kTcRows + g) * DP + lane + 32 * j] = acc[g][j];
+      }
+    }
+    __syncthreads();
+    unit_epilogue(a, u, kGenWarps, xm, xl, xo, DP, tid, kGenThreads, flag, sync);
+  }
+}
+
+size_t generic_smem_bytes(int DJ, int GM) {
+  const int DP = DJ * 32;
+  return sizeof(float) * ((size_t)GM * DP + 2 * kGenWarps * kTcRows + (size_t)kGenWarps * kTcRows * DP) +
+         16;
+}
+
+// ---------------------------------------------------------------------------
+// TMA + tensor-core kernel (bf16 / fp16 cache, block_size 16, head_dim 64/128)
+// ---------------------------------------------------------------------------
+enum : int32_t { kElemPage = 0, kElemEmpty = 1, kElemStop = 2 };
+
+struct __align__(16) SlotMeta {
+  int32_t kind;   // kElemPage / kElemEmpty / kElemStop
+  int32_t valid;  // valid tokens in the page (1..16)
+  int32_t last;   // last element of this warp for the current unit
+  int32_t work;   // work-unit id
+};
+
+constexpr int kBoxRows = 16;                 // tokens per page (block_size)
+constexpr int kBoxBytes = kBoxRows * 128;    // one [16][64] bf16 box, 128-byte swizzled rows
+
+template <int D> struct TcShape {
+  static constexpr int kBoxes = D / 64;
+  static constexpr int kTile = kBoxes * kBoxBytes;  // one K (or V) page of one head
+  static constexpr int kSlot = 2 * kTile;           // K + V
+  static constexpr int kKSteps = D / 16;
+  static constexpr int kNTiles = D / 8;
+  static constexpr int kXd = D + 4;  // padded exchange row (floats)
+};
+
+// Byte address inside a TMA tile with 128-byte swizzle: 16-byte chunk c of row r
+// lands at chunk c ^ (r % 8) of that row (tile base is 1024-byte aligned).
+__device__ __forceinline__ uint32_t swz(uint32_t tile, int r, int d0) {
+  const int box = d0 >> 6;
+  const int c = (d0 & 63) >> 3;
+  return tile + box * kBoxBytes + r * 128 + ((c ^ (r & 7)) << 4);
+}
+
+template <int D, int NW, int S>
+struct TcSmem {
+  static constexpr size_t kTiles = (size_t)NW * S * TcShape<D>::kSlot;
+  static constexpr size_t kMeta = kTiles;
+  static constexpr size_t kFull = kMeta + sizeof(SlotMeta) * NW * S;
+  static constexpr size_t kEmpty = kFull + 8 * NW * S;
+  static constexpr size_t kGroup = kEmpty + 8 * NW * S;
+  static constexpr size_t kFlag = kGroup + 8;
+  static constexpr size_t kXm = align_up(kFlag + 8, 16);
+  static constexpr size_t kXl = kXm + sizeof(float) * NW * kTcRows;
+  static constexpr size_t kXo = kXl + sizeof(float) * NW * kTcRows;
+  static constexpr size_t kBt = kXo + sizeof(float) * NW * kTcRows * TcShape<D>::kXd;
+  static size_t bytes(int32_t P) { return kBt + sizeof(int32_t) * (size_t)P + 1024; }
+};
+
+template <typename T, int D, int NW, int S>
+__global__ void __launch_bounds__((NW + 1) * 32, 1)
+decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                 DecodeArgs a) {
+  using Sh = TcShape<D>;
+  using L = TcSmem<D, NW, S>;
+  extern __shared__ uint8_t tc_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t *tiles = smem;
+  SlotMeta *meta = reinterpret_cast<SlotMeta *>(smem + L::kMeta);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::kFull);
+  uint64_t *empty = reinterpret_cast<uint64_t *>(smem + L::kEmpty);
+  uint64_t *group = reinterpret_cast<uint64_t *>(smem + L::kGroup);
+  int32_t *flag = reinterpret_cast<int32_t *>(smem + L::kFlag);
+  float *xm = reinterpret_cast<float *>(smem + L::kXm);
+  float *xl = reinterpret_cast<float *>(smem + L::kXl);
+  float *xo = reinterpret_cast<float *>(smem + L::kXo);
+  int32_t *btbuf = reinterpret_cast<int32_t *>(smem + L::kBt);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) {
+    for (int i = 0; i < NW * S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(group, NW);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const int32_t total = a.hdr[0];
+
+  if (warp == NW) {
+    // ======================= producer warp =======================
+    int32_t kcount[NW];
+#pragma unroll
+    for (int i = 0; i < NW; ++i) kcount[i] = 0;
+    bool ok = true;
+    for (int32_t w = blockIdx.x; w < total && ok; w += gridDim.x) {
+      const Unit u = decode_unit(a, w);
+      const int32_t npages = u.p_end - u.p_begin;
+      for (int32_t i = lane; i < npages; i += 32) {
+        int32_t page = a.bt[u.b * a.bt0 + (int64_t)(u.p_begin + i) * a.bt1];
+        if (page < 0 || page >= a.num_blocks) {
+          flag_status(a.status, PKV_DEV_PAGE_OUT_OF_RANGE);
+          page = -1;
+        }
+        btbuf[i] = page;
+      }
+      __syncwarp();
+      if (lane == 0) {
+        const int32_t rounds = npages > 0 ? (npages + NW - 1) / NW : 1;
+        for (int32_t j = 0; j < rounds && ok; ++j) {
+#pragma unroll
+          for (int cw = 0; cw < NW; ++cw) {
+            const int32_t pi = j * NW + cw;
+            const bool has = pi < npages;
+            const bool last = (j == rounds - 1);
+            if (!has && !last) continue;
+            const int32_t k = kcount[cw]++;
+            const int slot = cw * S + (k % S);
+            const int32_t use = k / S;
+            if (use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) {
+              flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
+              ok = false;
+              break;
+            }
+            const int32_t page = has ? btbuf[pi] : -1;
+            SlotMeta md;
+            md.kind = page >= 0 ? kElemPage : kElemEmpty;
+            md.valid = has ? min(kBoxRows, u.ctx - (u.p_begin + pi) * kBoxRows) : 0;
+            md.last = last ? 1 : 0;
+            md.work = w;
+            meta[slot] = md;
+            if (page >= 0) {
+              mbar_arrive_expect_tx(&full[slot], Sh::kSlot);
+              uint8_t *kt = tiles + (size_t)slot * Sh::kSlot;
+#pragma unroll
+              for (int bx = 0; bx < Sh::kBoxes; ++bx) {
+                tma_load_4d(kt + bx * kBoxBytes, &tmk, &full[slot], bx * 64, 0, u.kvh, page);
+                tma_load_4d(kt + Sh::kTile + bx * kBoxBytes, &tmv, &full[slot], bx * 64, 0, u.kvh,
+                            page);
+              }
+            } else {
+              mbar_arrive(&full[slot]);
+            }
+          }
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      __syncwarp();  // btbuf is rewritten for the next unit
+    }
+    if (lane == 0 && ok) {
+#pragma unroll
+      for (int cw = 0; cw < NW; ++cw) {
+        const int32_t k = kcount[cw]++;
+        const int slot = cw * S + (k % S);
+        const int32_t use = k / S;
+        if (use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) {
+          flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
+          break;
+        }
+        SlotMeta md{kElemStop, 0, 1, -1};
+        meta[slot] = md;
+        mbar_arrive(&full[slot]);
+      }
+    }
+    return;
+  }
+
+  // ======================= consumer warps =======================
+  using M = Mma16816<T>;
+  const int cw = warp;
+  const int r1 = lane >> 2, r2 = r1 + 8, cq = 2 * (lane & 3);
+  const uint16_t *qraw = reinterpret_cast<const uint16_t *>(a.q);
+  GroupSync sync{group, 0u, a.status};
+
+  uint32_t qa[Sh::kKSteps][4];
+  float o[Sh::kNTiles][4];
+  float m1 = -INFINITY, m2 = -INFINITY, l1 = 0.f, l2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < Sh::kNTiles; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  int32_t cur_work = -1;
+  Unit u{};
+
+  for (int32_t k = 0;; ++k) {
+    const int slot = cw * S + (k % S);
+    if (!mbar_wait_bounded(&full[slot], (k / S) & 1)) {
+      flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
+      return;
+    }
+    const SlotMeta md = meta[slot];
+    if (md.kind == kElemStop) break;
+    if (md.work != cur_work) {
+      cur_work = md.work;
+      u = decode_unit(a, md.work);
+      // query fragments (A operand): rows = head group rows, cols = head_dim
+      const int64_t qb = u.b * a.q0;
+#pragma unroll
+      for (int ks = 0; ks < Sh::kKSteps; ++ks) {
+        const int c = ks * 16 + cq;
+        auto ld2 = [&](int r, int cc) -> uint32_t {
+          if (r >= u.gcount) return 0u;
+          const int64_t base = qb + (int64_t)(u.qh0 + r) * a.q1;
+          const uint32_t lo = qraw[base + (int64_t)cc * a.q2];
+          const uint32_t hi = qraw[base + (int64_t)(cc + 1) * a.q2];
+          return lo | (hi << 16);
+        };
+        qa[ks][0] = ld2(r1, c);
+        qa[ks][1] = ld2(r2, c);
+        qa[ks][2] = ld2(r1, c + 8);
+        qa[ks][3] = ld2(r2, c + 8);
+      }
+    }
+
+    if (md.kind == kElemPage) {
+      const uint32_t kt = smem_u32(tiles + (size_t)slot * Sh::kSlot);
+      const uint32_t vt = kt + Sh::kTile;
+      // ---- S = Q K^T for the 16 tokens of the page (two n-tiles of 8 tokens)
+      float sacc[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
+#pragma unroll
+        for (int kp = 0; kp < Sh::kKSteps / 2; ++kp) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(swz(kt, nt * 8 + (lane & 7), kp * 32 + 8 * (lane >> 3)), b0, b1, b2, b3);
+          M::run(sacc[nt], qa[2 * kp][0], qa[2 * kp][1], qa[2 * kp][2], qa[2 * kp][3], b0, b1);
+          M::run(sacc[nt], qa[2 * kp + 1][0], qa[2 * kp + 1][1], qa[2 * kp + 1][2],
+                 qa[2 * kp + 1][3], b2, b3);
+        }
+      }
+      // ---- online softmax over the page (rows r1, r2; four tokens per lane)
+      float x1[4], x2[4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const bool ok = nt * 8 + cq + j < md.valid;
+          x1[nt * 2 + j] = ok ? (sacc[nt][j] * a.scale) * kLog2e : -INFINITY;
+          x2[nt * 2 + j] = ok ? (sacc[nt][2 + j] * a.scale) * kLog2e : -INFINITY;
+        }
+      }
+      float mx1 = fmaxf(fmaxf(x1[0], x1[1]), fmaxf(x1[2], x1[3]));
+      float mx2 = fmaxf(fmaxf(x2[0], x2[1]), fmaxf(x2[2], x2[3]));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      mx2 = fmaxf(mx2, __shfl_xor_sync(0xffffffffu, mx2, 1));
+      mx2 = fmaxf(mx2, __shfl_xor_sync(0xffffffffu, mx2, 2));
+      const float n1 = fmaxf(m1, mx1), n2 = fmaxf(m2, mx2);
+      const float al1 = (n1 == m1) ? 1.f : exp2_or_zero(m1 - n1);
+      const float al2 = (n2 == m2) ? 1.f : exp2_or_zero(m2 - n2);
+      float p1[4], p2[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        p1[i] = n1 == -INFINITY ? 0.f : exp2_or_zero(x1[i] - n1);
+        p2[i] = n2 == -INFINITY ? 0.f : exp2_or_zero(x2[i] - n2);
+      }
+      l1 = l1 * al1 + ((p1[0] + p1[1]) + (p1[2] + p1[3]));
+      l2 = l2 * al2 + ((p2[0] + p2[1]) + (p2[2] + p2[3]));
+      m1 = n1;
+      m2 = n2;
+#pragma unroll
+      for (int i = 0; i < Sh::kNTiles; ++i) {
+        o[i][0] *= al1;
+        o[i][1] *= al1;
+        o[i][2] *= al2;
+        o[i][3] *= al2;
+      }
+      // ---- O += P V (P as the A operand straight from the S fragments)
+      const uint32_t pa0 = M::pack(p1[0], p1[1]);
+      const uint32_t pa1 = M::pack(p2[0], p2[1]);
+      const uint32_t pa2 = M::pack(p1[2], p1[3]);
+      const uint32_t pa3 = M::pack(p2[2], p2[3]);
+#pragma unroll
+      for (int np = 0; np < Sh::kNTiles / 2; ++np) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_trans(swz(vt, ((lane >> 3) & 1) * 8 + (lane & 7), 8 * (2 * np + (lane >> 4))), b0,
+                      b1, b2, b3);
+        M::run(o[2 * np], pa0, pa1, pa2, pa3, b0, b1);
+        M::run(o[2 * np + 1], pa0, pa1, pa2, pa3, b2, b3);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+
+    if (md.last) {
+      // ---- this warp is done with the unit: publish its state, then combine
+      float s1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
+      s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+      float s2 = l2 + __shfl_xor_sync(0xffffffffu, l2, 1);
+      s2 += __shfl_xor_sync(0xffffffffu, s2, 2);
+      if ((lane & 3) == 0) {
+        if (r1 < u.gcount) {
+          xm[cw * kTcRows + r1] = m1;
+          xl[cw * kTcRows + r1] = s1;
+        }
+        if (r2 < u.gcount) {
+          xm[cw * kTcRows + r2] = m2;
+          xl[cw * kTcRows + r2] = s2;
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < Sh::kNTiles; ++nt) {
+        const int d = nt * 8 + cq;
+        if (r1 < u.gcount)
+          *reinterpret_cast<float2 *>(&xo[(cw * kTcRows + r1) * Sh::kXd + d]) =
+              make_float2(o[nt][0], o[nt][1]);
+        if (r2 < u.gcount)
+          *reinterpret_cast<float2 *>(&xo[(cw * kTcRows + r2) * Sh::kXd + d]) =
+              make_float2(o[nt][2], o[nt][3]);
+      }
+      if (!sync()) return;
+      if (!unit_epilogue(a, u, NW, xm, xl, xo, Sh::kXd, tid, NW * 32, flag, sync)) return;
+      m1 = m2 = -INFINITY;
+      l1 = l2 = 0.f;
+#pragma unroll
+      for (int i = 0; i < Sh::kNTiles; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host helpers
+// ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int encode_cache_map(CUtensorMap *m, const void *base, int32_t kv_dtype, int32_t D, int32_t Hkv,
+                     int32_t num_blocks, const int64_t *cs) {
+  auto fn = encode_fn();
+  if (!fn) {
+    set_error_detail("cuTensorMapEncodeTiled entry point unavailable");
+    return PKV_ERR_TENSOR_MAP;
+  }
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)kBoxRows, (cuuint64_t)Hkv,
+                              (cuuint64_t)num_blocks};
+  const cuuint64_t strides[3] = {(cuuint64_t)cs[2] * 2, (cuuint64_t)cs[1] * 2,
+                                 (cuuint64_t)cs[0] * 2};
+  const cuuint32_t box[4] = {64, (cuuint32_t)kBoxRows, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(m,
+                  kv_dtype == PKV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                  4, const_cast<void *>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error_detail("cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
+    return PKV_ERR_TENSOR_MAP;
+  }
+  return PKV_OK;
+}
+
+int device_sms() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
+    cudaGetLastError();
+    return 148;  // B200
+  }
+  return sms;
+}
+
+int32_t resolve_pps(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t max_blocks,
+                    int32_t pps) {
+  if (pps > 0) return pps;
+  const int32_t G = Hq / Hkv;
+  const int32_t rows = group_rows_for(G, D);
+  const int64_t units = (int64_t)B * Hkv * ((G + rows - 1) / rows);
+  const int64_t work = units * std::max<int32_t>(max_blocks, 1);
+  const int64_t target = (int64_t)device_sms() * 48;  // ~48 work units per SM
+  int64_t P = (work + target - 1) / target;
+  P = std::min<int64_t>(std::max<int64_t>(P, 8), 256);
+  return (int32_t)((P + 7) / 8 * 8);
+}
+
+bool tc_eligible(const void *k_cache, int32_t Hq, int32_t Hkv, int32_t D, int32_t bs,
+                 const int64_t *cs, int32_t q_dtype, int32_t kv_dtype, int32_t flags) {
+  if (flags & PKV_DECODE_FORCE_GENERIC) return false;
+  if (kv_dtype != PKV_DTYPE_BF16 && kv_dtype != PKV_DTYPE_F16) return false;
+  if (q_dtype != kv_dtype) return false;
+  if (bs != kBoxRows || (D != 64 && D != 128)) return false;
+  if (Hq % Hkv != 0) return false;
+  if (cs[3] != 1) return false;
+  for (int i = 0; i < 3; ++i)
+    if ((cs[i] * 2) % 16 != 0 || cs[i] <= 0) return false;
+  if (!aligned_to(k_cache, 16)) return false;
+  return true;
+}
+
+int validate_decode(const void *q, const void *kc, const void *vc, const int32_t *bt,
+                    const int32_t *ctx, const float *out, int32_t B, int32_t Hq, int32_t Hkv,
+                    int32_t D, int32_t bs, int32_t num_blocks, int32_t max_blocks,
+                    const int64_t *qs, const int64_t *cs, const int64_t *bts, const int64_t *os,
+                    int32_t q_dtype, int32_t kv_dtype) {
+  if (dtype_size(q_dtype) == 0 || dtype_size(kv_dtype) == 0) {
+    set_error_detail("unsupported dtype codes q=%d kv=%d", q_dtype, kv_dtype);
+    return PKV_ERR_UNSUPPORTED;
+  }
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || D <= 0 || bs <= 0 || num_blocks < 0 || max_blocks < 0) {
+    set_error_detail("invalid sizes");
+    return PKV_ERR_INVALID_ARG;
+  }
+  if (Hq % Hkv != 0) {
+    set_error_detail("num_q_heads (%d) must be a multiple of num_kv_heads (%d)", Hq, Hkv);
+    return PKV_ERR_INVALID_ARG;
+  }
+  if (D > 256) {
+    set_error_detail("head_dim %d > 256 is not supported", D);
+    return PKV_ERR_UNSUPPORTED;
+  }
+  if ((int64_t)max_blocks * bs > INT32_MAX) {
+    set_error_detail("max_blocks * block_size overflows int32");
+    return PKV_ERR_INVALID_ARG;
+  }
+  if (!qs || !cs || !bts || !os) {
+    set_error_detail("stride arrays must not be NULL");
+    return PKV_ERR_INVALID_ARG;
+  }
+  if (B > 0 && (!q || !kc || !vc || !bt || !ctx || !out)) {
+    set_error_detail("NULL tensor pointer");
+    return PKV_ERR_INVALID_ARG;
+  }
+  if (B > 0 && (!aligned_to(q, dtype_size(q_dtype)) || !aligned_to(kc, dtype_size(kv_dtype)) ||
+                !aligned_to(vc, dtype_size(kv_dtype)) || !aligned_to(out, 4)))
+    return PKV_ERR_ALIGNMENT;
+  return PKV_OK;
+}
+
+template <typename KT, int DJ, int GM>
+int launch_generic_t(const DecodeArgs &a, cudaStream_t st, int64_t max_units) {
+  const size_t smem = generic_smem_bytes(DJ, GM);
+  auto kern = decode_generic_kernel<KT, DJ, GM>;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess)
+    return check_launch("cudaFuncSetAttribute(generic)");
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGenThreads, smem) !=
+          cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  int64_t grid = (int64_t)device_sms() * per_sm;
+  if (grid > max_units) grid = max_units;
+  if (grid < 1) grid = 1;
+  kern<<<(unsigned)grid, kGenThreads, smem, st>>>(a);
+  return check_launch("decode_generic_kernel");
+}
+
+template <typename KT, int DJ>
+int launch_generic_g(const DecodeArgs &a, cudaStream_t st, int64_t max_units) {
+  if (a.GR <= 2) return launch_generic_t<KT, DJ, 2>(a, st, max_units);
+  if (a.GR <= 4) return launch_generic_t<KT, DJ, 4>(a, st, max_units);
+  if (a.GR <= 8) return launch_generic_t<KT, DJ, 8>(a, st, max_units);
+  if constexpr (DJ <= 4) return launch_generic_t<KT, DJ, 16>(a, st, max_units);
+  set_error_detail("head group of %d rows with head_dim %d is not supported", a.GR, a.D);
+  return PKV_ERR_UNSUPPORTED;
+}
+
+template <typename KT>
+int launch_generic_d(const DecodeArgs &a, cudaStream_t st, int64_t max_units) {
+  if (a.D <= 32) return launch_generic_g<KT, 1>(a, st, max_units);
+  if (a.D <= 64) return launch_generic_g<KT, 2>(a, st, max_units);
+  if (a.D <= 128) return launch_generic_g<KT, 4>(a, st, max_units);
+  return launch_generic_g<KT, 8>(a, st, max_units);
+}
+
+// Tensor-core kernel configuration: consumer warps and ring depth per warp.
+constexpr int kTcWarps = 4;
+constexpr int kTcStages = 4;
+
+template <typename T, int D>
+int launch_tc_t(const DecodeArgs &a, const CUtensorMap &mk, const CUtensorMap &mv, cudaStream_t st,
+                int64_t max_units) {
+  using L = TcSmem<D, kTcWarps, kTcStages>;
+  const size_t smem = L::bytes(a.P);
+  auto kern = decode_tc_kernel<T, D, kTcWarps, kTcStages>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
+    return check_launch("cudaFuncSetAttribute(tc)");
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, (kTcWarps + 1) * 32, smem) !=
+          cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  int64_t grid = (int64_t)device_sms() * per_sm;
+  if (grid > max_units) grid = max_units;
+  if (grid < 1) grid = 1;
+  kern<<<(unsigned)grid, (kTcWarps + 1) * 32, smem, st>>>(mk, mv, a);
+  return check_launch("decode_tc_kernel");
+}
+
+}  // namespace
+}  // namespace pkv
+
+using namespace pkv;
+
+extern "C" int32_t pkv_decode_pages_per_split(int32_t batch, int32_t num_q_heads,
+                                              int32_t num_kv_heads, int32_t head_dim,
+                                              int32_t max_blocks, int32_t pages_per_split) {
+  if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || max_blocks < 0 ||
+      num_q_heads % num_kv_heads != 0)
+    return PKV_ERR_INVALID_ARG;
+  return resolve_pps(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, pages_per_split);
+}
+
+extern "C" size_t pkv_decode_workspace_size(int32_t batch, int32_t num_q_heads,
+                                            int32_t num_kv_heads, int32_t head_dim,
+                                            int32_t max_blocks, int32_t pages_per_split) {
+  if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || max_blocks < 0 ||
+      num_q_heads % num_kv_heads != 0)
+    return 0;
+  const int32_t P =
+      resolve_pps(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, pages_per_split);
+  return ws_layout(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, P).total;
+}
+
+extern "C" int pkv_decode_kernel_kind(const void *k_cache, int32_t num_q_heads,
+                                      int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                                      const int64_t *cache_strides, int32_t q_dtype,
+                                      int32_t kv_dtype, int32_t flags) {
+  if (!cache_strides || num_kv_heads <= 0) return PKV_ERR_INVALID_ARG;
+  return tc_eligible(k_cache, num_q_heads, num_kv_heads, head_dim, block_size, cache_strides,
+                     q_dtype, kv_dtype, flags)
+             ? 1
+             : 0;
+}
+
+extern "C" int pkv_decode_plan(const int32_t *context_lens, int32_t batch, int32_t num_q_heads,
+                               int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                               int32_t max_blocks, int32_t pages_per_split, void *workspace,
+                               size_t workspace_bytes, int32_t *status, void *stream) {
+  if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 ||
+      max_blocks < 0 || num_q_heads % num_kv_heads != 0) {
+    set_error_detail("pkv_decode_plan: invalid sizes");
+    return PKV_ERR_INVALID_ARG;
+  }
+  if ((int64_t)max_blocks * block_size > INT32_MAX) {
+    set_error_detail("max_blocks * block_size overflows int32");
+    return PKV_ERR_INVALID_ARG;
+  }
+  const int32_t P =
+      resolve_pps(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, pages_per_split);
+  const WsLayout w = ws_layout(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, P);
+  if (workspace == nullptr || workspace_bytes < w.total || !aligned_to(workspace, 256)) {
+    set_error_detail("workspace needs %zu bytes (256-byte aligned), got %zu", w.total,
+                     workspace_bytes);
+    return PKV_ERR_WORKSPACE;
+  }
+  if (batch > 0 && context_lens == nullptr) {
+    set_error_detail("pkv_decode_plan: NULL context_lens");
+    return PKV_ERR_INVALID_ARG;
+  }
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  plan_kernel<<<1, kPlanThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      context_lens, batch, block_size, max_blocks, P, w.units_per_item,
+      reinterpret_cast<int32_t *>(ws + w.hdr), reinterpret_cast<int32_t *>(ws + w.seq_off),
+      reinterpret_cast<int32_t *>(ws + w.seq_nsplit), reinterpret_cast<int2 *>(ws + w.items),
+      reinterpret_cast<int32_t *>(ws + w.counters), status);
+  return check_launch("plan_kernel");
+}
+
+extern "C" int pkv_decode_run(const void *q, const void *k_cache, const void *v_cache,
+                              const int32_t *block_tables, const int32_t *context_lens,
+                              float *out, int32_t batch, int32_t num_q_heads,
+                              int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                              int32_t num_blocks, int32_t max_blocks, const int64_t *q_strides,
+                              const int64_t *cache_strides, const int64_t *bt_strides,
+                              const int64_t *out_strides, int32_t q_dtype, int32_t kv_dtype,
+                              float scale, int32_t pages_per_split, int32_t flags,
+                              void *workspace, size_t workspace_bytes, int32_t *status,
+                              void *stream) {
+  int rc = validate_decode(q, k_cache, v_cache, block_tables, context_lens, out, batch,
+                           num_q_heads, num_kv_heads, head_dim, block_size, num_blocks,
+                           max_blocks, q_strides, cache_strides, bt_strides, out_strides, q_dtype,
+                           kv_dtype);
+  if (rc) return rc;
+  if (batch == 0) return PKV_OK;
+  const int32_t P =
+      resolve_pps(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, pages_per_split);
+  const WsLayout w = ws_layout(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, P);
+  if (workspace == nullptr || workspace_bytes < w.total || !aligned_to(workspace, 256)) {
+    set_error_detail("workspace needs %zu bytes (256-byte aligned), got %zu", w.total,
+                     workspace_bytes);
+    return PKV_ERR_WORKSPACE;
+  }
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  DecodeArgs a{};
+  a.q = q;
+  a.kc = k_cache;
+  a.vc = v_cache;
+  a.bt = block_tables;
+  a.ctx = context_lens;
+  a.out = out;
+  a.B = batch;
+  a.Hq = num_q_heads;
+  a.Hkv = num_kv_heads;
+  a.G = num_q_heads / num_kv_heads;
+  a.GR = w.group_rows;
+  a.HG = (a.G + a.GR - 1) / a.GR;
+  a.D = head_dim;
+  a.bs = block_size;
+  a.num_blocks = num_blocks;
+  a.max_blocks = max_blocks;
+  a.P = P;
+  a.upi = w.units_per_item;
+  a.part_floats = w.part_floats;
+  a.q_dtype = q_dtype;
+  a.kv_dtype = kv_dtype;
+  a.q0 = q_strides[0]; a.q1 = q_strides[1]; a.q2 = q_strides[2];
+  a.c0 = cache_strides[0]; a.c1 = cache_strides[1]; a.c2 = cache_strides[2]; a.c3 = cache_strides[3];
+  a.bt0 = bt_strides[0]; a.bt1 = bt_strides[1];
+  a.o0 = out_strides[0]; a.o1 = out_strides[1]; a.o2 = out_strides[2];
+  a.scale = scale;
+  a.scale_log2 = scale * kLog2e;
+  a.hdr = reinterpret_cast<const int32_t *>(ws + w.hdr);
+  a.seq_off = reinterpret_cast<const int32_t *>(ws + w.seq_off);
+  a.seq_nsplit = reinterpret_cast<const int32_t *>(ws + w.seq_nsplit);
+  a.items = reinterpret_cast<const int2 *>(ws + w.items);
+  a.counters = reinterpret_cast<int32_t *>(ws + w.counters);
+  a.partials = reinterpret_cast<float *>(ws + w.partials);
+  a.status = status;
+  const int64_t max_units = w.max_items * w.units_per_item;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+
+  if (tc_eligible(k_cache, num_q_heads, num_kv_heads, head_dim, block_size, cache_strides,
+                  q_dtype, kv_dtype, flags) &&
+      num_blocks > 0 && aligned_to(v_cache, 16)) {
+    CUtensorMap mk, mv;
+    if ((rc = encode_cache_map(&mk, k_cache, kv_dtype, head_dim, num_kv_heads, num_blocks,
+                               cache_strides)))
+      return rc;
+    if ((rc = encode_cache_map(&mv, v_cache, kv_dtype, head_dim, num_kv_heads, num_blocks,
+                               cache_strides)))
+      return rc;
+    if (kv_dtype == PKV_DTYPE_BF16)
+      return head_dim == 128 ? launch_tc_t<__nv_bfloat16, 128>(a, mk, mv, st, max_units)
+                             : launch_tc_t<__nv_bfloat16, 64>(a, mk, mv, st, max_units);
+    return head_dim == 128 ? launch_tc_t<__half, 128>(a, mk, mv, st, max_units)
+                           : launch_tc_t<__half, 64>(a, mk, mv, st, max_units);
+  }
+  switch (kv_dtype) {
+    case PKV_DTYPE_BF16: return launch_generic_d<__nv_bfloat16>(a, st, max_units);
+    case PKV_DTYPE_F16: return launch_generic_d<__half>(a, st, max_units);
+    default: return launch_generic_d<float>(a, st, max_units);
+  }
+}
+
+extern "C" int pkv_decode(const void *q, const void *k_cache, const void *v_cache,
+                          const int32_t *block_tables, const int32_t *context_lens, float *out,
+                          int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                          int32_t head_dim, int32_t block_size, int32_t num_blocks,
+                          int32_t max_blocks, const int64_t *q_strides,
+                          const int64_t *cache_strides, const int64_t *bt_strides,
+                          const int64_t *out_strides, int32_t q_dtype, int32_t kv_dtype,
+                          float scale, int32_t pages_per_split, int32_t flags, void *workspace,
+                          size_t workspace_bytes, int32_t *status, void *stream) {
+  int rc = validate_decode(q, k_cache, v_cache, block_tables, context_lens, out, batch,
+                           num_q_heads, num_kv_heads, head_dim, block_size, num_blocks,
+                           max_blocks, q_strides, cache_strides, bt_strides, out_strides, q_dtype,
+                           kv_dtype);
+  if (rc) return rc;
+  if (batch == 0) return PKV_OK;
+  rc = pkv_decode_plan(context_lens, batch, num_q_heads, num_kv_heads, head_dim, block_size,
+                       max_blocks, pages_per_split, workspace, workspace_bytes, status, stream);
+  if (rc) return rc;
+  return pkv_decode_run(q, k_cache, v_cache, block_tables, context_lens, out, batch, num_q_heads,
+                        num_kv_heads, head_dim, block_size, num_blocks, max_blocks, q_strides,
+                        cache_strides, bt_strides, out_strides, q_dtype, kv_dtype, scale,
+                        pages_per_split, flags, workspace, workspace_bytes, status, stream);
+}

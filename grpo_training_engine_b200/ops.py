@@ -1,0 +1,392 @@
+"""Kernel-level paged-KV operations on torch tensors, calling libpkv.so.
+
+Each function validates its tensors, passes raw device pointers, element
+strides and the current CUDA stream through the C ABI (include/pkv.h) and
+returns without synchronising. There is no non-CUDA implementation: CPU
+tensors are rejected with the reference's ValueError, and a missing
+libpkv.so raises ImportError.
+
+Reference correspondence (src/triton_kernels/paged_kv.py):
+  paged_kv_append        _paged_kv_update_kernel launch   :253-319, :730-752
+  paged_attention_decode _paged_attention_decode_kernel   :63-251,  :754-783
+  paged_kv_append_prompt _prefill_paged_cache scatter     :572-586
+  gather_kv              the kernel's block-table addressing written densely :98-131
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+_DTYPES = {
+    torch.float32: _lib.DTYPE_F32,
+    torch.bfloat16: _lib.DTYPE_BF16,
+    torch.float16: _lib.DTYPE_F16,
+}
+
+
+def _dtype_code(t: torch.Tensor, what: str) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise ValueError(f"{what} must be float32, bfloat16 or float16, got {t.dtype}.") from None
+
+
+def _require_cuda(*tensors: Optional[torch.Tensor]) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("inputs and caches must be on CUDA device.")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"all tensors must be on one device, got {dev} and {t.device}.")
+    assert dev is not None
+    return dev
+
+
+def _as_i32(t: torch.Tensor) -> torch.Tensor:
+    return t if t.dtype == torch.int32 else t.to(torch.int32)
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _check_cache_pair(k_cache: torch.Tensor, v_cache: torch.Tensor) -> None:
+    if k_cache.ndim != 4 or v_cache.ndim != 4:
+        raise ValueError("k_cache/v_cache must be [num_blocks, heads, block, head_dim].")
+    if k_cache.shape != v_cache.shape:
+        raise ValueError("k_cache and v_cache must have identical shapes.")
+    if k_cache.dtype != v_cache.dtype:
+        raise ValueError("k_cache and v_cache must have the same dtype.")
+    if k_cache.stride() != v_cache.stride():
+        raise ValueError("k_cache and v_cache must have identical strides.")
+
+
+def _check_tables(block_tables: torch.Tensor, context_lens: torch.Tensor, batch: int) -> None:
+    if block_tables.ndim != 2:
+        raise ValueError(f"block_tables must be [batch, max_blocks], got {tuple(block_tables.shape)}.")
+    if context_lens.ndim != 1:
+        raise ValueError(f"context_lens must be [batch], got {tuple(context_lens.shape)}.")
+    if block_tables.shape[0] != batch:
+        raise ValueError("block_tables batch dimension must match input_ids batch.")
+    if context_lens.shape[0] != batch:
+        raise ValueError("context_lens batch dimension must match input_ids batch.")
+
+
+def _status_ptr(status: Optional[torch.Tensor]) -> Optional[int]:
+    if status is None:
+        return None
+    if status.dtype != torch.int32 or status.numel() < 1 or not status.is_cuda:
+        raise ValueError("status must be a CUDA int32 tensor with at least one element.")
+    return status.data_ptr()
+
+
+# ---------------------------------------------------------------------------
+# append / prompt append / gather
+# ---------------------------------------------------------------------------
+def paged_kv_append(
+    k_new: torch.Tensor,
+    v_new: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_tables: torch.Tensor,
+    context_lens: torch.Tensor,
+    *,
+    status: Optional[torch.Tensor] = None,
+) -> None:
+    """Write k_new/v_new [B, H, D] at position context_lens[b] (pre-append) in place.
+
+    Same slot rule as the reference update kernel (paged_kv.py:277-284); the
+    payload is copied bit for bit.
+    """
+    _check_cache_pair(k_cache, v_cache)
+    if k_new.ndim != 3 or k_new.shape != v_new.shape:
+        raise ValueError("k_new/v_new must be matching [batch, heads, head_dim] tensors.")
+    if k_new.stride() != v_new.stride():
+        raise ValueError("k_new and v_new must have identical strides.")
+    batch, heads, head_dim = k_new.shape
+    num_blocks, cache_heads, block_size, cache_dim = k_cache.shape
+    if heads != cache_heads or head_dim != cache_dim:
+        raise ValueError(
+            f"k_new {tuple(k_new.shape)} does not match cache heads/head_dim ({cache_heads}, {cache_dim})."
+        )
+    if k_new.dtype != k_cache.dtype or v_new.dtype != k_cache.dtype:
+        raise ValueError("k_new/v_new must have the cache dtype.")
+    _check_tables(block_tables, context_lens, batch)
+    dev = _require_cuda(k_new, v_new, k_cache, v_cache, block_tables, context_lens, status)
+    bt = _as_i32(block_tables)
+    ctx = _as_i32(context_lens)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        _lib.check(
+            "pkv_append",
+            lib.pkv_append(
+                k_new.data_ptr(), v_new.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                bt.data_ptr(), ctx.data_ptr(), batch, heads, head_dim, block_size, num_blocks,
+                bt.shape[1], _lib.i64_array(k_new.stride()), _lib.i64_array(k_cache.stride()),
+                _lib.i64_array(bt.stride()), _dtype_code(k_cache, "k_cache"), _status_ptr(status),
+                _stream(dev),
+            ),
+        )
+
+
+def paged_kv_append_prompt(
+    k: torch.Tensor,
+    v: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_tables: torch.Tensor,
+    start_pos: Optional[torch.Tensor] = None,
+    lens: Optional[torch.Tensor] = None,
+    *,
+    status: Optional[torch.Tensor] = None,
+) -> None:
+    """Bulk prompt write: k/v [B, H, T, D] (HF past_key_values layout) into pages.
+
+    Position start_pos[b] + t for t < lens[b] (defaults 0 and T), the
+    addressing of the reference prefill scatter (paged_kv.py:576-586) done
+    in one launch instead of B x T x L slice assignments.
+    """
+    _check_cache_pair(k_cache, v_cache)
+    if k.ndim != 4 or k.shape != v.shape or k.stride() != v.stride():
+        raise ValueError("k/v must be matching [batch, heads, seq_len, head_dim] tensors.")
+    batch, heads, seq_len, head_dim = k.shape
+    num_blocks, cache_heads, block_size, cache_dim = k_cache.shape
+    if heads != cache_heads or head_dim != cache_dim:
+        raise ValueError(f"k {tuple(k.shape)} does not match cache heads/head_dim ({cache_heads}, {cache_dim}).")
+    if k.dtype != k_cache.dtype or v.dtype != k_cache.dtype:
+        raise ValueError("k/v must have the cache dtype.")
+    if block_tables.ndim != 2 or block_tables.shape[0] != batch:
+        raise ValueError("block_tables must be [batch, max_blocks].")
+    for name, t in (("start_pos", start_pos), ("lens", lens)):
+        if t is not None and (t.ndim != 1 or t.shape[0] != batch):
+            raise ValueError(f"{name} must be [batch].")
+    dev = _require_cuda(k, v, k_cache, v_cache, block_tables, start_pos, lens, status)
+    bt = _as_i32(block_tables)
+    sp = None if start_pos is None else _as_i32(start_pos)
+    ln = None if lens is None else _as_i32(lens)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        _lib.check(
+            "pkv_append_prompt",
+            lib.pkv_append_prompt(
+                k.data_ptr(), v.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), bt.data_ptr(),
+                _lib.ptr(sp), _lib.ptr(ln), batch, heads, seq_len, head_dim, block_size, num_blocks,
+                bt.shape[1], _lib.i64_array(k.stride()), _lib.i64_array(k_cache.stride()),
+                _lib.i64_array(bt.stride()), _dtype_code(k_cache, "k_cache"), _status_ptr(status),
+                _stream(dev),
+            ),
+        )
+
+
+def gather_kv(
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_tables: torch.Tensor,
+    context_lens: torch.Tensor,
+    max_tokens: Optional[int] = None,
+    *,
+    status: Optional[torch.Tensor] = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Dense K, V [B, H, T, D] of the paged cache; positions >= context_lens[b] are zero.
+
+    max_tokens defaults to the block-table capacity max_blocks * block_size.
+    """
+    _check_cache_pair(k_cache, v_cache)
+    batch = block_tables.shape[0] if block_tables.ndim == 2 else -1
+    _check_tables(block_tables, context_lens, batch)
+    dev = _require_cuda(k_cache, v_cache, block_tables, context_lens, status)
+    num_blocks, heads, block_size, head_dim = k_cache.shape
+    bt = _as_i32(block_tables)
+    ctx = _as_i32(context_lens)
+    if max_tokens is None:
+        max_tokens = bt.shape[1] * block_size
+    k_out = torch.empty((batch, heads, max_tokens, head_dim), dtype=k_cache.dtype, device=dev)
+    v_out = torch.empty_like(k_out)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        _lib.check(
+            "pkv_gather",
+            lib.pkv_gather(
+                k_cache.data_ptr(), v_cache.data_ptr(), bt.data_ptr(), ctx.data_ptr(),
+                k_out.data_ptr(), v_out.data_ptr(), batch, heads, head_dim, block_size, num_blocks,
+                bt.shape[1], max_tokens, _lib.i64_array(k_cache.stride()),
+                _lib.i64_array(bt.stride()), _lib.i64_array(k_out.stride()),
+                _dtype_code(k_cache, "k_cache"), _status_ptr(status), _stream(dev),
+            ),
+        )
+    return k_out, v_out
+
+
+# ---------------------------------------------------------------------------
+# decode attention
+# ---------------------------------------------------------------------------
+@dataclass
+class DecodePlan:
+    """A decode work plan in a device workspace, valid for one context_lens.
+
+    A plan depends only on context_lens and the sizes, so a caller that runs
+    several layers with the same context_lens (one decode step of a model)
+    makes one plan and calls ``paged_attention_decode(..., plan=plan)`` per
+    layer. The workspace is also the split-K scratch of every call that uses
+    the plan: calls sharing a plan must be ordered on one stream.
+    """
+
+    batch: int
+    num_q_heads: int
+    num_kv_heads: int
+    head_dim: int
+    block_size: int
+    max_blocks: int
+    pages_per_split: int
+    workspace: torch.Tensor
+    context_lens: torch.Tensor
+
+    def matches(self, batch, num_q_heads, num_kv_heads, head_dim, block_size, max_blocks) -> bool:
+        return (self.batch, self.num_q_heads, self.num_kv_heads, self.head_dim, self.block_size, self.max_blocks) == (
+            batch, num_q_heads, num_kv_heads, head_dim, block_size, max_blocks)
+
+
+def decode_workspace_bytes(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, pages_per_split=0) -> int:
+    n = _lib.load().pkv_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, pages_per_split)
+    if n == 0:
+        raise ValueError("invalid decode geometry for the workspace size query.")
+    return int(n)
+
+
+def _pages_per_split(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, num_splits, pages_per_split) -> int:
+    if pages_per_split <= 0 and num_splits and num_splits > 0:
+        pages_per_split = max(1, math.ceil(max(max_blocks, 1) / num_splits))
+    return _lib.check(
+        "pkv_decode_pages_per_split",
+        _lib.load().pkv_decode_pages_per_split(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, pages_per_split),
+    )
+
+
+def plan_decode(
+    context_lens: torch.Tensor,
+    num_q_heads: int,
+    num_kv_heads: int,
+    head_dim: int,
+    block_size: int,
+    max_blocks: int,
+    num_splits: int = 0,
+    *,
+    pages_per_split: int = 0,
+    workspace: Optional[torch.Tensor] = None,
+    status: Optional[torch.Tensor] = None,
+) -> DecodePlan:
+    """Plan the split-K decode of all sequences for one context_lens (post-append lengths)."""
+    if context_lens.ndim != 1:
+        raise ValueError(f"context_lens must be [batch], got {tuple(context_lens.shape)}.")
+    if num_q_heads % num_kv_heads != 0:
+        raise ValueError(f"num_heads ({num_q_heads}) must be divisible by num_kv_heads ({num_kv_heads}).")
+    dev = _require_cuda(context_lens, workspace, status)
+    batch = context_lens.shape[0]
+    ctx = _as_i32(context_lens)
+    pps = _pages_per_split(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, num_splits, pages_per_split)
+    need = decode_workspace_bytes(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, pps)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        _lib.check(
+            "pkv_decode_plan",
+            lib.pkv_decode_plan(
+                ctx.data_ptr(), batch, num_q_heads, num_kv_heads, head_dim, block_size, max_blocks, pps,
+                workspace.data_ptr(), workspace.numel() * workspace.element_size(), _status_ptr(status),
+                _stream(dev),
+            ),
+        )
+    return DecodePlan(batch, num_q_heads, num_kv_heads, head_dim, block_size, max_blocks, pps, workspace, ctx)
+
+
+def paged_attention_decode(
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_tables: torch.Tensor,
+    context_lens: torch.Tensor,
+    scale: Optional[float] = None,
+    out: Optional[torch.Tensor] = None,
+    num_splits: int = 0,
+    *,
+    pages_per_split: int = 0,
+    plan: Optional[DecodePlan] = None,
+    force_generic: bool = False,
+    status: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """Single-query attention over the paged cache; returns fp32 [B, Hq, D].
+
+    q is [B, Hq, D]; the caches are [num_blocks, Hkv, block_size, D] with
+    Hq a multiple of Hkv (query head h reads cache head h // (Hq // Hkv),
+    the grouped-query mapping of HF repeat_kv). Hq == Hkv is the reference's
+    head-replicated layout. context_lens are POST-append lengths
+    (paged_kv.py:697,761,938); scale defaults to 1/sqrt(D) (paged_kv.py:681,900).
+    num_splits > 0 caps the number of split-K chunks per sequence;
+    pages_per_split > 0 sets the chunk length directly; both 0 = heuristic.
+    """
+    _check_cache_pair(k_cache, v_cache)
+    if q.ndim != 3:
+        raise ValueError(f"q must be [batch, heads, head_dim], got {tuple(q.shape)}.")
+    batch, hq, head_dim = q.shape
+    num_blocks, hkv, block_size, cache_dim = k_cache.shape
+    if cache_dim != head_dim:
+        raise ValueError(f"q head_dim {head_dim} does not match cache head_dim {cache_dim}.")
+    if hq % hkv != 0:
+        raise ValueError(f"num_heads ({hq}) must be divisible by num_kv_heads ({hkv}).")
+    _check_tables(block_tables, context_lens, batch)
+    dev = _require_cuda(q, k_cache, v_cache, block_tables, context_lens, out, status)
+    if out is None:
+        out = torch.empty((batch, hq, head_dim), dtype=torch.float32, device=dev)
+    elif out.dtype != torch.float32 or tuple(out.shape) != (batch, hq, head_dim):
+        raise ValueError("out must be a float32 [batch, heads, head_dim] tensor.")
+    if scale is None:
+        scale = 1.0 / math.sqrt(head_dim)
+    bt = _as_i32(block_tables)
+    max_blocks = bt.shape[1]
+    if plan is None:
+        plan = plan_decode(context_lens, hq, hkv, head_dim, block_size, max_blocks, num_splits,
+                           pages_per_split=pages_per_split, status=status)
+    elif not plan.matches(batch, hq, hkv, head_dim, block_size, max_blocks):
+        raise ValueError("decode plan was made for a different geometry.")
+    lib = _lib.load()
+    ws = plan.workspace
+    flags = _lib.DECODE_FORCE_GENERIC if force_generic else 0
+    with torch.cuda.device(dev):
+        _lib.check(
+            "pkv_decode_run",
+            lib.pkv_decode_run(
+                q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), bt.data_ptr(), plan.context_lens.data_ptr(),
+                out.data_ptr(), batch, hq, hkv, head_dim, block_size, num_blocks, max_blocks,
+                _lib.i64_array(q.stride()), _lib.i64_array(k_cache.stride()), _lib.i64_array(bt.stride()),
+                _lib.i64_array(out.stride()), _dtype_code(q, "q"), _dtype_code(k_cache, "k_cache"),
+                float(scale), plan.pages_per_split, flags, ws.data_ptr(), ws.numel() * ws.element_size(),
+                _status_ptr(status), _stream(dev),
+            ),
+        )
+    return out
+
+
+def decode_kernel_kind(q: torch.Tensor, k_cache: torch.Tensor, force_generic: bool = False) -> str:
+    """'tensor_core' or 'cuda_core': which decode kernel these tensors select."""
+    hq, head_dim = q.shape[1], q.shape[2]
+    _, hkv, block_size, _ = k_cache.shape
+    kind = _lib.check(
+        "pkv_decode_kernel_kind",
+        _lib.load().pkv_decode_kernel_kind(
+            k_cache.data_ptr(), hq, hkv, head_dim, block_size, _lib.i64_array(k_cache.stride()),
+            _dtype_code(q, "q"), _dtype_code(k_cache, "k_cache"),
+            _lib.DECODE_FORCE_GENERIC if force_generic else 0,
+        ),
+    )
+    return "tensor_core" if kind == 1 else "cuda_core"

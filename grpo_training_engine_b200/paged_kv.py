@@ -1,0 +1,367 @@
+"""Paged-KV rollout decoding with the reference's Python signatures.
+
+Drop-in for src/triton_kernels/paged_kv.py: ``paged_kv_decode`` (low-level,
+caller-owned cache and closures, paged_kv.py:840-985) and
+``paged_kv_decode_model`` (HF Qwen2-style model, paged_kv.py:589-837). The
+KV page append and the decode attention run in libpkv.so (sm_100a CUDA); the
+per-token model glue (norms, projections, RoPE, MLP, sampling) stays in
+torch, as it does in the reference.
+
+Behaviour kept from the reference (same conditions, same messages): input
+validation (paged_kv.py:366-415), max_new_tokens > 0, the capacity check,
+qkv_proj_fn / logits_fn shape checks, the [B, max_new_tokens] return shape,
+finished rows emitting input_ids[:, 0] (low level) or pad_token_id (model
+level), context_lens advancing only for unfinished rows (low level) or for
+all rows (model level).
+
+Deliberate differences (reference defects, see the design notes):
+  D1 the model path gives every row its own pages (the reference shares one
+     block table across the micro-batch, paged_kv.py:635-638, so rows
+     overwrite each other's appended tokens);
+  D3 the model path keeps the grouped-query cache (Hkv heads) instead of
+     replicating K/V to Hq heads (paged_kv.py:574-575,723-724);
+  D4 the low-level path checks that every step fits the block table up
+     front (the reference checks only the first step, paged_kv.py:871-872).
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Callable, Optional, Tuple, cast
+
+import torch
+
+from . import ops
+from .kv_pool import KVPagePool
+
+
+# ---------------------------------------------------------------------------
+# validation and sampling (same contract as paged_kv.py:366-450)
+# ---------------------------------------------------------------------------
+def _validate_inputs(
+    input_ids: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_tables: torch.Tensor,
+    context_lens: torch.Tensor,
+) -> Tuple[int, int, int, int]:
+    """Shape/device/dtype checks; returns (heads, block_size, head_dim, max_context)."""
+    if input_ids.ndim != 2:
+        raise ValueError(f"input_ids must be [batch, seq_len], got {input_ids.shape}.")
+    if k_cache.ndim != 4 or v_cache.ndim != 4:
+        raise ValueError("k_cache/v_cache must be [num_blocks, heads, block, head_dim].")
+    if k_cache.shape != v_cache.shape:
+        raise ValueError("k_cache and v_cache must have identical shapes.")
+    if block_tables.ndim != 2:
+        raise ValueError(f"block_tables must be [batch, max_blocks], got {block_tables.shape}.")
+    if context_lens.ndim != 1:
+        raise ValueError(f"context_lens must be [batch], got {context_lens.shape}.")
+    batch_size = input_ids.shape[0]
+    if block_tables.shape[0] != batch_size:
+        raise ValueError("block_tables batch dimension must match input_ids batch.")
+    if context_lens.shape[0] != batch_size:
+        raise ValueError("context_lens batch dimension must match input_ids batch.")
+    if not (input_ids.is_cuda and k_cache.is_cuda and v_cache.is_cuda):
+        raise ValueError("inputs and caches must be on CUDA device.")
+    if not block_tables.is_cuda or not context_lens.is_cuda:
+        raise ValueError("block_tables and context_lens must be on CUDA device.")
+    if k_cache.dtype != torch.bfloat16 or v_cache.dtype != torch.bfloat16:
+        raise ValueError("k_cache/v_cache must be bfloat16.")
+    _, num_heads, block_size, head_dim = k_cache.shape
+    max_context = block_tables.shape[1] * block_size
+    return num_heads, block_size, head_dim, max_context
+
+
+def _apply_top_p(logits: torch.Tensor, top_p: float) -> torch.Tensor:
+    """Nucleus filter: keep the sorted tokens whose cumulative probability stays <= top_p.
+
+    The most likely token is always kept; top_p >= 1 keeps everything and
+    top_p <= 0 masks everything (the rule of paged_kv.py:418-434).
+    """
+    if top_p >= 1.0:
+        return logits
+    if top_p <= 0.0:
+        return torch.full_like(logits, -float("inf"))
+    ordered, order = torch.sort(logits, dim=-1, descending=True)
+    mass = torch.softmax(ordered, dim=-1).cumsum(dim=-1)
+    drop = mass > top_p
+    drop[..., 0] = False  # the most likely token always survives
+    kept = torch.full_like(logits, -float("inf"))
+    return kept.scatter(-1, order, ordered.masked_fill(drop, -float("inf")))
+
+
+def _sample_tokens(
+    logits: torch.Tensor,
+    do_sample: bool,
+    temperature: float,
+    top_p: float,
+    generator: Optional[torch.Generator],
+) -> torch.Tensor:
+    """Greedy when not sampling (or temperature <= 0), else temperature + top-p multinomial."""
+    if not do_sample or temperature <= 0.0:
+        return torch.argmax(logits, dim=-1)
+    probs = torch.softmax(_apply_top_p(logits / max(temperature, 1e-6), top_p), dim=-1)
+    return torch.multinomial(probs, num_samples=1, generator=generator).squeeze(-1)
+
+
+def _make_generator(device: torch.device, seed: Optional[int]) -> Optional[torch.Generator]:
+    if seed is None:
+        return None
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    return gen
+
+
+# ---------------------------------------------------------------------------
+# low-level decode loop (paged_kv.py:840-985)
+# ---------------------------------------------------------------------------
+@torch.no_grad()
+def paged_kv_decode(
+    input_ids: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_tables: torch.Tensor,
+    context_lens: torch.Tensor,
+    qkv_proj_fn: Callable[[torch.Tensor], Tuple[torch.Tensor, torch.Tensor, torch.Tensor]],
+    logits_fn: Callable[[torch.Tensor], torch.Tensor],
+    max_new_tokens: int = 128,
+    temperature: float = 1.0,
+    top_p: float = 1.0,
+    do_sample: bool = True,
+    eos_token_id: Optional[int] = None,
+    pad_token_id: Optional[int] = None,
+    seed: Optional[int] = None,
+    attention_mask: Optional[torch.Tensor] = None,
+    use_cache: Optional[bool] = None,
+) -> torch.Tensor:
+    """Autoregressive decode over a caller-owned paged cache; returns [B, max_new_tokens].
+
+    Each step: q, k_new, v_new = qkv_proj_fn(last_tokens) ([B, H, D], with H
+    the cache heads or any multiple of them for grouped-query models); the
+    new K/V go to position context_lens[b]; unfinished rows advance
+    context_lens; attention over the pages gives fp32 [B, H, D] for
+    logits_fn. attention_mask and use_cache are accepted and ignored, as in
+    the reference.
+    """
+    if max_new_tokens <= 0:
+        raise ValueError(f"max_new_tokens must be > 0, got {max_new_tokens}.")
+    num_heads, block_size, head_dim, max_context = _validate_inputs(
+        input_ids, k_cache, v_cache, block_tables, context_lens
+    )
+    if context_lens.max().item() >= max_context:
+        raise ValueError("context_lens exceed block table capacity.")
+    if context_lens.max().item() + max_new_tokens > max_context:
+        raise ValueError("context_lens + max_new_tokens exceed block table capacity.")
+    eos = -1 if eos_token_id is None else eos_token_id
+    pad = 0 if pad_token_id is None else pad_token_id
+
+    batch_size = input_ids.shape[0]
+    device = input_ids.device
+    generated = torch.full((batch_size, max_new_tokens), pad, device=device, dtype=input_ids.dtype)
+    generator = _make_generator(device, seed)
+    last_tokens = input_ids[:, -1]
+    finished = torch.zeros(batch_size, device=device, dtype=torch.bool)
+    context_lens = context_lens.to(torch.int32)
+    block_tables = block_tables.to(torch.int32)
+    scale = 1.0 / math.sqrt(head_dim)
+
+    for step in range(max_new_tokens):
+        if finished.all():
+            break
+        q, k_new, v_new = qkv_proj_fn(last_tokens)
+        if q.ndim != 3 or q.shape[0] != batch_size or q.shape[2] != head_dim or q.shape[1] % num_heads != 0:
+            raise ValueError("qkv_proj_fn must return [B, H, D] tensors.")
+        q = q.to(dtype=torch.bfloat16)
+        k_new = k_new.to(dtype=torch.bfloat16)
+        v_new = v_new.to(dtype=torch.bfloat16)
+        if k_new.stride() != v_new.stride():
+            v_new = v_new.contiguous()
+            k_new = k_new.contiguous()
+        ops.paged_kv_append(k_new, v_new, k_cache, v_cache, block_tables, context_lens)
+        context_lens = context_lens + (~finished).to(context_lens.dtype)
+        attn_out = ops.paged_attention_decode(q, k_cache, v_cache, block_tables, context_lens, scale=scale)
+        logits = logits_fn(attn_out)
+        if logits.ndim != 2 or logits.shape[0] != batch_size:
+            raise ValueError("logits_fn must return [B, vocab] logits.")
+        next_tokens = _sample_tokens(logits, do_sample, temperature, top_p, generator)
+        next_tokens = torch.where(finished, input_ids[:, 0], next_tokens)
+        generated[:, step] = next_tokens
+        last_tokens = next_tokens
+        if eos >= 0:
+            finished = finished | (next_tokens == eos)
+    return generated
+
+
+# ---------------------------------------------------------------------------
+# model-level decode (paged_kv.py:453-837)
+# ---------------------------------------------------------------------------
+def _first_attr(objs, names):
+    for obj in objs:
+        if obj is None:
+            continue
+        for n in names:
+            v = getattr(obj, n, None)
+            if v is not None:
+                return v
+    return None
+
+
+def _get_model_components(model: torch.nn.Module):
+    """(embed, layers, norm, rotary_emb, lm_head, Hq, Hkv, head_dim, hidden) of an HF decoder."""
+    root = getattr(model, "model", None) or model
+    for attr in ("embed_tokens", "layers", "norm", "rotary_emb"):
+        if not hasattr(root, attr):
+            raise AttributeError(f"Model missing {attr} for paged_kv_decode.")
+    if not hasattr(model, "lm_head"):
+        raise AttributeError("Model missing lm_head for paged_kv_decode.")
+    config = getattr(model, "config", None)
+    num_heads = _first_attr([model, config], ["num_heads", "n_heads", "num_attention_heads"])
+    if num_heads is None:
+        raise ValueError("Unable to infer num_heads for paged_kv_decode.")
+    num_kv_heads = _first_attr([model, config], ["num_kv_heads", "n_kv_heads", "num_key_value_heads"])
+    if num_kv_heads is None:
+        raise ValueError("Unable to infer num_kv_heads for paged_kv_decode.")
+    hidden = _first_attr([model, config], ["hidden_size", "embed_dim"])
+    if hidden is None:
+        raise ValueError("Unable to infer hidden_size for paged_kv_decode.")
+    head_dim = _first_attr([model, config], ["head_dim", "attention_head_size"])
+    if head_dim is None:
+        head_dim = int(hidden) // int(num_heads)
+    num_heads, num_kv_heads = int(num_heads), int(num_kv_heads)
+    if num_heads % num_kv_heads != 0:
+        raise ValueError(f"num_heads ({num_heads}) must be divisible by num_kv_heads ({num_kv_heads}).")
+    return (root.embed_tokens, list(root.layers), root.norm, root.rotary_emb, model.lm_head,
+            num_heads, num_kv_heads, int(head_dim), int(hidden))
+
+
+def _layer_kv(past_kv, layer_idx: int) -> tuple[torch.Tensor, torch.Tensor]:
+    layers = getattr(past_kv, "layers", None)
+    if layers is not None:
+        return layers[layer_idx].keys, layers[layer_idx].values
+    k, v = past_kv[layer_idx]
+    return k, v
+
+
+def _prefill_paged_cache(
+    model: torch.nn.Module,
+    input_ids: torch.Tensor,
+    attention_mask: torch.Tensor,
+    pool: KVPagePool,
+    block_tables: torch.Tensor,
+) -> None:
+    """HF forward over the prompt (minus its last token), then one bulk page write per layer.
+
+    Replaces the reference's B x T x L loop of slice assignments with
+    ``.item()`` syncs (paged_kv.py:547-586) by one append_prompt launch per
+    layer, in the grouped-query layout (no repeat_kv).
+    """
+    if input_ids.numel() == 0:
+        return
+    outputs = model.model(input_ids=input_ids, attention_mask=attention_mask, use_cache=True)
+    past_kv = outputs.past_key_values
+    if past_kv is None:
+        return
+    for layer_idx in range(pool.num_layers):
+        k_layer, v_layer = _layer_kv(past_kv, layer_idx)
+        k_cache, v_cache = pool.layer(layer_idx)
+        k_layer = k_layer.to(k_cache.dtype)
+        v_layer = v_layer.to(k_cache.dtype)
+        if k_layer.stride() != v_layer.stride():
+            k_layer, v_layer = k_layer.contiguous(), v_layer.contiguous()
+        ops.paged_kv_append_prompt(k_layer, v_layer, k_cache, v_cache, block_tables)
+
+
+@torch.no_grad()
+def paged_kv_decode_model(
+    model: torch.nn.Module,
+    input_ids: torch.Tensor,
+    attention_mask: torch.Tensor,
+    max_new_tokens: int,
+    block_size: int,
+    do_sample: bool,
+    temperature: float,
+    top_p: float,
+    pad_token_id: int,
+    eos_token_id: Optional[int],
+    seed: Optional[int],
+) -> torch.Tensor:
+    """Rollout of an HF Qwen2-style decoder over a paged cache; returns [B, max_new_tokens].
+
+    The prompt minus its last token is prefilled with an HF forward and
+    written into pages; each step then embeds the last token, and per layer
+    runs norm -> q/k/v projection + RoPE -> page append -> paged decode
+    attention -> o_proj -> MLP, then samples the next token
+    (paged_kv.py:690-837).
+    """
+    if max_new_tokens <= 0:
+        raise ValueError(f"max_new_tokens must be > 0, got {max_new_tokens}.")
+    (embeddings, layers, norm, rotary_emb, lm_head, num_heads, num_kv_heads, head_dim, _) = (
+        _get_model_components(model)
+    )
+    batch_size, prompt_len = input_ids.shape
+    if prompt_len == 0:
+        raise ValueError("input_ids must have at least 1 token.")
+    device = input_ids.device
+    max_context_needed = max(prompt_len - 1 + max_new_tokens + 1, 1)
+    pages_per_seq = math.ceil(max_context_needed / block_size)
+
+    pool = KVPagePool(batch_size * pages_per_seq, len(layers), num_kv_heads, block_size, head_dim,
+                      dtype=torch.bfloat16, device=device)
+    tables = [pool.alloc(pages_per_seq) for _ in range(batch_size)]
+    block_tables = pool.block_table(tables, width=pages_per_seq)
+    context_lens = torch.full((batch_size,), prompt_len - 1, device=device, dtype=torch.int32)
+    if prompt_len > 1:
+        _prefill_paged_cache(model, input_ids[:, :-1], attention_mask[:, :-1], pool, block_tables)
+
+    generated = torch.full((batch_size, max_new_tokens), pad_token_id, device=device, dtype=input_ids.dtype)
+    generator = _make_generator(device, seed)
+    last_tokens = input_ids[:, -1]
+    finished = torch.zeros(batch_size, device=device, dtype=torch.bool)
+    scale = 1.0 / math.sqrt(head_dim)
+    from transformers.models.qwen2.modeling_qwen2 import apply_rotary_pos_emb
+
+    def _step() -> tuple[torch.Tensor, torch.Tensor]:
+        hidden = cast(torch.Tensor, embeddings(last_tokens))
+        if hidden.ndim == 2:
+            hidden = hidden.unsqueeze(1)
+        cos, sin = rotary_emb(hidden, context_lens.unsqueeze(1))
+        new_context_lens = context_lens + 1
+        plan = ops.plan_decode(new_context_lens, num_heads, num_kv_heads, head_dim, block_size,
+                               block_tables.shape[1])
+        for layer_idx, layer in enumerate(layers):
+            attn = layer.self_attn
+            residual = hidden
+            h = layer.input_layernorm(hidden)
+            q = attn.q_proj(h).view(batch_size, 1, num_heads, head_dim).transpose(1, 2)
+            k = attn.k_proj(h).view(batch_size, 1, num_kv_heads, head_dim).transpose(1, 2)
+            v = attn.v_proj(h).view(batch_size, 1, num_kv_heads, head_dim).transpose(1, 2)
+            q, k = apply_rotary_pos_emb(q, k, cos, sin)
+            q1 = q[:, :, 0, :].to(torch.bfloat16)
+            k1 = k[:, :, 0, :].to(torch.bfloat16).contiguous()
+            v1 = v[:, :, 0, :].to(torch.bfloat16).contiguous()
+            k_cache, v_cache = pool.layer(layer_idx)
+            ops.paged_kv_append(k1, v1, k_cache, v_cache, block_tables, context_lens)
+            attn_out = ops.paged_attention_decode(q1, k_cache, v_cache, block_tables, new_context_lens,
+                                                  scale=scale, plan=plan)
+            attn_out = attn_out.to(hidden.dtype).reshape(batch_size, 1, num_heads * head_dim)
+            hidden = residual + attn.o_proj(attn_out)
+            residual = hidden
+            hidden = residual + layer.mlp(layer.post_attention_layernorm(hidden))
+        hidden = norm(hidden)
+        logits = lm_head(hidden[:, -1, :])
+        return _sample_tokens(logits, do_sample, temperature, top_p, generator), new_context_lens
+
+    for step in range(max_new_tokens):
+        if finished.all():
+            break
+        next_tokens, new_context_lens = _step()
+        next_tokens = torch.where(finished, torch.full_like(next_tokens, pad_token_id), next_tokens)
+        generated[:, step] = next_tokens
+        last_tokens = next_tokens
+        if eos_token_id is not None and eos_token_id >= 0:
+            finished = finished | (next_tokens == eos_token_id)
+        context_lens = new_context_lens
+    return generated
+
+
+__all__ = ["paged_kv_decode", "paged_kv_decode_model"]

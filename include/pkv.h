@@ -1,0 +1,212 @@
+/*
+ * pkv.h — C ABI of the B200 paged-KV library (libpkv.so).
+ *
+ * The library implements the rollout hot path of the GRPO trainer: the paged
+ * KV-cache page append and the paged-KV (GQA) single-query decode attention.
+ * Every entry point takes plain device pointers, element strides and sizes,
+ * enqueues its kernels on the given CUDA stream (a cudaStream_t passed as
+ * void*; NULL = legacy default stream) and returns without synchronising.
+ *
+ * Conventions shared by all entry points
+ *   - Strides are in ELEMENTS (not bytes), exactly like torch.Tensor.stride().
+ *   - The KV cache of one layer has the logical shape
+ *         [num_blocks, num_kv_heads, block_size, head_dim]
+ *     (the layout of the reference's per-layer k_cache/v_cache,
+ *     src/triton_kernels/paged_kv.py:378-381,412). k_cache and v_cache share
+ *     one set of strides, as they share stride_kb/kh/kt/kd in the reference
+ *     kernels (paged_kv.py:74-77,264-267).
+ *   - block_tables is int32 [batch, max_blocks]; context_lens is int32 [batch].
+ *   - Page ids outside [0, num_blocks) and context lengths outside
+ *     [0, max_blocks * block_size] never cause an out-of-bounds access: the
+ *     kernel skips the access (append/gather) or treats the page as empty
+ *     (decode) and ORs a PKV_DEV_* bit into *status when status != NULL.
+ *   - Return value: PKV_OK (0) or a negative PKV_ERR_* code. The library never
+ *     traps on the device and never allocates device memory: scratch space
+ *     (the decode workspace) is provided by the caller.
+ *   - Launch failures are reported through cudaGetLastError() as PKV_ERR_CUDA;
+ *     pkv_last_error_detail() returns a thread-local description of the most
+ *     recent error on the calling thread.
+ */
+#ifndef PKV_H_
+#define PKV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PKV_ABI_VERSION 1
+
+/* Element types. The reference stores the cache in bfloat16
+ * (paged_kv.py:409-410, 629-633); float32 is accepted because the reference
+ * kernels themselves are dtype-agnostic (they cast to fp32, paged_kv.py:120,132,240). */
+enum {
+    PKV_DTYPE_F32 = 0,
+    PKV_DTYPE_BF16 = 1,
+    PKV_DTYPE_F16 = 2
+};
+
+/* Host-side status codes. */
+enum {
+    PKV_OK = 0,
+    PKV_ERR_INVALID_ARG = -1, /* null pointer, negative size, bad stride     */
+    PKV_ERR_UNSUPPORTED = -2, /* dtype / head_dim combination not built      */
+    PKV_ERR_ALIGNMENT = -3,   /* pointer not aligned to its element size     */
+    PKV_ERR_WORKSPACE = -4,   /* workspace missing or smaller than required  */
+    PKV_ERR_CUDA = -5,        /* a CUDA runtime call or launch failed        */
+    PKV_ERR_TENSOR_MAP = -6   /* cuTensorMapEncodeTiled rejected the layout  */
+};
+
+/* Device-side status bits, OR-ed into the optional int32 *status word. */
+enum {
+    PKV_DEV_CTX_OUT_OF_RANGE = 1,  /* context_lens[b] < 0 or > max_blocks*block_size */
+    PKV_DEV_PAGE_OUT_OF_RANGE = 2, /* block_tables entry outside [0, num_blocks)      */
+    PKV_DEV_WAIT_TIMEOUT = 4       /* a bounded device-side wait gave up              */
+};
+
+/* Decode flags. */
+enum {
+    PKV_DECODE_FORCE_GENERIC = 1 /* use the CUDA-core kernel even when the
+                                    TMA + tensor-core kernel could run */
+};
+
+int pkv_abi_version(void);
+const char *pkv_error_string(int status);
+const char *pkv_last_error_detail(void);
+
+/*
+ * pkv_append — write one new K and V token per (sequence, head) into its page.
+ *
+ * Replaces the reference's _paged_kv_update_kernel
+ * (src/triton_kernels/paged_kv.py:253-319) and its launch
+ * (paged_kv.py:730-752, 914-936): for every b < batch, h < num_heads the slot
+ * is position context_lens[b] (the PRE-append length): page
+ * block_tables[b, ctx / block_size], offset ctx % block_size
+ * (paged_kv.py:277-284); k_cache[page, h, off, :] = k_new[b, h, :] and the
+ * same for v (paged_kv.py:286-319). The payload is copied bit for bit.
+ *
+ * new_strides[3]  : strides of k_new / v_new [batch, num_heads, head_dim]
+ * cache_strides[4]: strides of k_cache / v_cache
+ * bt_strides[2]   : strides of block_tables
+ * dtype           : element type of k_new, v_new and the caches (all equal)
+ */
+int pkv_append(const void *k_new, const void *v_new, void *k_cache, void *v_cache,
+               const int32_t *block_tables, const int32_t *context_lens,
+               int32_t batch, int32_t num_heads, int32_t head_dim,
+               int32_t block_size, int32_t num_blocks, int32_t max_blocks,
+               const int64_t *new_strides, const int64_t *cache_strides,
+               const int64_t *bt_strides, int32_t dtype, int32_t *status,
+               void *stream);
+
+/*
+ * pkv_append_prompt — bulk write of a prompt's K/V into pages.
+ *
+ * Replaces the B x T x L host loop of the reference's _prefill_paged_cache
+ * (src/triton_kernels/paged_kv.py:572-586): for b < batch, t < lens[b],
+ * h < num_heads, position pos = start_pos[b] + t goes to page
+ * block_tables[b, pos / block_size], offset pos % block_size, and
+ * k_cache[page, h, off, :] = k_src[b, h, t, :] (same for v).
+ * k_src/v_src have the [batch, num_heads, seq_len, head_dim] layout of a
+ * HuggingFace past_key_values layer. start_pos == NULL means 0 for every
+ * sequence; lens == NULL means seq_len for every sequence.
+ * src_strides[4]: strides of k_src / v_src.
+ */
+int pkv_append_prompt(const void *k_src, const void *v_src, void *k_cache,
+                      void *v_cache, const int32_t *block_tables,
+                      const int32_t *start_pos, const int32_t *lens,
+                      int32_t batch, int32_t num_heads, int32_t seq_len,
+                      int32_t head_dim, int32_t block_size, int32_t num_blocks,
+                      int32_t max_blocks, const int64_t *src_strides,
+                      const int64_t *cache_strides, const int64_t *bt_strides,
+                      int32_t dtype, int32_t *status, void *stream);
+
+/*
+ * pkv_gather — dense copy of the paged cache: k_out[b, h, t, :] =
+ * k_cache[block_tables[b, t / bs], h, t % bs, :] for t < context_lens[b],
+ * zero for context_lens[b] <= t < max_tokens (same for v). This is the
+ * addressing of the reference decode kernel (paged_kv.py:98-131) written out
+ * densely; the reference uses it implicitly in its dense parity test
+ * (tests/test_triton_performance.py:196-219).
+ * out_strides[4]: strides of k_out / v_out [batch, num_heads, max_tokens, head_dim].
+ */
+int pkv_gather(const void *k_cache, const void *v_cache,
+               const int32_t *block_tables, const int32_t *context_lens,
+               void *k_out, void *v_out, int32_t batch, int32_t num_heads,
+               int32_t head_dim, int32_t block_size, int32_t num_blocks,
+               int32_t max_blocks, int32_t max_tokens,
+               const int64_t *cache_strides, const int64_t *bt_strides,
+               const int64_t *out_strides, int32_t dtype, int32_t *status,
+               void *stream);
+
+/*
+ * Decode attention: out[b, h, :] = sum_{t < ctx_b} softmax_t(scale * q[b,h] . K[t]) V[t]
+ * with K/V the pages of sequence b for kv head h / (num_q_heads / num_kv_heads),
+ * fp32 accumulation and an fp32 output; out = acc / max(sum, 1e-6), so an
+ * empty context yields zeros. Replaces _paged_attention_decode_kernel
+ * (src/triton_kernels/paged_kv.py:63-251) and its launches
+ * (paged_kv.py:754-783, 939-969). context_lens is the POST-append length
+ * (paged_kv.py:697,761,938). num_q_heads == num_kv_heads reproduces the
+ * reference's head-replicated cache; num_q_heads = G * num_kv_heads is the
+ * grouped-query layout (one cache head serves G consecutive query heads).
+ *
+ * Long contexts are split into chunks of pages_per_split pages; partial
+ * (max, sum, acc) triples go to the caller's workspace and are merged by
+ * the last chunk to finish. pages_per_split == 0 selects the library's
+ * heuristic for the current device.
+ *
+ * pkv_decode = pkv_decode_plan + pkv_decode_run. The plan depends only on
+ * context_lens (and the sizes), so a caller that runs many layers with the
+ * same context_lens may plan once and run per layer on the same workspace.
+ */
+int32_t pkv_decode_pages_per_split(int32_t batch, int32_t num_q_heads,
+                                   int32_t num_kv_heads, int32_t head_dim,
+                                   int32_t max_blocks, int32_t pages_per_split);
+
+size_t pkv_decode_workspace_size(int32_t batch, int32_t num_q_heads,
+                                 int32_t num_kv_heads, int32_t head_dim,
+                                 int32_t max_blocks, int32_t pages_per_split);
+
+int pkv_decode_plan(const int32_t *context_lens, int32_t batch,
+                    int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                    int32_t block_size, int32_t max_blocks,
+                    int32_t pages_per_split, void *workspace,
+                    size_t workspace_bytes, int32_t *status, void *stream);
+
+int pkv_decode_run(const void *q, const void *k_cache, const void *v_cache,
+                   const int32_t *block_tables, const int32_t *context_lens,
+                   float *out, int32_t batch, int32_t num_q_heads,
+                   int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                   int32_t num_blocks, int32_t max_blocks,
+                   const int64_t *q_strides, const int64_t *cache_strides,
+                   const int64_t *bt_strides, const int64_t *out_strides,
+                   int32_t q_dtype, int32_t kv_dtype, float scale,
+                   int32_t pages_per_split, int32_t flags, void *workspace,
+                   size_t workspace_bytes, int32_t *status, void *stream);
+
+int pkv_decode(const void *q, const void *k_cache, const void *v_cache,
+               const int32_t *block_tables, const int32_t *context_lens,
+               float *out, int32_t batch, int32_t num_q_heads,
+               int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+               int32_t num_blocks, int32_t max_blocks,
+               const int64_t *q_strides, const int64_t *cache_strides,
+               const int64_t *bt_strides, const int64_t *out_strides,
+               int32_t q_dtype, int32_t kv_dtype, float scale,
+               int32_t pages_per_split, int32_t flags, void *workspace,
+               size_t workspace_bytes, int32_t *status, void *stream);
+
+/*
+ * Which decode kernel pkv_decode_run would launch for these arguments:
+ * 1 = TMA + tensor-core kernel, 0 = CUDA-core kernel, <0 = error code.
+ */
+int pkv_decode_kernel_kind(const void *k_cache, int32_t num_q_heads,
+                           int32_t num_kv_heads, int32_t head_dim,
+                           int32_t block_size, const int64_t *cache_strides,
+                           int32_t q_dtype, int32_t kv_dtype, int32_t flags);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PKV_H_ */

@@ -1,0 +1,250 @@
+"""The reference-signature drivers on the GPU.
+
+1. The reference's own paged-decode test scenario
+   (tests/test_triton_performance.py:136-271): a tiny model decodes greedily
+   through the low-level ``paged_kv_decode`` and must produce exactly the
+   tokens of a dense fp32 attention reference; run here through this
+   package's façade, plus larger batched / grouped-query / shuffled-page
+   variants the reference never tests.
+2. The model-level path on a tiny random HF Qwen2 decoder: paged rollout vs
+   the same step computed with dense K/V tensors.
+"""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+import grpo_training_engine_b200 as pkg
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda")
+
+
+class TinyPagedModel(torch.nn.Module):
+    """Same structure as the reference test model, with optional grouped-query heads."""
+
+    def __init__(self, vocab, num_heads, head_dim, num_kv_heads=None):
+        super().__init__()
+        self.num_heads, self.head_dim = num_heads, head_dim
+        self.num_kv_heads = num_kv_heads or num_heads
+        embed = num_heads * head_dim
+        self.embed = torch.nn.Embedding(vocab, embed)
+        self.q_proj = torch.nn.Linear(embed, embed, bias=False)
+        self.k_proj = torch.nn.Linear(embed, self.num_kv_heads * head_dim, bias=False)
+        self.v_proj = torch.nn.Linear(embed, self.num_kv_heads * head_dim, bias=False)
+        self.out_proj = torch.nn.Linear(embed, vocab, bias=False)
+
+    def _project(self, ids):
+        x = self.embed(ids)
+        if x.ndim == 2:
+            x = x.unsqueeze(1)
+        b, s, _ = x.shape
+        q = self.q_proj(x).view(b, s, self.num_heads, self.head_dim)
+        k = self.k_proj(x).view(b, s, self.num_kv_heads, self.head_dim)
+        v = self.v_proj(x).view(b, s, self.num_kv_heads, self.head_dim)
+        return q, k, v
+
+    def qkv_for_decode(self, ids):
+        q, k, v = self._project(ids)
+        return q[:, 0], k[:, 0], v[:, 0]
+
+    def logits_from_attn(self, attn_out):
+        return self.out_proj(attn_out.reshape(attn_out.shape[0], -1))
+
+    @torch.no_grad()
+    def generate(self, input_ids, max_tokens):
+        """Dense reference: fp32 softmax attention over bf16-rounded q/K/V."""
+        tokens, out = input_ids, []
+        scale = 1.0 / math.sqrt(self.head_dim)
+        g = self.num_heads // self.num_kv_heads
+        for _ in range(max_tokens):
+            q, k, v = self._project(tokens)
+            q_last = q[:, -1].to(torch.bfloat16).float()
+            k = k.to(torch.bfloat16).float().repeat_interleave(g, dim=2)
+            v = v.to(torch.bfloat16).float().repeat_interleave(g, dim=2)
+            scores = (q_last[:, None] * k).sum(-1) * scale
+            weights = torch.softmax(scores.transpose(1, 2), dim=-1)
+            attn = (weights[..., None] * v.transpose(1, 2)).sum(dim=-2)
+            nxt = torch.argmax(self.logits_from_attn(attn), dim=-1)
+            out.append(nxt)
+            tokens = torch.cat([tokens, nxt[:, None]], dim=1)
+        return torch.stack(out, dim=1)
+
+
+def _run_low_level(model, input_ids, block_size, max_new_tokens, shuffle_seed=None):
+    batch, prompt_len = input_ids.shape
+    max_ctx = prompt_len - 1 + max_new_tokens + 1
+    max_blocks = math.ceil(max_ctx / block_size)
+    num_blocks = batch * max_blocks
+    k_cache = torch.zeros((num_blocks, model.num_kv_heads, block_size, model.head_dim), device=DEV, dtype=torch.bfloat16)
+    v_cache = torch.zeros_like(k_cache)
+    ids = torch.arange(num_blocks, dtype=torch.int32)
+    if shuffle_seed is not None:
+        ids = ids[torch.randperm(num_blocks, generator=torch.Generator().manual_seed(shuffle_seed))]
+    block_tables = ids.reshape(batch, max_blocks).to(DEV)
+    context_lens = torch.full((batch,), prompt_len - 1, device=DEV, dtype=torch.int32)
+    if prompt_len > 1:
+        with torch.no_grad():
+            _, kp, vp = model._project(input_ids[:, :-1])
+        # bulk prompt write ([B, H, T, D] layout) instead of the reference's per-position loop
+        pkg.paged_kv_append_prompt(kp.transpose(1, 2).to(torch.bfloat16).contiguous(),
+                                   vp.transpose(1, 2).to(torch.bfloat16).contiguous(),
+                                   k_cache, v_cache, block_tables)
+    return pkg.paged_kv_decode(
+        None, input_ids=input_ids, k_cache=k_cache, v_cache=v_cache, block_tables=block_tables,
+        context_lens=context_lens, qkv_proj_fn=model.qkv_for_decode, logits_fn=model.logits_from_attn,
+        max_new_tokens=max_new_tokens, temperature=0.0, top_p=1.0, do_sample=False, eos_token_id=None,
+        pad_token_id=0, seed=123,
+    )
+
+
+def test_reference_scenario_token_exact():
+    """tests/test_triton_performance.py:136-271 verbatim in its numbers: seed 7, B=1,
+    vocab 32, H=2, D=8, prompt 3, 3 new tokens, block size 4."""
+    torch.manual_seed(7)
+    torch.cuda.manual_seed_all(7)
+    model = TinyPagedModel(32, 2, 8).to(DEV)
+    input_ids = torch.randint(0, 32, (1, 3), device=DEV)
+    got = _run_low_level(model, input_ids, block_size=4, max_new_tokens=3)
+    assert torch.equal(got, model.generate(input_ids, 3))
+
+
+@pytest.mark.parametrize(
+    "batch,heads,kv_heads,head_dim,block_size,prompt,new",
+    [(4, 2, 2, 8, 4, 5, 8), (3, 12, 2, 128, 16, 40, 24), (2, 28, 4, 128, 16, 19, 12), (5, 4, 1, 64, 16, 1, 6)],
+)
+def test_batched_gqa_shuffled_pages_token_exact(batch, heads, kv_heads, head_dim, block_size, prompt, new):
+    torch.manual_seed(1000 + batch)
+    model = TinyPagedModel(64, heads, head_dim, kv_heads).to(DEV)
+    input_ids = torch.randint(0, 64, (batch, prompt), device=DEV)
+    got = _run_low_level(model, input_ids, block_size, new, shuffle_seed=batch)
+    assert torch.equal(got, model.generate(input_ids, new))
+
+
+def test_low_level_eos_and_padding_semantics():
+    torch.manual_seed(3)
+    model = TinyPagedModel(16, 2, 8).to(DEV)
+    input_ids = torch.randint(0, 16, (4, 3), device=DEV)
+    ref = model.generate(input_ids, 6)
+    eos = int(ref[0, 1])
+    k_cache = torch.zeros((8, 2, 4, 8), device=DEV, dtype=torch.bfloat16)
+    out = pkg.paged_kv_decode(
+        None, input_ids=input_ids, k_cache=k_cache, v_cache=torch.zeros_like(k_cache),
+        block_tables=torch.arange(8, dtype=torch.int32, device=DEV).reshape(4, 2),
+        context_lens=torch.zeros(4, dtype=torch.int32, device=DEV), qkv_proj_fn=model.qkv_for_decode,
+        logits_fn=model.logits_from_attn, max_new_tokens=6, do_sample=False, eos_token_id=eos,
+    )
+    assert out.shape == (4, 6)
+    for row in range(4):
+        hits = (out[row] == eos).nonzero()
+        if len(hits):
+            first = int(hits[0])
+            # finished rows re-emit input_ids[:, 0] (paged_kv.py:978)
+            assert (out[row, first + 1:] == input_ids[row, 0]).all()
+
+
+def test_low_level_capacity_errors():
+    model = TinyPagedModel(16, 2, 8).to(DEV)
+    ids = torch.zeros(1, 2, dtype=torch.long, device=DEV)
+    kc = torch.zeros((2, 2, 4, 8), device=DEV, dtype=torch.bfloat16)
+    common = dict(k_cache=kc, v_cache=kc.clone(), block_tables=torch.zeros(1, 2, dtype=torch.int32, device=DEV),
+                  qkv_proj_fn=model.qkv_for_decode, logits_fn=model.logits_from_attn)
+    with pytest.raises(ValueError, match="context_lens exceed block table capacity."):
+        pkg.paged_kv_decode(None, ids, context_lens=torch.tensor([8], dtype=torch.int32, device=DEV), **common)
+    with pytest.raises(ValueError, match="exceed block table capacity"):
+        pkg.paged_kv_decode(None, ids, context_lens=torch.tensor([6], dtype=torch.int32, device=DEV),
+                            max_new_tokens=4, **common)
+
+
+# -------------------------------------------------------------- model-level path
+def _tiny_qwen2(seed=0):
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    torch.manual_seed(seed)
+    cfg = Qwen2Config(vocab_size=96, hidden_size=128, intermediate_size=256, num_hidden_layers=3,
+                      num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=512,
+                      rms_norm_eps=1e-6, tie_word_embeddings=False)
+    model = Qwen2ForCausalLM(cfg).to(DEV, torch.bfloat16).eval()
+    return model
+
+
+@torch.no_grad()
+def _dense_rollout(model, input_ids, max_new_tokens):
+    """Same per-step computation as paged_kv_decode_model, with dense K/V tensors."""
+    from transformers.models.qwen2.modeling_qwen2 import apply_rotary_pos_emb
+
+    m = model.model
+    cfg = model.config
+    hq, hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+    d = cfg.hidden_size // hq
+    batch, prompt = input_ids.shape
+    out = m(input_ids=input_ids[:, :-1], attention_mask=torch.ones_like(input_ids[:, :-1]), use_cache=True)
+    pk = out.past_key_values
+    ks = [pk.layers[i].keys.to(torch.bfloat16) for i in range(cfg.num_hidden_layers)]
+    vs = [pk.layers[i].values.to(torch.bfloat16) for i in range(cfg.num_hidden_layers)]
+    last = input_ids[:, -1]
+    pos = prompt - 1
+    toks, gaps = [], []
+    for _ in range(max_new_tokens):
+        h = m.embed_tokens(last).unsqueeze(1)
+        cos, sin = m.rotary_emb(h, torch.full((batch, 1), pos, device=DEV))
+        for li, layer in enumerate(m.layers):
+            a = layer.self_attn
+            r = h
+            x = layer.input_layernorm(h)
+            q = a.q_proj(x).view(batch, 1, hq, d).transpose(1, 2)
+            k = a.k_proj(x).view(batch, 1, hkv, d).transpose(1, 2)
+            v = a.v_proj(x).view(batch, 1, hkv, d).transpose(1, 2)
+            q, k = apply_rotary_pos_emb(q, k, cos, sin)
+            ks[li] = torch.cat([ks[li], k.to(torch.bfloat16)], dim=2)
+            vs[li] = torch.cat([vs[li], v.to(torch.bfloat16)], dim=2)
+            kf = ks[li].float().repeat_interleave(hq // hkv, dim=1)
+            vf = vs[li].float().repeat_interleave(hq // hkv, dim=1)
+            qf = q.to(torch.bfloat16).float()
+            w = torch.softmax((qf @ kf.transpose(-1, -2)) / math.sqrt(d), dim=-1)
+            att = (w @ vf).to(h.dtype).transpose(1, 2).reshape(batch, 1, hq * d)
+            h = r + a.o_proj(att)
+            h = h + layer.mlp(layer.post_attention_layernorm(h))
+        logits = model.lm_head(m.norm(h)[:, -1]).float()
+        top2 = logits.topk(2, dim=-1).values
+        gaps.append(top2[:, 0] - top2[:, 1])
+        last = logits.argmax(-1)
+        toks.append(last)
+        pos += 1
+    return torch.stack(toks, 1), torch.stack(gaps, 1)
+
+
+def test_model_level_matches_dense_rollout():
+    model = _tiny_qwen2()
+    torch.manual_seed(5)
+    input_ids = torch.randint(0, 96, (4, 21), device=DEV)
+    got = pkg.paged_kv_decode(model, input_ids, torch.ones_like(input_ids), max_new_tokens=10,
+                              do_sample=False, pad_token_id=0)
+    ref, gaps = _dense_rollout(model, input_ids, 10)
+    assert got.shape == (4, 10)
+    for row in range(4):
+        diff = (got[row] != ref[row]).nonzero()
+        if len(diff):  # only a near-tie in the dense logits may flip a greedy token
+            first = int(diff[0])
+            assert float(gaps[row, first]) < 0.05, (row, first, float(gaps[row, first]))
+
+
+def test_model_level_rows_do_not_share_pages():
+    """Each row owns its pages (defect D1): a batched greedy rollout of different
+    prompts equals each prompt rolled out alone. With one block table shared by
+    all rows, as in the reference model path, rows overwrite each other's KV."""
+    model = _tiny_qwen2(1)
+    torch.manual_seed(8)
+    ids = torch.randint(0, 96, (4, 13), device=DEV)
+    batched = pkg.paged_kv_decode(model, ids, torch.ones_like(ids), max_new_tokens=8, do_sample=False)
+    for i in range(4):
+        single = pkg.paged_kv_decode(model, ids[i:i + 1], torch.ones_like(ids[i:i + 1]), max_new_tokens=8,
+                                     do_sample=False)
+        ref, gaps = _dense_rollout(model, ids[i:i + 1], 8)
+        for got in (batched[i], single[0]):
+            diff = (got != ref[0]).nonzero()
+            if len(diff):
+                assert float(gaps[0, int(diff[0])]) < 0.05

@@ -1,0 +1,296 @@
+"""Parity of the CUDA kernels (through the C ABI) with the reference and the oracle.
+
+Bars: append, prompt append and gather bit-exact;
+decode output within max-abs 1e-5 of the reference arithmetic for fp32
+caches and 2e-2 for bf16/fp16 caches (fp32 accumulation).
+"""
+
+from __future__ import annotations
+
+import hashlib
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+from conftest import ATOL, load_golden
+from grpo_training_engine_b200 import (
+    decode_kernel_kind,
+    gather_kv,
+    paged_attention_decode,
+    paged_kv_append,
+    paged_kv_append_prompt,
+    plan_decode,
+)
+from grpo_training_engine_b200 import _lib
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+RAW = {torch.float32: torch.int32, torch.bfloat16: torch.int16, torch.float16: torch.int16}
+
+
+def _sha(*tensors: torch.Tensor) -> str:
+    h = hashlib.sha256()
+    for t in tensors:
+        h.update(np.ascontiguousarray(t.detach().cpu().contiguous().view(RAW[t.dtype]).numpy()).tobytes())
+    return h.hexdigest()
+
+
+def _maxabs(a: torch.Tensor, b) -> float:
+    b = torch.as_tensor(b)
+    return float((a.detach().cpu().float() - b.float()).abs().max()) if a.numel() else 0.0
+
+
+# ------------------------------------------------------------------ golden vectors
+@pytest.mark.parametrize("name", [c["name"] for c in cases.CASES])
+@pytest.mark.parametrize("force_generic", [False, True])
+def test_golden_append_and_decode(name, force_generic):
+    case = cases.BY_NAME[name]
+    ref_out, meta = load_golden(name)
+    t = cases.to_torch(cases.make_inputs(case), case["dtype"], device=DEV)
+    ctx = t["context_lens"]
+    if case["append"]:
+        paged_kv_append(t["k_new"], t["v_new"], t["k_cache"], t["v_cache"], t["block_tables"], ctx)
+        ctx = ctx + 1
+    assert _sha(t["k_cache"], t["v_cache"]) == meta["cache_after_append_sha"]
+    out = paged_attention_decode(t["q"], t["k_cache"], t["v_cache"], t["block_tables"], ctx,
+                                 force_generic=force_generic)
+    torch.cuda.synchronize()
+    assert _maxabs(out, ref_out) <= ATOL[case["dtype"]], _maxabs(out, ref_out)
+
+
+@pytest.mark.parametrize("name", [c["name"] for c in cases.CASES if c.get("prompt_steps")])
+def test_golden_prompt_scatter(name):
+    case = cases.BY_NAME[name]
+    _, meta = load_golden(name)
+    t = cases.to_torch(cases.make_inputs(case), case["dtype"], device=DEV)
+    kc = torch.zeros_like(t["k_cache"])
+    vc = torch.zeros_like(t["v_cache"])
+    paged_kv_append_prompt(t["prompt_k"], t["prompt_v"], kc, vc, t["block_tables"])
+    assert _sha(kc, vc) == meta["prompt_cache_sha"]
+
+
+def test_bf16_golden_selects_tensor_core_kernel():
+    case = cases.BY_NAME["bf16_qwen7b_g7"]
+    t = cases.to_torch(cases.make_inputs(case), case["dtype"], device=DEV)
+    assert decode_kernel_kind(t["q"], t["k_cache"]) == "tensor_core"
+    assert decode_kernel_kind(t["q"], t["k_cache"], force_generic=True) == "cuda_core"
+
+
+# ------------------------------------------------------------- random vs oracle
+def _random_case(seed, batch, hq, hkv, d, bs, ctxs, dtype, num_blocks=None, spare=3):
+    g = torch.Generator().manual_seed(seed)
+    max_blocks = max(1, max(math.ceil(c / bs) for c in ctxs) + 1)
+    num_blocks = num_blocks or batch * max_blocks + spare
+    perm = torch.randperm(num_blocks, generator=g)[: batch * max_blocks].reshape(batch, max_blocks).int()
+    q = torch.randn(batch, hq, d, generator=g).to(dtype)
+    kc = torch.randn(num_blocks, hkv, bs, d, generator=g).to(dtype)
+    vc = torch.randn(num_blocks, hkv, bs, d, generator=g).to(dtype)
+    ctx = torch.tensor(ctxs, dtype=torch.int32)
+    return q, kc, vc, perm, ctx
+
+
+DECODE_SHAPES = [
+    # (batch, hq, hkv, head_dim, block_size, dtype, ctxs)
+    (4, 12, 2, 128, 16, torch.bfloat16, [1, 16, 17, 777]),          # 1.5B geometry
+    (3, 28, 4, 128, 16, torch.bfloat16, [5000, 33, 2048]),           # 7B geometry
+    (2, 8, 8, 128, 16, torch.bfloat16, [100, 300]),                  # replicated heads (G=1)
+    (2, 32, 2, 128, 16, torch.bfloat16, [129, 64]),                  # G=16 (one full MMA tile)
+    (2, 40, 2, 64, 16, torch.float16, [500, 1]),                     # G=20 -> two head groups
+    (2, 16, 2, 64, 16, torch.bfloat16, [0, 95]),                     # empty context
+    (3, 12, 2, 128, 16, torch.float32, [37, 128, 300]),              # fp32 -> CUDA cores
+    (2, 6, 3, 96, 8, torch.bfloat16, [50, 9]),                       # odd head_dim / block size
+    (2, 4, 1, 256, 32, torch.float16, [200, 31]),                    # wide heads
+    (2, 2, 2, 8, 4, torch.float32, [6, 3]),                          # reference test geometry
+]
+
+
+@pytest.mark.parametrize("shape", DECODE_SHAPES, ids=lambda s: f"b{s[0]}q{s[1]}kv{s[2]}d{s[3]}bs{s[4]}")
+@pytest.mark.parametrize("splits", [0, 1, 5])
+def test_decode_matches_oracle(shape, splits):
+    batch, hq, hkv, d, bs, dtype, ctxs = shape
+    q, kc, vc, bt, ctx = _random_case(11, batch, hq, hkv, d, bs, ctxs, dtype)
+    ref = oracle.decode(q, kc, vc, bt, ctx)
+    tol = ATOL[str(dtype).split(".")[1]]
+    for force_generic in (False, True):
+        out = paged_attention_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), ctx.to(DEV),
+                                     num_splits=splits, force_generic=force_generic)
+        assert _maxabs(out, ref) <= tol, (force_generic, _maxabs(out, ref))
+
+
+@pytest.mark.parametrize("pages_per_split", [1, 2, 8, 64])
+def test_split_invariance_and_determinism(pages_per_split):
+    q, kc, vc, bt, ctx = _random_case(5, 6, 12, 2, 128, 16, [3000, 1, 17, 512, 4096, 2049], torch.bfloat16)
+    args = [x.to(DEV) for x in (q, kc, vc, bt, ctx)]
+    a = paged_attention_decode(*args, pages_per_split=pages_per_split)
+    b = paged_attention_decode(*args, pages_per_split=pages_per_split)
+    assert torch.equal(a, b)  # no atomics in the arithmetic: bitwise reproducible
+    whole = paged_attention_decode(*args, pages_per_split=4096)
+    assert _maxabs(a, whole.cpu()) < 2e-3
+    ref = oracle.decode(q, kc, vc, bt, ctx)
+    assert _maxabs(a, ref) <= 2e-2
+
+
+def test_strided_views_and_pool_layers():
+    """Caches as layers of a 5-D pool, q as a slice, out as a strided view."""
+    L, nb, hkv, bs, d, hq, batch = 3, 40, 2, 16, 128, 12, 3
+    g = torch.Generator().manual_seed(2)
+    pool = torch.randn(2, L, nb, hkv, bs, d, generator=g).to(torch.bfloat16)
+    big_q = torch.randn(batch, hq * 2, d, generator=g).to(torch.bfloat16)
+    bt = torch.randperm(nb, generator=g)[: batch * 10].reshape(batch, 10).int()
+    ctx = torch.tensor([150, 7, 160], dtype=torch.int32)
+    pool_d = pool.to(DEV)
+    out_big = torch.zeros(batch, hq, d * 2, device=DEV)
+    for layer in range(L):
+        kc, vc = pool_d[0, layer], pool_d[1, layer]
+        q = big_q[:, ::2].to(DEV)  # non-contiguous heads
+        out = out_big[:, :, ::2]
+        paged_attention_decode(q, kc, vc, bt.to(DEV), ctx.to(DEV), out=out)
+        ref = oracle.decode(big_q[:, ::2], pool[0, layer], pool[1, layer], bt, ctx)
+        assert _maxabs(out, ref) <= 2e-2
+        assert not out_big[:, :, 1::2].any()
+
+
+def test_plan_reuse_across_layers():
+    q, kc, vc, bt, ctx = _random_case(8, 5, 12, 2, 128, 16, [900, 3, 64, 65, 1500], torch.bfloat16)
+    qd, kd, vd, btd, cd = (x.to(DEV) for x in (q, kc, vc, bt, ctx))
+    plan = plan_decode(cd, 12, 2, 128, 16, bt.shape[1], pages_per_split=8)
+    for _ in range(3):
+        out = paged_attention_decode(qd, kd, vd, btd, cd, plan=plan)
+        assert _maxabs(out, oracle.decode(q, kc, vc, bt, ctx)) <= 2e-2
+
+
+def test_full_scale_properties():
+    """Size-independent properties at config-4 lengths: constant V gives V; zero K gives mean(V)."""
+    batch, hq, hkv, d, bs = 32, 12, 2, 128, 16
+    g = torch.Generator().manual_seed(9)
+    ctxs = torch.randint(1024, 8193, (batch,), generator=g)
+    max_blocks = int(math.ceil(ctxs.max().item() / bs))
+    nb = batch * max_blocks
+    bt = torch.randperm(nb, generator=g).reshape(batch, max_blocks).int().to(DEV)
+    q = torch.randn(batch, hq, d, generator=g).to(torch.bfloat16).to(DEV)
+    kc = torch.randn(nb, hkv, bs, d, generator=g).to(torch.bfloat16).to(DEV)
+    vc = torch.full((nb, hkv, bs, d), 0.75, dtype=torch.bfloat16, device=DEV)
+    ctx = ctxs.int().to(DEV)
+    out = paged_attention_decode(q, kc, vc, bt, ctx)
+    assert float((out - 0.75).abs().max()) < 4e-3
+    kz = torch.zeros_like(kc)
+    vr = torch.randn(nb, hkv, bs, d, generator=g).to(torch.bfloat16).to(DEV)
+    out = paged_attention_decode(q, kz, vr, bt, ctx)
+    dense_v, _ = gather_kv(vr, vr, bt, ctx)
+    mean = dense_v.float().sum(dim=2) / ctx.view(-1, 1, 1).float()
+    exp = mean.repeat_interleave(hq // hkv, dim=1)
+    assert float((out - exp).abs().max()) < 1e-3
+
+
+def test_large_ragged_batch_vs_oracle():
+    q, kc, vc, bt, ctx = _random_case(21, 48, 12, 2, 128, 16,
+                                      torch.randint(1024, 8193, (48,), generator=torch.Generator().manual_seed(1)).tolist(),
+                                      torch.bfloat16)
+    out = paged_attention_decode(*(x.to(DEV) for x in (q, kc, vc, bt, ctx)))
+    assert _maxabs(out, oracle.decode(q, kc, vc, bt, ctx)) <= 2e-2
+
+
+def test_out_of_range_inputs_are_flagged_not_faulted():
+    q, kc, vc, bt, ctx = _random_case(3, 3, 12, 2, 128, 16, [40, 40, 40], torch.bfloat16)
+    bad_bt = bt.clone()
+    bad_bt[1, 1] = kc.shape[0] + 5  # page id past the pool
+    bad_bt[2, 0] = -1
+    for force_generic in (False, True):
+        status = torch.zeros(1, dtype=torch.int32, device=DEV)
+        out = paged_attention_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), bad_bt.to(DEV), ctx.to(DEV),
+                                     status=status, force_generic=force_generic)
+        assert int(status.item()) & _lib.DEV_PAGE_OUT_OF_RANGE
+        # invalid pages are skipped, exactly like the oracle does
+        assert _maxabs(out, oracle.decode(q, kc, vc, bad_bt, ctx)) <= 2e-2
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    too_long = torch.tensor([40, 10_000, -3], dtype=torch.int32)
+    out = paged_attention_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), too_long.to(DEV), status=status)
+    assert int(status.item()) & _lib.DEV_CTX_OUT_OF_RANGE
+    assert _maxabs(out, oracle.decode(q, kc, vc, bt, too_long)) <= 2e-2
+    # append past the table is skipped and flagged
+    status.zero_()
+    kn = torch.randn(3, 2, 128, dtype=torch.bfloat16, device=DEV)
+    before = kc.to(DEV)
+    after = before.clone()
+    paged_kv_append(kn, kn.clone(), after, after.clone(), bt.to(DEV), torch.tensor([10_000, -1, 10_000], dtype=torch.int32, device=DEV), status=status)
+    assert int(status.item()) & _lib.DEV_CTX_OUT_OF_RANGE
+    assert torch.equal(before, after)
+
+
+# ---------------------------------------------------------------- append / gather
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("d", [8, 6, 128])
+def test_append_gather_bit_exact(dtype, d):
+    g = torch.Generator().manual_seed(4)
+    batch, heads, bs, nb, mb = 5, 3, 8, 40, 6
+    bt = torch.randperm(nb, generator=g)[: batch * mb].reshape(batch, mb).int()
+    ctx = torch.tensor([0, 7, 8, 30, 47], dtype=torch.int32)
+    kc = torch.randn(nb, heads, bs, d, generator=g).to(dtype)
+    vc = torch.randn(nb, heads, bs, d, generator=g).to(dtype)
+    kn = torch.randn(batch, heads, d, generator=g).to(dtype)
+    vn = torch.randn(batch, heads, d, generator=g).to(dtype)
+    kd, vd = kc.to(DEV), vc.to(DEV)
+    paged_kv_append(kn.to(DEV), vn.to(DEV), kd, vd, bt.to(DEV), ctx.to(DEV))
+    oracle.append(kn, vn, kc, vc, bt, ctx)
+    assert _sha(kd, vd) == _sha(kc, vc)
+    k1, v1 = gather_kv(kd, vd, bt.to(DEV), (ctx + 1).to(DEV))
+    k2, v2 = oracle.gather(kc, vc, bt, ctx + 1)
+    assert _sha(k1, v1) == _sha(k2, v2)
+
+
+def test_append_prompt_with_offsets_and_lengths():
+    g = torch.Generator().manual_seed(6)
+    batch, heads, bs, nb, mb, d, T = 3, 2, 16, 30, 8, 128, 50
+    bt = torch.randperm(nb, generator=g)[: batch * mb].reshape(batch, mb).int()
+    k = torch.randn(batch, heads, T, d, generator=g).to(torch.bfloat16)
+    v = torch.randn(batch, heads, T, d, generator=g).to(torch.bfloat16)
+    start = torch.tensor([0, 5, 70], dtype=torch.int32)
+    lens = torch.tensor([50, 13, 40], dtype=torch.int32)
+    kc = torch.zeros(nb, heads, bs, d, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    kd, vd = kc.to(DEV), vc.to(DEV)
+    paged_kv_append_prompt(k.to(DEV), v.to(DEV), kd, vd, bt.to(DEV), start.to(DEV), lens.to(DEV))
+    oracle.append_prompt(k, v, kc, vc, bt, start, lens)
+    assert _sha(kd, vd) == _sha(kc, vc)
+
+
+def test_config2_append_gather_round_trip():
+    """28 layers x 2 kv heads x 128, bs 16, 8 sequences; 512-token
+    prompt written in bulk, then 512 single-token appends; gather must return
+    every written token bit for bit."""
+    L, batch, hkv, d, bs, P, N = 28, 8, 2, 128, 16, 512, 512
+    pages = (P + N) // bs
+    g = torch.Generator(device=DEV).manual_seed(22)
+    nb = batch * pages + 7
+    perm = torch.randperm(nb, device=DEV, generator=g)[: batch * pages].reshape(batch, pages).int()
+    k_pool = torch.zeros(L, nb, hkv, bs, d, dtype=torch.bfloat16, device=DEV)
+    v_pool = torch.zeros_like(k_pool)
+    prompt_k = torch.randn(L, batch, hkv, P, d, device=DEV, generator=g).to(torch.bfloat16)
+    prompt_v = torch.randn(L, batch, hkv, P, d, device=DEV, generator=g).to(torch.bfloat16)
+    new_k = torch.randn(N, L, batch, hkv, d, device=DEV, generator=g).to(torch.bfloat16)
+    new_v = torch.randn(N, L, batch, hkv, d, device=DEV, generator=g).to(torch.bfloat16)
+    for layer in range(L):
+        paged_kv_append_prompt(prompt_k[layer], prompt_v[layer], k_pool[layer], v_pool[layer], perm)
+    ctx = torch.full((batch,), P, dtype=torch.int32, device=DEV)
+    for step in range(N):
+        for layer in range(L):
+            paged_kv_append(new_k[step, layer], new_v[step, layer], k_pool[layer], v_pool[layer], perm, ctx)
+        ctx += 1
+    for layer in range(L):
+        kg, vg = gather_kv(k_pool[layer], v_pool[layer], perm, ctx)
+        exp_k = torch.cat([prompt_k[layer], new_k[:, layer].permute(1, 2, 0, 3)], dim=2)
+        exp_v = torch.cat([prompt_v[layer], new_v[:, layer].permute(1, 2, 0, 3)], dim=2)
+        assert torch.equal(kg.view(torch.int16), exp_k.view(torch.int16))
+        assert torch.equal(vg.view(torch.int16), exp_v.view(torch.int16))
+    # and one layer against the oracle's scatter of the same data
+    layer = 5
+    kc = torch.zeros(nb, hkv, bs, d, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    full_k = torch.cat([prompt_k[layer], new_k[:, layer].permute(1, 2, 0, 3)], dim=2).cpu()
+    full_v = torch.cat([prompt_v[layer], new_v[:, layer].permute(1, 2, 0, 3)], dim=2).cpu()
+    oracle.append_prompt(full_k, full_v, kc, vc, perm.cpu())
+    assert _sha(k_pool[layer], v_pool[layer]) == _sha(kc, vc)
