@@ -70,10 +70,13 @@ def global_lengths(config: int, n_total: int, seed: int = 1234) -> np.ndarray:
 class Workload:
     """One rank's shard: page pool, block tables, per-layer q/k_new/v_new, context lengths."""
 
-    def __init__(self, config: int, rank: int, world: int, layers: int | None, device):
+    def __init__(self, config: int, rank: int, world: int, layers: int | None, device, seqs: int | None = None):
         from grpo_training_engine_b200.sharding import lpt_assign
 
-        c = CONFIGS[config]
+        c = dict(CONFIGS[config])
+        if seqs:
+            c["seqs"] = seqs
+            c["name"] += f" [reduced to {seqs} seqs/GPU]"
         self.config, self.cfg = config, c
         self.layers = layers or c["layers"]
         hq, hkv, d, bs = c["hq"], c["hkv"], c["d"], c["bs"]
@@ -275,7 +278,7 @@ def run_ours(args, rank, world, local):
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    wl = Workload(args.config, rank, world, args.layers, device)
+    wl = Workload(args.config, rank, world, args.layers, device, args.seqs)
     L, B = wl.layers, wl.B
     stream = torch.cuda.current_stream(device)
 
@@ -658,6 +661,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", type=int, default=4, choices=sorted(CONFIGS))
     ap.add_argument("--layers", type=int, default=None, help="override the layer count (diagnostics only)")
+    ap.add_argument("--seqs", type=int, default=None, help="override sequences per GPU (diagnostics only)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--pages-per-split", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")

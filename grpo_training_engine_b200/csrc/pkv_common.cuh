@@ -174,9 +174,9 @@ template <> struct Mma16816<__nv_bfloat16> {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&v);
   }
-  static __device__ __forceinline__ uint16_t bits(float x) {
-    __nv_bfloat16 v = __float2bfloat16_rn(x);
-    return *reinterpret_cast<uint16_t *>(&v);
+  static __device__ __forceinline__ float unpack_lo(uint32_t v) { return __uint_as_float(v << 16); }
+  static __device__ __forceinline__ float unpack_hi(uint32_t v) {
+    return __uint_as_float(v & 0xffff0000u);
   }
 };
 
@@ -193,9 +193,11 @@ template <> struct Mma16816<__half> {
     __half2 v = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&v);
   }
-  static __device__ __forceinline__ uint16_t bits(float x) {
-    __half v = __float2half_rn(x);
-    return *reinterpret_cast<uint16_t *>(&v);
+  static __device__ __forceinline__ float unpack_lo(uint32_t v) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(v & 0xffffu)));
+  }
+  static __device__ __forceinline__ float unpack_hi(uint32_t v) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(v >> 16)));
   }
 };
 

@@ -80,7 +80,7 @@ WsLayout ws_layout(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t max_bl
   w.hdr = off; off += 256;
   w.seq_off = off; off = align_up(off + sizeof(int32_t) * (size_t)B, 256);
   w.seq_nsplit = off; off = align_up(off + sizeof(int32_t) * (size_t)B, 256);
-  w.items = off; off = align_up(off + sizeof(int2) * (size_t)w.max_items, 256);
+  w.items = off; off = align_up(off + sizeof(int4) * (size_t)w.max_items, 256);
   w.counters = off; off = align_up(off + sizeof(int32_t) * (size_t)B * w.units_per_item, 256);
   w.partials = off;
   off = align_up(off + sizeof(float) * (size_t)w.max_items * w.units_per_item * w.part_floats, 256);
@@ -100,6 +100,7 @@ struct DecodeArgs {
   const void *vc;
   int32_t B, Hq, Hkv, G, GR, HG, D, bs, num_blocks, max_blocks, P, upi, part_floats;
   int32_t q_dtype, kv_dtype;
+  int32_t q_vec;  // q rows are 16-byte aligned and contiguous in head_dim
   int64_t q0, q1, q2;
   int64_t c0, c1, c2, c3;
   int64_t bt0, bt1;
@@ -108,10 +109,11 @@ struct DecodeArgs {
   const int32_t *hdr;
   const int32_t *seq_off;
   const int32_t *seq_nsplit;
-  const int2 *items;
+  const int4 *items;  // per item {b, split, clamped ctx, splits of b}
   int32_t *counters;
   float *partials;
   int32_t *status;
+  int32_t *sched;  // {next unit, finished CTAs}: dynamic scheduling of the tensor-core kernel
 };
 
 __device__ __forceinline__ int32_t clamp_ctx(const DecodeArgs &a, int32_t b) {
@@ -124,17 +126,17 @@ struct Unit {
   int32_t b, s, kvh, hg, nsplit, ctx, p_begin, p_end, gcount, qh0;
 };
 
-__device__ __forceinline__ Unit decode_unit(const DecodeArgs &a, int32_t w) {
+// Work unit w = (item, kv head, head group); the item descriptor comes from the plan.
+__device__ __forceinline__ Unit unit_from(const DecodeArgs &a, int32_t w, int4 it) {
   Unit u;
   const int32_t item = w / a.upi;
   const int32_t r = w - item * a.upi;
   u.kvh = r / a.HG;
   u.hg = r - u.kvh * a.HG;
-  const int2 it = a.items[item];
   u.b = it.x;
   u.s = it.y;
-  u.nsplit = a.seq_nsplit[u.b];
-  u.ctx = clamp_ctx(a, u.b);
+  u.ctx = it.z;
+  u.nsplit = it.w;
   const int32_t npages = (u.ctx + a.bs - 1) / a.bs;
   u.p_begin = u.s * a.P;
   u.p_end = min(u.p_begin + a.P, npages);
@@ -145,6 +147,10 @@ __device__ __forceinline__ Unit decode_unit(const DecodeArgs &a, int32_t w) {
   return u;
 }
 
+__device__ __forceinline__ Unit decode_unit(const DecodeArgs &a, int32_t w) {
+  return unit_from(a, w, a.items[w / a.upi]);
+}
+
 // ---------------------------------------------------------------------------
 // plan: per-sequence split counts, prefix offsets, item list, zeroed counters
 // ---------------------------------------------------------------------------
@@ -152,7 +158,7 @@ constexpr int kPlanThreads = 1024;
 
 __global__ void __launch_bounds__(kPlanThreads)
 plan_kernel(const int32_t *__restrict__ ctx, int32_t B, int32_t bs, int32_t max_blocks, int32_t P,
-            int32_t upi, int32_t *hdr, int32_t *seq_off, int32_t *seq_nsplit, int2 *items,
+            int32_t upi, int32_t *hdr, int32_t *seq_off, int32_t *seq_nsplit, int4 *items,
             int32_t *counters, int32_t *status) {
   __shared__ int32_t warp_tot[kPlanThreads / 32];
   __shared__ int32_t carry;
@@ -164,9 +170,9 @@ plan_kernel(const int32_t *__restrict__ ctx, int32_t B, int32_t bs, int32_t max_
   const int32_t cap = max_blocks * bs;
   for (int32_t base = 0; base < B; base += kPlanThreads) {
     const int32_t b = base + tid;
-    int32_t n = 0;
+    int32_t n = 0, c = 0;
     if (b < B) {
-      int32_t c = ctx[b];
+      c = ctx[b];
       if (c < 0 || c > cap) {
         flag_status(status, PKV_DEV_CTX_OUT_OF_RANGE);
         c = c < 0 ? 0 : cap;
@@ -197,7 +203,7 @@ plan_kernel(const int32_t *__restrict__ ctx, int32_t B, int32_t bs, int32_t max_
     if (b < B) {
       seq_off[b] = excl;
       seq_nsplit[b] = n;
-      for (int32_t s = 0; s < n; ++s) items[excl + s] = make_int2(b, s);
+      for (int32_t s = 0; s < n; ++s) items[excl + s] = make_int4(b, s, c, n);
     }
     __syncthreads();
     if (tid == 0) carry += warp_tot[kPlanThreads / 32 - 1];
@@ -208,6 +214,8 @@ plan_kernel(const int32_t *__restrict__ ctx, int32_t B, int32_t bs, int32_t max_
     hdr[1] = P;
     hdr[2] = B;
     hdr[3] = upi;
+    hdr[4] = 0;  // next unit to hand out (dynamic scheduling)
+    hdr[5] = 0;  // CTAs that have finished fetching units
   }
 }
 
@@ -218,9 +226,9 @@ plan_kernel(const int32_t *__restrict__ ctx, int32_t B, int32_t bs, int32_t max_
 // to xd floats. `sync` is a barrier over the participating threads.
 // ---------------------------------------------------------------------------
 template <typename Sync>
-__device__ bool unit_epilogue(const DecodeArgs &a, const Unit &u, int nwarps, const float *xm,
-                              const float *xl, const float *xo, int xd, int tid, int nthreads,
-                              int32_t *flag_smem, Sync &sync) {
+__device__ bool unit_epilogue(const DecodeArgs &a, const Unit &u, int nwarps, int xr,
+                              const float *xm, const float *xl, const float *xo, int xd, int tid,
+                              int nthreads, int32_t *flag_smem, Sync &sync) {
   const int32_t D = a.D;
   const int32_t GR = a.GR;
   const int32_t n = u.gcount * D;
@@ -229,13 +237,13 @@ __device__ bool unit_epilogue(const DecodeArgs &a, const Unit &u, int nwarps, co
   for (int32_t i = tid; i < n; i += nthreads) {
     const int32_t g = i / D, d = i - g * D;
     float M = -INFINITY;
-    for (int w = 0; w < nwarps; ++w) M = fmaxf(M, xm[w * kTcRows + g]);
+    for (int w = 0; w < nwarps; ++w) M = fmaxf(M, xm[w * xr + g]);
     float L = 0.f, O = 0.f;
     if (M != -INFINITY) {
       for (int w = 0; w < nwarps; ++w) {
-        const float f = exp2_or_zero(xm[w * kTcRows + g] - M);
-        L += f * xl[w * kTcRows + g];
-        O += f * xo[(w * kTcRows + g) * xd + d];
+        const float f = exp2_or_zero(xm[w * xr + g] - M);
+        L += f * xl[w * xr + g];
+        O += f * xo[(w * xr + g) * xd + d];
       }
     }
     if (u.nsplit == 1) {
@@ -252,8 +260,13 @@ __device__ bool unit_epilogue(const DecodeArgs &a, const Unit &u, int nwarps, co
   __threadfence();
   if (!sync()) return false;
   if (tid == 0) {
-    const int old = atomicAdd(&a.counters[((int64_t)u.b * a.Hkv + u.kvh) * a.HG + u.hg], 1);
-    *flag_smem = (old == u.nsplit - 1);
+    int32_t *cnt = &a.counters[((int64_t)u.b * a.Hkv + u.kvh) * a.HG + u.hg];
+    const int old = atomicAdd(cnt, 1);
+    const bool last = (old == u.nsplit - 1);
+    // Every split of this (sequence, head group) has arrived: reset the counter so
+    // the same plan can drive the next launch (one plan serves all layers of a step).
+    if (last) atomicExch(cnt, 0);
+    *flag_smem = last;
   }
   if (!sync()) return false;
   if (*flag_smem) {
@@ -367,8 +380,8 @@ decode_generic_kernel(DecodeArgs a) {
           for (int j = 0; j < DJ; ++j) s = fmaf(q_s[g * DP + lane + 32 * j], kr[j], s);
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-          // reference order: logits = (q . k) * scale (paged_kv.py:133-135)
-          const float x = (s * a.scale) * kLog2e;
+          // logits = (q . k) * scale (paged_kv.py:133-135), kept in log2 units
+          const float x = s * a.scale_log2;
           const float mn = fmaxf(m[g], x);
           const float alpha = (mn == m[g]) ? 1.f : exp2_or_zero(m[g] - mn);
           const float p = exp2f(x - mn);
@@ -392,7 +405,7 @@ decode_generic_kernel(DecodeArgs a) {
       }
     }
     __syncthreads();
-    unit_epilogue(a, u, kGenWarps, xm, xl, xo, DP, tid, kGenThreads, flag, sync);
+    unit_epilogue(a, u, kGenWarps, kTcRows, xm, xl, xo, DP, tid, kGenThreads, flag, sync);
   }
 }
 
@@ -407,15 +420,23 @@ size_t generic_smem_bytes(int DJ, int GM) {
 // ---------------------------------------------------------------------------
 enum : int32_t { kElemPage = 0, kElemEmpty = 1, kElemStop = 2 };
 
+// One pipeline element as the producer publishes it to a consumer warp: the
+// page (or its absence) plus everything the consumer needs about the unit,
+// so consumers never touch global memory for bookkeeping.
 struct __align__(16) SlotMeta {
-  int32_t kind;   // kElemPage / kElemEmpty / kElemStop
-  int32_t valid;  // valid tokens in the page (1..16)
-  int32_t last;   // last element of this warp for the current unit
-  int32_t work;   // work-unit id
+  int32_t kind;    // kElemPage / kElemEmpty / kElemStop
+  int32_t valid;   // valid tokens in the page (1..16)
+  int32_t last;    // last element of this warp for the unit
+  int32_t work;    // work-unit id
+  int32_t qslot;   // smem slot holding the unit's query rows
+  int32_t b, s, nsplit;
+  int32_t kvh, hg, gcount, qh0;
+  int32_t pad[4];
 };
 
-constexpr int kBoxRows = 16;                 // tokens per page (block_size)
-constexpr int kBoxBytes = kBoxRows * 128;    // one [16][64] bf16 box, 128-byte swizzled rows
+constexpr int kBoxRows = 16;               // tokens per page (block_size)
+constexpr int kBoxBytes = kBoxRows * 128;  // one [16][64] 16-bit box, 128-byte swizzled rows
+constexpr int kQSlots = 2;                 // query-row slots (units in flight per CTA)
 
 template <int D> struct TcShape {
   static constexpr int kBoxes = D / 64;
@@ -423,31 +444,41 @@ template <int D> struct TcShape {
   static constexpr int kSlot = 2 * kTile;           // K + V
   static constexpr int kKSteps = D / 16;
   static constexpr int kNTiles = D / 8;
-  static constexpr int kXd = D + 4;  // padded exchange row (floats)
+  static constexpr int kXd = D + 4;           // padded exchange row (floats)
+  static constexpr int kQRow = D * 2 + 16;    // padded query row (bytes): conflict-free ldmatrix
+  static constexpr int kQSlot = kTcRows * kQRow;
 };
-
-// Byte address inside a TMA tile with 128-byte swizzle: 16-byte chunk c of row r
-// lands at chunk c ^ (r % 8) of that row (tile base is 1024-byte aligned).
-__device__ __forceinline__ uint32_t swz(uint32_t tile, int r, int d0) {
-  const int box = d0 >> 6;
-  const int c = (d0 & 63) >> 3;
-  return tile + box * kBoxBytes + r * 128 + ((c ^ (r & 7)) << 4);
-}
 
 template <int D, int NW, int S>
 struct TcSmem {
   static constexpr size_t kTiles = (size_t)NW * S * TcShape<D>::kSlot;
-  static constexpr size_t kMeta = kTiles;
-  static constexpr size_t kFull = kMeta + sizeof(SlotMeta) * NW * S;
+  static constexpr size_t kQ = kTiles;
+  static constexpr size_t kMeta = kQ + (size_t)kQSlots * TcShape<D>::kQSlot;
+  static constexpr size_t kFull = align_up(kMeta + sizeof(SlotMeta) * NW * S, 16);
   static constexpr size_t kEmpty = kFull + 8 * NW * S;
-  static constexpr size_t kGroup = kEmpty + 8 * NW * S;
+  static constexpr size_t kQEmpty = kEmpty + 8 * NW * S;
+  static constexpr size_t kGroup = kQEmpty + 8 * kQSlots;
   static constexpr size_t kFlag = kGroup + 8;
   static constexpr size_t kXm = align_up(kFlag + 8, 16);
   static constexpr size_t kXl = kXm + sizeof(float) * NW * kTcRows;
   static constexpr size_t kXo = kXl + sizeof(float) * NW * kTcRows;
-  static constexpr size_t kBt = kXo + sizeof(float) * NW * kTcRows * TcShape<D>::kXd;
-  static size_t bytes(int32_t P) { return kBt + sizeof(int32_t) * (size_t)P + 1024; }
+  // exchange rows for `rows` query heads per warp, then the producer's block-table buffer
+  __host__ __device__ static size_t bt_offset(int rows) {
+    return align_up(kXo + sizeof(float) * (size_t)NW * rows * TcShape<D>::kXd, 16);
+  }
+  static size_t bytes(int rows, int32_t P) { return bt_offset(rows) + sizeof(int32_t) * (size_t)P + 1024; }
 };
+
+// Packs (x, y) into a 16-bit pair `hi` and the rounding remainders into `lo`.
+template <typename M>
+__device__ __forceinline__ void split_pair(float x, float y, uint32_t &hi, uint32_t &lo) {
+  hi = M::pack(x, y);
+  const float hx = M::unpack_lo(hi), hy = M::unpack_hi(hi);
+  lo = M::pack(x - hx, y - hy);
+}
+
+// Block-table entries of a unit held in the producer's registers, lane-strided.
+constexpr int kBtRegs = 8;  // supports up to 256 pages per unit
 
 template <typename T, int D, int NW, int S>
 __global__ void __launch_bounds__((NW + 1) * 32, 1)
@@ -459,15 +490,17 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t *tiles = smem;
+  uint8_t *qbuf = smem + L::kQ;
   SlotMeta *meta = reinterpret_cast<SlotMeta *>(smem + L::kMeta);
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::kFull);
   uint64_t *empty = reinterpret_cast<uint64_t *>(smem + L::kEmpty);
+  uint64_t *qempty = reinterpret_cast<uint64_t *>(smem + L::kQEmpty);
   uint64_t *group = reinterpret_cast<uint64_t *>(smem + L::kGroup);
   int32_t *flag = reinterpret_cast<int32_t *>(smem + L::kFlag);
   float *xm = reinterpret_cast<float *>(smem + L::kXm);
   float *xl = reinterpret_cast<float *>(smem + L::kXl);
   float *xo = reinterpret_cast<float *>(smem + L::kXo);
-  int32_t *btbuf = reinterpret_cast<int32_t *>(smem + L::kBt);
+  int32_t *btbuf = reinterpret_cast<int32_t *>(smem + L::bt_offset(a.GR));
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid == 0) {
@@ -475,6 +508,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
+    for (int i = 0; i < kQSlots; ++i) mbar_init(&qempty[i], 1);
     mbar_init(group, NW);
     fence_mbar_init();
   }
@@ -483,24 +517,105 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
   const int32_t total = a.hdr[0];
 
   if (warp == NW) {
-    // ======================= producer warp =======================
+    // =========================== producer warp ===========================
+    // Units come from a global counter (dynamic scheduling). The warp keeps a
+    // three-deep software pipeline so no global-load latency is exposed at a
+    // unit boundary: while lane 0 streams unit n, the unit id of n+3 is being
+    // fetched, the descriptor of n+2 loaded, and the block-table entries and
+    // query rows of n+1 loaded into registers.
+    const uint32_t FULL = 0xffffffffu;
+    int32_t fetched = 0;
+    if (lane == 0) fetched = atomicAdd(&a.sched[0], 1);
+    int32_t w1 = __shfl_sync(FULL, fetched, 0);
+    if (lane == 0) fetched = atomicAdd(&a.sched[0], 1);
+    int32_t w2 = __shfl_sync(FULL, fetched, 0);
+    if (lane == 0) fetched = atomicAdd(&a.sched[0], 1);  // w3, broadcast at the first rotation
+    const int4 none = make_int4(0, 0, 0, 1);
+    int4 d1 = w1 < total ? a.items[w1 / a.upi] : none;
+    int4 d2 = w2 < total ? a.items[w2 / a.upi] : none;
+
+    // registers holding the NEXT unit's block-table entries and query rows
+    int32_t btr[kBtRegs];
+    uint4 qr[(kTcRows * D * 2 / 16 + 31) / 32];
+    constexpr int kQVec = kTcRows * D * 2 / 16;  // 16-byte vectors of a query block
+    constexpr int kQPerLane = (kQVec + 31) / 32;
+    auto load_next = [&](int32_t w, int4 d) {
+      Unit u = unit_from(a, w, d);
+      const int32_t np = u.p_end - u.p_begin;
+#pragma unroll
+      for (int i = 0; i < kBtRegs; ++i) {
+        const int32_t pi = lane + 32 * i;
+        btr[i] = (w < total && pi < np) ? a.bt[u.b * a.bt0 + (int64_t)(u.p_begin + pi) * a.bt1] : -1;
+      }
+      const uint8_t *qb = reinterpret_cast<const uint8_t *>(a.q);
+#pragma unroll
+      for (int i = 0; i < kQPerLane; ++i) {
+        const int v = lane + 32 * i;
+        const int r = v / (D / 8), c = v % (D / 8);
+        uint4 x = make_uint4(0, 0, 0, 0);
+        if (w < total && v < kQVec && r < u.gcount) {
+          const int64_t row = u.b * a.q0 + (int64_t)(u.qh0 + r) * a.q1;
+          if (a.q_vec) {
+            x = *reinterpret_cast<const uint4 *>(qb + 2 * row + 16 * c);
+          } else {  // arbitrary strides: eight 16-bit loads
+            const uint16_t *qh = reinterpret_cast<const uint16_t *>(a.q);
+            uint32_t wv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              wv[e] = (uint32_t)qh[row + (int64_t)(8 * c + 2 * e) * a.q2] |
+                      ((uint32_t)qh[row + (int64_t)(8 * c + 2 * e + 1) * a.q2] << 16);
+            x = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+          }
+        }
+        qr[i] = x;
+      }
+    };
+    load_next(w1, d1);
+
     int32_t kcount[NW];
 #pragma unroll
     for (int i = 0; i < NW; ++i) kcount[i] = 0;
     bool ok = true;
-    for (int32_t w = blockIdx.x; w < total && ok; w += gridDim.x) {
-      const Unit u = decode_unit(a, w);
+    int32_t nunit = 0;  // units issued by this CTA (query slot = nunit % kQSlots)
+    while (w1 < total && ok) {
+      const Unit u = unit_from(a, w1, d1);
       const int32_t npages = u.p_end - u.p_begin;
-      for (int32_t i = lane; i < npages; i += 32) {
-        int32_t page = a.bt[u.b * a.bt0 + (int64_t)(u.p_begin + i) * a.bt1];
-        if (page < 0 || page >= a.num_blocks) {
-          flag_status(a.status, PKV_DEV_PAGE_OUT_OF_RANGE);
-          page = -1;
+      const int qs = nunit % kQSlots;
+      // (1) the unit's block-table entries and query rows -> smem
+      if (nunit >= kQSlots) {
+        if (!mbar_wait_bounded(&qempty[qs], ((nunit / kQSlots) - 1) & 1)) {
+          flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
+          ok = false;
         }
-        btbuf[i] = page;
+      }
+#pragma unroll
+      for (int i = 0; i < kBtRegs; ++i) {
+        const int32_t pi = lane + 32 * i;
+        if (pi < npages) {
+          int32_t page = btr[i];
+          if (page < 0 || page >= a.num_blocks) {
+            flag_status(a.status, PKV_DEV_PAGE_OUT_OF_RANGE);
+            page = -1;
+          }
+          btbuf[pi] = page;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kQPerLane; ++i) {
+        const int v = lane + 32 * i;
+        if (v < kQVec) {
+          const int r = v / (D / 8), c = v % (D / 8);
+          *reinterpret_cast<uint4 *>(qbuf + qs * Sh::kQSlot + r * Sh::kQRow + 16 * c) = qr[i];
+        }
       }
       __syncwarp();
-      if (lane == 0) {
+      // (2) prefetch the next unit; fetch the unit after the one after
+      load_next(w2, d2);
+      const int32_t w3 = __shfl_sync(FULL, fetched, 0);
+      const int4 d3 = w3 < total ? a.items[w3 / a.upi] : none;
+      if (lane == 0 && w3 < total) fetched = atomicAdd(&a.sched[0], 1);
+      // (3) stream the unit's pages to the consumer warps (page p -> warp p % NW)
+      if (lane == 0 && ok) {
         const int32_t rounds = npages > 0 ? (npages + NW - 1) / NW : 1;
         for (int32_t j = 0; j < rounds && ok; ++j) {
 #pragma unroll
@@ -522,7 +637,15 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
             md.kind = page >= 0 ? kElemPage : kElemEmpty;
             md.valid = has ? min(kBoxRows, u.ctx - (u.p_begin + pi) * kBoxRows) : 0;
             md.last = last ? 1 : 0;
-            md.work = w;
+            md.work = w1;
+            md.qslot = qs;
+            md.b = u.b;
+            md.s = u.s;
+            md.nsplit = u.nsplit;
+            md.kvh = u.kvh;
+            md.hg = u.hg;
+            md.gcount = u.gcount;
+            md.qh0 = u.qh0;
             meta[slot] = md;
             if (page >= 0) {
               mbar_arrive_expect_tx(&full[slot], Sh::kSlot);
@@ -530,8 +653,8 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
 #pragma unroll
               for (int bx = 0; bx < Sh::kBoxes; ++bx) {
                 tma_load_4d(kt + bx * kBoxBytes, &tmk, &full[slot], bx * 64, 0, u.kvh, page);
-                tma_load_4d(kt + Sh::kTile + bx * kBoxBytes, &tmv, &full[slot], bx * 64, 0, u.kvh,
-                            page);
+                tma_load_4d(kt + Sh::kTile + bx * kBoxBytes, &tmv, &full[slot], bx * 64, 0,
+                            u.kvh, page);
               }
             } else {
               mbar_arrive(&full[slot]);
@@ -539,8 +662,23 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
           }
         }
       }
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-      __syncwarp();  // btbuf is rewritten for the next unit
+      ok = __shfl_sync(FULL, ok ? 1 : 0, 0) != 0;
+      __syncwarp();  // btbuf / qbuf are rewritten for the next unit
+      ++nunit;
+      w1 = w2;
+      d1 = d2;
+      w2 = w3;
+      d2 = d3;
+    }
+    if (lane == 0) {
+      // This CTA will fetch no more units. The last CTA to get here resets the
+      // scheduling counters so the plan can drive the next launch.
+      __threadfence();
+      const int done = atomicAdd(&a.sched[1], 1);
+      if (done == (int)gridDim.x - 1) {
+        atomicExch(&a.sched[0], 0);
+        atomicExch(&a.sched[1], 0);
+      }
     }
     if (lane == 0 && ok) {
 #pragma unroll
@@ -552,7 +690,10 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
           flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
           break;
         }
-        SlotMeta md{kElemStop, 0, 1, -1};
+        SlotMeta md{};
+        md.kind = kElemStop;
+        md.last = 1;
+        md.work = -1;
         meta[slot] = md;
         mbar_arrive(&full[slot]);
       }
@@ -560,12 +701,26 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
     return;
   }
 
-  // ======================= consumer warps =======================
+  // =========================== consumer warps ===========================
   using M = Mma16816<T>;
   const int cw = warp;
   const int r1 = lane >> 2, r2 = r1 + 8, cq = 2 * (lane & 3);
-  const uint16_t *qraw = reinterpret_cast<const uint16_t *>(a.q);
   GroupSync sync{group, 0u, a.status};
+
+  // per-lane byte offsets inside a swizzled tile (128-byte rows, 16-byte
+  // chunk c of row r stored at chunk c ^ (r % 8)); the remaining parts of the
+  // addresses are compile-time constants
+  const uint32_t c0 = (uint32_t)((lane >> 3) ^ (lane & 7));
+  const uint32_t k_off0 = (lane & 7) * 128 + (c0 << 4);
+  const uint32_t k_off1 = (lane & 7) * 128 + ((c0 ^ 4u) << 4);
+  const uint32_t cv = (uint32_t)((lane >> 4) ^ (lane & 7));
+  const uint32_t v_row = ((lane >> 3) & 1) * 1024 + (lane & 7) * 128;
+  const uint32_t v_off0 = v_row + ((cv ^ 0u) << 4);
+  const uint32_t v_off1 = v_row + ((cv ^ 2u) << 4);
+  const uint32_t v_off2 = v_row + ((cv ^ 4u) << 4);
+  const uint32_t v_off3 = v_row + ((cv ^ 6u) << 4);
+  // query rows: lane -> row (lane % 8) + 8 * ((lane / 8) % 2), column 8 * (lane / 16)
+  const uint32_t q_off = ((lane & 7) + 8 * ((lane >> 3) & 1)) * Sh::kQRow + 16 * (lane >> 4);
 
   uint32_t qa[Sh::kKSteps][4];
   float o[Sh::kNTiles][4];
@@ -573,7 +728,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
 #pragma unroll
   for (int i = 0; i < Sh::kNTiles; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   int32_t cur_work = -1;
-  Unit u{};
+  const float sl2 = a.scale_log2;
 
   for (int32_t k = 0;; ++k) {
     const int slot = cw * S + (k % S);
@@ -585,29 +740,16 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
     if (md.kind == kElemStop) break;
     if (md.work != cur_work) {
       cur_work = md.work;
-      u = decode_unit(a, md.work);
-      // query fragments (A operand): rows = head group rows, cols = head_dim
-      const int64_t qb = u.b * a.q0;
+      const uint32_t qb = smem_u32(qbuf + md.qslot * Sh::kQSlot) + q_off;
 #pragma unroll
-      for (int ks = 0; ks < Sh::kKSteps; ++ks) {
-        const int c = ks * 16 + cq;
-        auto ld2 = [&](int r, int cc) -> uint32_t {
-          if (r >= u.gcount) return 0u;
-          const int64_t base = qb + (int64_t)(u.qh0 + r) * a.q1;
-          const uint32_t lo = qraw[base + (int64_t)cc * a.q2];
-          const uint32_t hi = qraw[base + (int64_t)(cc + 1) * a.q2];
-          return lo | (hi << 16);
-        };
-        qa[ks][0] = ld2(r1, c);
-        qa[ks][1] = ld2(r2, c);
-        qa[ks][2] = ld2(r1, c + 8);
-        qa[ks][3] = ld2(r2, c + 8);
-      }
+      for (int ks = 0; ks < Sh::kKSteps; ++ks)
+        ldsm_x4(qb + ks * 32, qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
     }
 
     if (md.kind == kElemPage) {
       const uint32_t kt = smem_u32(tiles + (size_t)slot * Sh::kSlot);
       const uint32_t vt = kt + Sh::kTile;
+      const uint32_t kb0 = kt + k_off0, kb1 = kt + k_off1;
       // ---- S = Q K^T for the 16 tokens of the page (two n-tiles of 8 tokens)
       float sacc[2][4];
 #pragma unroll
@@ -616,7 +758,8 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
 #pragma unroll
         for (int kp = 0; kp < Sh::kKSteps / 2; ++kp) {
           uint32_t b0, b1, b2, b3;
-          ldsm_x4(swz(kt, nt * 8 + (lane & 7), kp * 32 + 8 * (lane >> 3)), b0, b1, b2, b3);
+          const uint32_t base = (kp & 1) ? kb1 : kb0;
+          ldsm_x4(base + nt * 1024 + (kp >> 1) * kBoxBytes, b0, b1, b2, b3);
           M::run(sacc[nt], qa[2 * kp][0], qa[2 * kp][1], qa[2 * kp][2], qa[2 * kp][3], b0, b1);
           M::run(sacc[nt], qa[2 * kp + 1][0], qa[2 * kp + 1][1], qa[2 * kp + 1][2],
                  qa[2 * kp + 1][3], b2, b3);
@@ -624,20 +767,31 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
       }
       // ---- online softmax over the page (rows r1, r2; four tokens per lane)
       float x1[4], x2[4];
+      if (md.valid == kBoxRows) {
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
+        for (int nt = 0; nt < 2; ++nt) {
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const bool ok = nt * 8 + cq + j < md.valid;
-          x1[nt * 2 + j] = ok ? (sacc[nt][j] * a.scale) * kLog2e : -INFINITY;
-          x2[nt * 2 + j] = ok ? (sacc[nt][2 + j] * a.scale) * kLog2e : -INFINITY;
+          for (int j = 0; j < 2; ++j) {
+            x1[nt * 2 + j] = sacc[nt][j] * sl2;
+            x2[nt * 2 + j] = sacc[nt][2 + j] * sl2;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const bool in = nt * 8 + cq + j < md.valid;
+            x1[nt * 2 + j] = in ? sacc[nt][j] * sl2 : -INFINITY;
+            x2[nt * 2 + j] = in ? sacc[nt][2 + j] * sl2 : -INFINITY;
+          }
         }
       }
       float mx1 = fmaxf(fmaxf(x1[0], x1[1]), fmaxf(x1[2], x1[3]));
       float mx2 = fmaxf(fmaxf(x2[0], x2[1]), fmaxf(x2[2], x2[3]));
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
       mx2 = fmaxf(mx2, __shfl_xor_sync(0xffffffffu, mx2, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
       mx2 = fmaxf(mx2, __shfl_xor_sync(0xffffffffu, mx2, 2));
       const float n1 = fmaxf(m1, mx1), n2 = fmaxf(m2, mx2);
       const float al1 = (n1 == m1) ? 1.f : exp2_or_zero(m1 - n1);
@@ -652,25 +806,33 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
       l2 = l2 * al2 + ((p2[0] + p2[1]) + (p2[2] + p2[3]));
       m1 = n1;
       m2 = n2;
+      // the running max settles after a few pages: rescale only when it moved
+      if (__any_sync(0xffffffffu, (al1 != 1.f) || (al2 != 1.f))) {
 #pragma unroll
-      for (int i = 0; i < Sh::kNTiles; ++i) {
-        o[i][0] *= al1;
-        o[i][1] *= al1;
-        o[i][2] *= al2;
-        o[i][3] *= al2;
+        for (int i = 0; i < Sh::kNTiles; ++i) {
+          o[i][0] *= al1;
+          o[i][1] *= al1;
+          o[i][2] *= al2;
+          o[i][3] *= al2;
+        }
       }
-      // ---- O += P V (P as the A operand straight from the S fragments)
-      const uint32_t pa0 = M::pack(p1[0], p1[1]);
-      const uint32_t pa1 = M::pack(p2[0], p2[1]);
-      const uint32_t pa2 = M::pack(p1[2], p1[3]);
-      const uint32_t pa3 = M::pack(p2[2], p2[3]);
+      // ---- O += P V, P as the A operand straight from the S fragments. P is split
+      // into a 16-bit head and a 16-bit remainder (P = hi + lo, |lo| <= 2^-9 |P|),
+      // so the product keeps ~17 significant bits of P instead of 8.
+      uint32_t ph[4], pl[4];
+      split_pair<M>(p1[0], p1[1], ph[0], pl[0]);
+      split_pair<M>(p2[0], p2[1], ph[1], pl[1]);
+      split_pair<M>(p1[2], p1[3], ph[2], pl[2]);
+      split_pair<M>(p2[2], p2[3], ph[3], pl[3]);
 #pragma unroll
       for (int np = 0; np < Sh::kNTiles / 2; ++np) {
         uint32_t b0, b1, b2, b3;
-        ldsm_x4_trans(swz(vt, ((lane >> 3) & 1) * 8 + (lane & 7), 8 * (2 * np + (lane >> 4))), b0,
-                      b1, b2, b3);
-        M::run(o[2 * np], pa0, pa1, pa2, pa3, b0, b1);
-        M::run(o[2 * np + 1], pa0, pa1, pa2, pa3, b2, b3);
+        const uint32_t vo = (np & 3) == 0 ? v_off0 : (np & 3) == 1 ? v_off1 : (np & 3) == 2 ? v_off2 : v_off3;
+        ldsm_x4_trans(vt + vo + (np >> 2) * kBoxBytes, b0, b1, b2, b3);
+        M::run(o[2 * np], ph[0], ph[1], ph[2], ph[3], b0, b1);
+        M::run(o[2 * np + 1], ph[0], ph[1], ph[2], ph[3], b2, b3);
+        M::run(o[2 * np], pl[0], pl[1], pl[2], pl[3], b0, b1);
+        M::run(o[2 * np + 1], pl[0], pl[1], pl[2], pl[3], b2, b3);
       }
     }
     __syncwarp();
@@ -678,32 +840,44 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
 
     if (md.last) {
       // ---- this warp is done with the unit: publish its state, then combine
+      Unit u;
+      u.b = md.b;
+      u.s = md.s;
+      u.kvh = md.kvh;
+      u.hg = md.hg;
+      u.nsplit = md.nsplit;
+      u.gcount = md.gcount;
+      u.qh0 = md.qh0;
+      const int xr = a.GR;
       float s1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
       s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
       float s2 = l2 + __shfl_xor_sync(0xffffffffu, l2, 1);
       s2 += __shfl_xor_sync(0xffffffffu, s2, 2);
       if ((lane & 3) == 0) {
         if (r1 < u.gcount) {
-          xm[cw * kTcRows + r1] = m1;
-          xl[cw * kTcRows + r1] = s1;
+          xm[cw * xr + r1] = m1;
+          xl[cw * xr + r1] = s1;
         }
         if (r2 < u.gcount) {
-          xm[cw * kTcRows + r2] = m2;
-          xl[cw * kTcRows + r2] = s2;
+          xm[cw * xr + r2] = m2;
+          xl[cw * xr + r2] = s2;
         }
       }
 #pragma unroll
       for (int nt = 0; nt < Sh::kNTiles; ++nt) {
         const int d = nt * 8 + cq;
         if (r1 < u.gcount)
-          *reinterpret_cast<float2 *>(&xo[(cw * kTcRows + r1) * Sh::kXd + d]) =
+          *reinterpret_cast<float2 *>(&xo[(cw * xr + r1) * Sh::kXd + d]) =
               make_float2(o[nt][0], o[nt][1]);
         if (r2 < u.gcount)
-          *reinterpret_cast<float2 *>(&xo[(cw * kTcRows + r2) * Sh::kXd + d]) =
+          *reinterpret_cast<float2 *>(&xo[(cw * xr + r2) * Sh::kXd + d]) =
               make_float2(o[nt][2], o[nt][3]);
       }
       if (!sync()) return;
-      if (!unit_epilogue(a, u, NW, xm, xl, xo, Sh::kXd, tid, NW * 32, flag, sync)) return;
+      if (!unit_epilogue(a, u, NW, xr, xm, xl, xo, Sh::kXd, tid, NW * 32, flag, sync)) return;
+      // every consumer warp has read the unit's query rows and passed the last
+      // barrier of the epilogue: the producer may refill the query slot
+      if (tid == 0) mbar_arrive(&qempty[md.qslot]);
       m1 = m2 = -INFINITY;
       l1 = l2 = 0.f;
 #pragma unroll
@@ -765,17 +939,21 @@ int device_sms() {
   return sms;
 }
 
+// Largest split the kernels take (the tensor-core producer holds a unit's
+// block-table entries in kBtRegs registers per lane).
+constexpr int32_t kMaxPagesPerSplit = kBtRegs * 32;
+
 int32_t resolve_pps(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t max_blocks,
                     int32_t pps) {
-  if (pps > 0) return pps;
+  if (pps > 0) return pps < kMaxPagesPerSplit ? pps : kMaxPagesPerSplit;
   const int32_t G = Hq / Hkv;
   const int32_t rows = group_rows_for(G, D);
   const int64_t units = (int64_t)B * Hkv * ((G + rows - 1) / rows);
   const int64_t work = units * std::max<int32_t>(max_blocks, 1);
   const int64_t target = (int64_t)device_sms() * 48;  // ~48 work units per SM
   int64_t P = (work + target - 1) / target;
-  P = std::min<int64_t>(std::max<int64_t>(P, 8), 256);
-  return (int32_t)((P + 7) / 8 * 8);
+  P = std::min<int64_t>(std::max<int64_t>(P, 8), kMaxPagesPerSplit);
+  return (int32_t)std::min<int64_t>((P + 7) / 8 * 8, kMaxPagesPerSplit);
 }
 
 bool tc_eligible(const void *k_cache, int32_t Hq, int32_t Hkv, int32_t D, int32_t bs,
@@ -869,16 +1047,19 @@ int launch_generic_d(const DecodeArgs &a, cudaStream_t st, int64_t max_units) {
   return launch_generic_g<KT, 8>(a, st, max_units);
 }
 
-// Tensor-core kernel configuration: consumer warps and ring depth per warp.
-constexpr int kTcWarps = 4;
-constexpr int kTcStages = 4;
+// Tensor-core kernel configuration: 8 consumer warps (two per SM sub-partition,
+// so one warp's MMA / shuffle latency hides behind the other's work) and a
+// per-warp ring of S pages: 8 x 2 x 8 KB = 128 KB of K/V in flight per SM for
+// head_dim 128, 8 x 4 x 4 KB for head_dim 64.
+constexpr int kTcWarps = 8;
 
 template <typename T, int D>
 int launch_tc_t(const DecodeArgs &a, const CUtensorMap &mk, const CUtensorMap &mv, cudaStream_t st,
                 int64_t max_units) {
-  using L = TcSmem<D, kTcWarps, kTcStages>;
-  const size_t smem = L::bytes(a.P);
-  auto kern = decode_tc_kernel<T, D, kTcWarps, kTcStages>;
+  constexpr int S = D == 128 ? 2 : 4;
+  using L = TcSmem<D, kTcWarps, S>;
+  const size_t smem = L::bytes(a.GR, a.P);
+  auto kern = decode_tc_kernel<T, D, kTcWarps, S>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return check_launch("cudaFuncSetAttribute(tc)");
@@ -959,7 +1140,7 @@ extern "C" int pkv_decode_plan(const int32_t *context_lens, int32_t batch, int32
   plan_kernel<<<1, kPlanThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       context_lens, batch, block_size, max_blocks, P, w.units_per_item,
       reinterpret_cast<int32_t *>(ws + w.hdr), reinterpret_cast<int32_t *>(ws + w.seq_off),
-      reinterpret_cast<int32_t *>(ws + w.seq_nsplit), reinterpret_cast<int2 *>(ws + w.items),
+      reinterpret_cast<int32_t *>(ws + w.seq_nsplit), reinterpret_cast<int4 *>(ws + w.items),
       reinterpret_cast<int32_t *>(ws + w.counters), status);
   return check_launch("plan_kernel");
 }
@@ -1012,6 +1193,7 @@ extern "C" int pkv_decode_run(const void *q, const void *k_cache, const void *v_
   a.q_dtype = q_dtype;
   a.kv_dtype = kv_dtype;
   a.q0 = q_strides[0]; a.q1 = q_strides[1]; a.q2 = q_strides[2];
+  a.q_vec = (a.q2 == 1 && a.q0 % 8 == 0 && a.q1 % 8 == 0 && aligned_to(q, 16)) ? 1 : 0;
   a.c0 = cache_strides[0]; a.c1 = cache_strides[1]; a.c2 = cache_strides[2]; a.c3 = cache_strides[3];
   a.bt0 = bt_strides[0]; a.bt1 = bt_strides[1];
   a.o0 = out_strides[0]; a.o1 = out_strides[1]; a.o2 = out_strides[2];
@@ -1020,7 +1202,8 @@ extern "C" int pkv_decode_run(const void *q, const void *k_cache, const void *v_
   a.hdr = reinterpret_cast<const int32_t *>(ws + w.hdr);
   a.seq_off = reinterpret_cast<const int32_t *>(ws + w.seq_off);
   a.seq_nsplit = reinterpret_cast<const int32_t *>(ws + w.seq_nsplit);
-  a.items = reinterpret_cast<const int2 *>(ws + w.items);
+  a.items = reinterpret_cast<const int4 *>(ws + w.items);
+  a.sched = reinterpret_cast<int32_t *>(ws + w.hdr) + 4;
   a.counters = reinterpret_cast<int32_t *>(ws + w.counters);
   a.partials = reinterpret_cast<float *>(ws + w.partials);
   a.status = status;
