@@ -337,7 +337,8 @@ def run_ours(args, rank, world, local):
     peak, peak_kind = measured_peaks()
     dec_bytes = wl.decode_bytes_layer()
     achieved = dec_bytes / (decode_avg_ms / 1e3) / 1e9
-    launches = args.steps * (1 + 2 * L)
+    merges = 1 if wl.max_blocks > plan_pps(wl, args) else 0  # split-K merge launch per layer
+    launches = args.steps * (1 + (2 + merges) * L)
 
     # ---- end-to-end through the public ops with pinned host buffers
     e2e = None

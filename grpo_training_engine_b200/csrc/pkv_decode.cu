@@ -12,14 +12,15 @@
 //
 // Work decomposition (shared by both kernels):
 //   plan kernel   : per sequence, n_b = ceil(pages_b / P) chunks of P pages
-//                   ("splits"); a flat item list (b, split) is written into the
-//                   caller's workspace together with per-sequence offsets and
-//                   zeroed arrival counters.
-//   decode kernel : persistent CTAs stride over work units
-//                   (item, kv head, head group). A unit whose sequence has one
-//                   split writes the final output; otherwise it writes a
-//                   partial (max, sum, acc) and the last unit of the sequence
-//                   to arrive (atomic counter) merges all partials.
+//                   ("splits"); a flat list of item descriptors
+//                   (b, split, length, n_b) is written into the caller's
+//                   workspace together with per-sequence offsets.
+//   decode kernel : persistent CTAs take work units (item, kv head, head
+//                   group). A unit whose sequence has one split writes the
+//                   final output; otherwise it writes a partial
+//                   (max, sum, unnormalised acc).
+//   merge kernel  : one CTA per (sequence, head group) combines the partials
+//                   of multi-split sequences, in split order.
 //
 // Two decode kernels:
 //   decode_tc_kernel      bf16/fp16 cache, block_size 16, head_dim 64/128.
@@ -51,7 +52,7 @@ constexpr int kGenWarps = kGenThreads / 32;
 // workspace layout
 // ---------------------------------------------------------------------------
 struct WsLayout {
-  size_t hdr, seq_off, seq_nsplit, items, counters, partials, total;
+  size_t hdr, seq_off, seq_nsplit, items, partials, total;
   int64_t max_items;
   int32_t units_per_item;  // num_kv_heads * head_groups
   int32_t group_rows;      // query heads per head group (partial row count)
@@ -81,7 +82,6 @@ WsLayout ws_layout(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t max_bl
   w.seq_off = off; off = align_up(off + sizeof(int32_t) * (size_t)B, 256);
   w.seq_nsplit = off; off = align_up(off + sizeof(int32_t) * (size_t)B, 256);
   w.items = off; off = align_up(off + sizeof(int4) * (size_t)w.max_items, 256);
-  w.counters = off; off = align_up(off + sizeof(int32_t) * (size_t)B * w.units_per_item, 256);
   w.partials = off;
   off = align_up(off + sizeof(float) * (size_t)w.max_items * w.units_per_item * w.part_floats, 256);
   w.total = off;
@@ -110,17 +110,10 @@ struct DecodeArgs {
   const int32_t *seq_off;
   const int32_t *seq_nsplit;
   const int4 *items;  // per item {b, split, clamped ctx, splits of b}
-  int32_t *counters;
   float *partials;
   int32_t *status;
   int32_t *sched;  // {next unit, finished CTAs}: dynamic scheduling of the tensor-core kernel
 };
-
-__device__ __forceinline__ int32_t clamp_ctx(const DecodeArgs &a, int32_t b) {
-  int32_t c = a.ctx[b];
-  const int32_t cap = a.max_blocks * a.bs;
-  return c < 0 ? 0 : (c > cap ? cap : c);
-}
 
 struct Unit {
   int32_t b, s, kvh, hg, nsplit, ctx, p_begin, p_end, gcount, qh0;
@@ -152,19 +145,17 @@ __device__ __forceinline__ Unit decode_unit(const DecodeArgs &a, int32_t w) {
 }
 
 // ---------------------------------------------------------------------------
-// plan: per-sequence split counts, prefix offsets, item list, zeroed counters
+// plan: per-sequence split counts, prefix offsets, item descriptors
 // ---------------------------------------------------------------------------
 constexpr int kPlanThreads = 1024;
 
 __global__ void __launch_bounds__(kPlanThreads)
 plan_kernel(const int32_t *__restrict__ ctx, int32_t B, int32_t bs, int32_t max_blocks, int32_t P,
             int32_t upi, int32_t *hdr, int32_t *seq_off, int32_t *seq_nsplit, int4 *items,
-            int32_t *counters, int32_t *status) {
+            int32_t *status) {
   __shared__ int32_t warp_tot[kPlanThreads / 32];
   __shared__ int32_t carry;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t ncount = (int64_t)B * upi;
-  for (int64_t i = tid; i < ncount; i += kPlanThreads) counters[i] = 0;
   if (tid == 0) carry = 0;
   __syncthreads();
   const int32_t cap = max_blocks * bs;
@@ -227,8 +218,8 @@ plan_kernel(const int32_t *__restrict__ ctx, int32_t B, int32_t bs, int32_t max_
 // ---------------------------------------------------------------------------
 template <typename Sync>
 __device__ bool unit_epilogue(const DecodeArgs &a, const Unit &u, int nwarps, int xr,
-                              const float *xm, const float *xl, const float *xo, int xd, int tid,
-                              int nthreads, int32_t *flag_smem, Sync &sync) {
+                              const float *xm, const float *xl, const float *const *xo, int xd,
+                              int tid, int nthreads, Sync &sync) {
   const int32_t D = a.D;
   const int32_t GR = a.GR;
   const int32_t n = u.gcount * D;
@@ -243,12 +234,12 @@ __device__ bool unit_epilogue(const DecodeArgs &a, const Unit &u, int nwarps, in
       for (int w = 0; w < nwarps; ++w) {
         const float f = exp2_or_zero(xm[w * xr + g] - M);
         L += f * xl[w * xr + g];
-        O += f * xo[(w * xr + g) * xd + d];
+        O += f * xo[w][g * xd + d];
       }
     }
     if (u.nsplit == 1) {
       a.out[u.b * a.o0 + (int64_t)(u.qh0 + g) * a.o1 + d * a.o2] = O / fmaxf(L, 1e-6f);
-    } else {
+    } else {  // merged by merge_kernel after the launch
       part[2 * GR + g * D + d] = O;
       if (d == 0) {
         part[g] = M;
@@ -256,40 +247,42 @@ __device__ bool unit_epilogue(const DecodeArgs &a, const Unit &u, int nwarps, in
       }
     }
   }
-  if (u.nsplit == 1) return sync();
-  __threadfence();
-  if (!sync()) return false;
-  if (tid == 0) {
-    int32_t *cnt = &a.counters[((int64_t)u.b * a.Hkv + u.kvh) * a.HG + u.hg];
-    const int old = atomicAdd(cnt, 1);
-    const bool last = (old == u.nsplit - 1);
-    // Every split of this (sequence, head group) has arrived: reset the counter so
-    // the same plan can drive the next launch (one plan serves all layers of a step).
-    if (last) atomicExch(cnt, 0);
-    *flag_smem = last;
-  }
-  if (!sync()) return false;
-  if (*flag_smem) {
-    __threadfence();
-    const int64_t base = (int64_t)a.seq_off[u.b] * a.upi + u.kvh * a.HG + u.hg;
-    for (int32_t i = tid; i < n; i += nthreads) {
-      const int32_t g = i / D, d = i - g * D;
-      float M = -INFINITY;
-      for (int32_t s = 0; s < u.nsplit; ++s)
-        M = fmaxf(M, __ldcg(a.partials + (base + (int64_t)s * a.upi) * a.part_floats + g));
-      float L = 0.f, O = 0.f;
-      if (M != -INFINITY) {
-        for (int32_t s = 0; s < u.nsplit; ++s) {
-          const float *p = a.partials + (base + (int64_t)s * a.upi) * a.part_floats;
-          const float f = exp2_or_zero(__ldcg(p + g) - M);
-          L += f * __ldcg(p + GR + g);
-          O += f * __ldcg(p + 2 * GR + g * D + d);
-        }
-      }
-      a.out[u.b * a.o0 + (int64_t)(u.qh0 + g) * a.o1 + d * a.o2] = O / fmaxf(L, 1e-6f);
-    }
-  }
   return sync();
+}
+
+// ---------------------------------------------------------------------------
+// split-K merge: one CTA per (sequence, kv head x head group); sequences with a
+// single split were finished by the decode kernel and return at once.
+// ---------------------------------------------------------------------------
+constexpr int kMergeThreads = 128;
+
+__global__ void __launch_bounds__(kMergeThreads) merge_kernel(DecodeArgs a) {
+  const int32_t b = blockIdx.x;
+  const int32_t r = blockIdx.y;
+  const int32_t n = a.seq_nsplit[b];
+  if (n <= 1) return;
+  const int32_t kvh = r / a.HG, hg = r - kvh * a.HG;
+  const int32_t gcount = min(a.GR, a.G - hg * a.GR);
+  const int32_t qh0 = kvh * a.G + hg * a.GR;
+  const int32_t D = a.D, GR = a.GR;
+  const float *base = a.partials + ((int64_t)a.seq_off[b] * a.upi + r) * a.part_floats;
+  const int64_t stride = (int64_t)a.upi * a.part_floats;  // next split of the same head group
+  for (int32_t i = threadIdx.x; i < gcount * D; i += kMergeThreads) {
+    const int32_t g = i / D, d = i - g * D;
+    float M = -INFINITY;
+    for (int32_t s = 0; s < n; ++s) M = fmaxf(M, base[s * stride + g]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll 4
+      for (int32_t s = 0; s < n; ++s) {
+        const float *p = base + s * stride;
+        const float f = exp2_or_zero(p[g] - M);
+        L += f * p[GR + g];
+        O += f * p[2 * GR + g * D + d];
+      }
+    }
+    a.out[b * a.o0 + (int64_t)(qh0 + g) * a.o1 + d * a.o2] = O / fmaxf(L, 1e-6f);
+  }
 }
 
 struct CtaSync {
@@ -327,7 +320,6 @@ decode_generic_kernel(DecodeArgs a) {
   float *xm = q_s + GM * DP;                 // [NW][16]
   float *xl = xm + kGenWarps * kTcRows;      // [NW][16]
   float *xo = xl + kGenWarps * kTcRows;      // [NW][16][DP]
-  int32_t *flag = reinterpret_cast<int32_t *>(xo + kGenWarps * kTcRows * DP);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const KT *kc = reinterpret_cast<const KT *>(a.kc);
@@ -405,7 +397,10 @@ decode_generic_kernel(DecodeArgs a) {
       }
     }
     __syncthreads();
-    unit_epilogue(a, u, kGenWarps, kTcRows, xm, xl, xo, DP, tid, kGenThreads, flag, sync);
+    const float *xo_w[kGenWarps];
+#pragma unroll
+    for (int w = 0; w < kGenWarps; ++w) xo_w[w] = xo + w * kTcRows * DP;
+    unit_epilogue(a, u, kGenWarps, kTcRows, xm, xl, xo_w, DP, tid, kGenThreads, sync);
   }
 }
 
@@ -444,7 +439,6 @@ template <int D> struct TcShape {
   static constexpr int kSlot = 2 * kTile;           // K + V
   static constexpr int kKSteps = D / 16;
   static constexpr int kNTiles = D / 8;
-  static constexpr int kXd = D + 4;           // padded exchange row (floats)
   static constexpr int kQRow = D * 2 + 16;    // padded query row (bytes): conflict-free ldmatrix
   static constexpr int kQSlot = kTcRows * kQRow;
 };
@@ -458,15 +452,11 @@ struct TcSmem {
   static constexpr size_t kEmpty = kFull + 8 * NW * S;
   static constexpr size_t kQEmpty = kEmpty + 8 * NW * S;
   static constexpr size_t kGroup = kQEmpty + 8 * kQSlots;
-  static constexpr size_t kFlag = kGroup + 8;
-  static constexpr size_t kXm = align_up(kFlag + 8, 16);
+  static constexpr size_t kXSlot = kGroup + 8;  // [NW] slot holding each warp's exchange rows
+  static constexpr size_t kXm = align_up(kXSlot + 4 * NW, 16);
   static constexpr size_t kXl = kXm + sizeof(float) * NW * kTcRows;
-  static constexpr size_t kXo = kXl + sizeof(float) * NW * kTcRows;
-  // exchange rows for `rows` query heads per warp, then the producer's block-table buffer
-  __host__ __device__ static size_t bt_offset(int rows) {
-    return align_up(kXo + sizeof(float) * (size_t)NW * rows * TcShape<D>::kXd, 16);
-  }
-  static size_t bytes(int rows, int32_t P) { return bt_offset(rows) + sizeof(int32_t) * (size_t)P + 1024; }
+  static constexpr size_t kBt = kXl + sizeof(float) * NW * kTcRows;
+  static size_t bytes(int32_t P) { return kBt + sizeof(int32_t) * (size_t)P + 1024; }
 };
 
 // Packs (x, y) into a 16-bit pair `hi` and the rounding remainders into `lo`.
@@ -496,11 +486,10 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
   uint64_t *empty = reinterpret_cast<uint64_t *>(smem + L::kEmpty);
   uint64_t *qempty = reinterpret_cast<uint64_t *>(smem + L::kQEmpty);
   uint64_t *group = reinterpret_cast<uint64_t *>(smem + L::kGroup);
-  int32_t *flag = reinterpret_cast<int32_t *>(smem + L::kFlag);
+  int32_t *xslot = reinterpret_cast<int32_t *>(smem + L::kXSlot);
   float *xm = reinterpret_cast<float *>(smem + L::kXm);
   float *xl = reinterpret_cast<float *>(smem + L::kXl);
-  float *xo = reinterpret_cast<float *>(smem + L::kXo);
-  int32_t *btbuf = reinterpret_cast<int32_t *>(smem + L::bt_offset(a.GR));
+  int32_t *btbuf = reinterpret_cast<int32_t *>(smem + L::kBt);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid == 0) {
@@ -836,9 +825,11 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
-
-    if (md.last) {
+    // A unit's last element keeps its slot until the unit epilogue is done: the
+    // slot's 8 KB (4 KB for head_dim 64) holds this warp's exchange rows.
+    if (!md.last) {
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    } else {
       // ---- this warp is done with the unit: publish its state, then combine
       Unit u;
       u.b = md.b;
@@ -849,6 +840,10 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
       u.gcount = md.gcount;
       u.qh0 = md.qh0;
       const int xr = a.GR;
+      // padded rows when they fit in the slot (fewer bank conflicts), else dense
+      const int xd = (a.GR * (D + 4) * 4 <= Sh::kSlot) ? D + 4 : D;
+      float *xo = reinterpret_cast<float *>(tiles + (size_t)slot * Sh::kSlot);
+      if (lane == 0) xslot[cw] = slot;
       float s1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
       s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
       float s2 = l2 + __shfl_xor_sync(0xffffffffu, l2, 1);
@@ -867,16 +862,19 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
       for (int nt = 0; nt < Sh::kNTiles; ++nt) {
         const int d = nt * 8 + cq;
         if (r1 < u.gcount)
-          *reinterpret_cast<float2 *>(&xo[(cw * xr + r1) * Sh::kXd + d]) =
-              make_float2(o[nt][0], o[nt][1]);
+          *reinterpret_cast<float2 *>(&xo[r1 * xd + d]) = make_float2(o[nt][0], o[nt][1]);
         if (r2 < u.gcount)
-          *reinterpret_cast<float2 *>(&xo[(cw * xr + r2) * Sh::kXd + d]) =
-              make_float2(o[nt][2], o[nt][3]);
+          *reinterpret_cast<float2 *>(&xo[r2 * xd + d]) = make_float2(o[nt][2], o[nt][3]);
       }
       if (!sync()) return;
-      if (!unit_epilogue(a, u, NW, xr, xm, xl, xo, Sh::kXd, tid, NW * 32, flag, sync)) return;
-      // every consumer warp has read the unit's query rows and passed the last
-      // barrier of the epilogue: the producer may refill the query slot
+      const float *xo_w[NW];
+#pragma unroll
+      for (int w = 0; w < NW; ++w)
+        xo_w[w] = reinterpret_cast<const float *>(tiles + (size_t)xslot[w] * Sh::kSlot);
+      if (!unit_epilogue(a, u, NW, xr, xm, xl, xo_w, xd, tid, NW * 32, sync)) return;
+      // every consumer warp has read the unit's query rows and all exchange
+      // rows: release the held slot and the query slot
+      if (lane == 0) mbar_arrive(&empty[slot]);
       if (tid == 0) mbar_arrive(&qempty[md.qslot]);
       m1 = m2 = -INFINITY;
       l1 = l2 = 0.f;
@@ -1049,16 +1047,16 @@ int launch_generic_d(const DecodeArgs &a, cudaStream_t st, int64_t max_units) {
 
 // Tensor-core kernel configuration: 8 consumer warps (two per SM sub-partition,
 // so one warp's MMA / shuffle latency hides behind the other's work) and a
-// per-warp ring of S pages: 8 x 2 x 8 KB = 128 KB of K/V in flight per SM for
-// head_dim 128, 8 x 4 x 4 KB for head_dim 64.
+// per-warp ring of S pages: 8 x 3 x 8 KB = 192 KB of K/V staging per SM for
+// head_dim 128, 8 x 6 x 4 KB for head_dim 64.
 constexpr int kTcWarps = 8;
 
 template <typename T, int D>
 int launch_tc_t(const DecodeArgs &a, const CUtensorMap &mk, const CUtensorMap &mv, cudaStream_t st,
                 int64_t max_units) {
-  constexpr int S = D == 128 ? 2 : 4;
+  constexpr int S = D == 128 ? 3 : 6;
   using L = TcSmem<D, kTcWarps, S>;
-  const size_t smem = L::bytes(a.GR, a.P);
+  const size_t smem = L::bytes(a.P);
   auto kern = decode_tc_kernel<T, D, kTcWarps, S>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
@@ -1141,7 +1139,7 @@ extern "C" int pkv_decode_plan(const int32_t *context_lens, int32_t batch, int32
       context_lens, batch, block_size, max_blocks, P, w.units_per_item,
       reinterpret_cast<int32_t *>(ws + w.hdr), reinterpret_cast<int32_t *>(ws + w.seq_off),
       reinterpret_cast<int32_t *>(ws + w.seq_nsplit), reinterpret_cast<int4 *>(ws + w.items),
-      reinterpret_cast<int32_t *>(ws + w.counters), status);
+      status);
   return check_launch("plan_kernel");
 }
 
@@ -1204,7 +1202,6 @@ extern "C" int pkv_decode_run(const void *q, const void *k_cache, const void *v_
   a.seq_nsplit = reinterpret_cast<const int32_t *>(ws + w.seq_nsplit);
   a.items = reinterpret_cast<const int4 *>(ws + w.items);
   a.sched = reinterpret_cast<int32_t *>(ws + w.hdr) + 4;
-  a.counters = reinterpret_cast<int32_t *>(ws + w.counters);
   a.partials = reinterpret_cast<float *>(ws + w.partials);
   a.status = status;
   const int64_t max_units = w.max_items * w.units_per_item;
@@ -1221,16 +1218,29 @@ extern "C" int pkv_decode_run(const void *q, const void *k_cache, const void *v_
                                cache_strides)))
       return rc;
     if (kv_dtype == PKV_DTYPE_BF16)
-      return head_dim == 128 ? launch_tc_t<__nv_bfloat16, 128>(a, mk, mv, st, max_units)
-                             : launch_tc_t<__nv_bfloat16, 64>(a, mk, mv, st, max_units);
-    return head_dim == 128 ? launch_tc_t<__half, 128>(a, mk, mv, st, max_units)
+      rc = head_dim == 128 ? launch_tc_t<__nv_bfloat16, 128>(a, mk, mv, st, max_units)
+                           : launch_tc_t<__nv_bfloat16, 64>(a, mk, mv, st, max_units);
+    else
+      rc = head_dim == 128 ? launch_tc_t<__half, 128>(a, mk, mv, st, max_units)
                            : launch_tc_t<__half, 64>(a, mk, mv, st, max_units);
+  } else {
+    switch (kv_dtype) {
+      case PKV_DTYPE_BF16: rc = launch_generic_d<__nv_bfloat16>(a, st, max_units); break;
+      case PKV_DTYPE_F16: rc = launch_generic_d<__half>(a, st, max_units); break;
+      default: rc = launch_generic_d<float>(a, st, max_units); break;
+    }
   }
-  switch (kv_dtype) {
-    case PKV_DTYPE_BF16: return launch_generic_d<__nv_bfloat16>(a, st, max_units);
-    case PKV_DTYPE_F16: return launch_generic_d<__half>(a, st, max_units);
-    default: return launch_generic_d<float>(a, st, max_units);
+  if (rc) return rc;
+  // sequences longer than one split left partials: merge them (stream-ordered)
+  if (max_blocks > P) {
+    if (w.units_per_item > 65535) {
+      set_error_detail("num_kv_heads x head groups = %d exceeds the merge grid", w.units_per_item);
+      return PKV_ERR_UNSUPPORTED;
+    }
+    merge_kernel<<<dim3((unsigned)batch, (unsigned)w.units_per_item), kMergeThreads, 0, st>>>(a);
+    rc = check_launch("merge_kernel");
   }
+  return rc;
 }
 
 extern "C" int pkv_decode(const void *q, const void *k_cache, const void *v_cache,
