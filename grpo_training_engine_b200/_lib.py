@@ -32,6 +32,7 @@ DEV_PAGE_OUT_OF_RANGE = 2
 DEV_WAIT_TIMEOUT = 4
 
 DECODE_FORCE_GENERIC = 1
+NOALLOC_SCRATCH_BYTES = 32 << 20  # PKV_NOALLOC_SCRATCH_BYTES in include/pkv.h
 
 _i32 = C.c_int32
 _i64p = C.POINTER(C.c_int64)
@@ -69,6 +70,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
          _i64p, _i64p, _i64p, _i64p, _i32, _i32, C.c_float, _i32, _i32, _vp, _sz, _vp, _vp],
     ),
+    "pkv_decode_noalloc": (
+        C.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
+         _i64p, _i64p, _i64p, _i64p, _i32, _i32, C.c_float, _i32, _i32, _vp, _vp],
+    ),
     "pkv_decode_kernel_kind": (C.c_int, [_vp, _i32, _i32, _i32, _i32, _i64p, _i32, _i32, _i32]),
 }
 
@@ -93,7 +99,7 @@ def load() -> C.CDLL:
     path = Path(os.environ.get("PKV_LIBRARY", str(LIB_PATH)))
     if not path.exists():
         raise ImportError(
-            f"{path} is missing: build it with `python -m grpo_training_engine_b200.build` "
+            f"{path} is missing: build it with `python grpo_training_engine_b200/build.py` "
             "(the paged-KV path has no non-CUDA implementation)"
         )
     try:
@@ -101,7 +107,11 @@ def load() -> C.CDLL:
     except OSError as exc:  # pragma: no cover - depends on the environment
         raise ImportError(f"cannot load {path}: {exc}") from exc
     for name, (res, args) in SIGNATURES.items():
-        fn = getattr(lib, name)
+        try:
+            fn = getattr(lib, name)
+        except AttributeError as exc:
+            raise ImportError(f"{path} is stale (no {name}): rebuild it with "
+                              "`python grpo_training_engine_b200/build.py`") from exc
         fn.restype = res
         fn.argtypes = args
     _LIB = lib

@@ -4,7 +4,7 @@ The library is compiled with nvcc straight to sm_100a machine code, links the
 CUDA runtime statically and exports only the ``pkv_*`` C entry points (a
 linker version script hides everything else, so the runtime inside the
 library never interposes on the one PyTorch loads). Run as
-``python -m grpo_training_engine_b200.build`` or through
+``python grpo_training_engine_b200/build.py`` or through
 ``__graft_entry__.build()``.
 """
 
@@ -22,7 +22,7 @@ CSRC = PKG_DIR / "csrc"
 INCLUDE = REPO_DIR / "include"
 LIB_PATH = PKG_DIR / "libpkv.so"
 
-SOURCES = ["pkv_copy.cu", "pkv_decode.cu"]
+SOURCES = ["pkv_copy.cu", "pkv_decode.cu", "pkv_noalloc.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -197,6 +197,36 @@ int pkv_decode(const void *q, const void *k_cache, const void *v_cache,
                size_t workspace_bytes, int32_t *status, void *stream);
 
 /*
+ * pkv_decode_noalloc — pkv_decode without a caller workspace. No counterpart
+ * in the reference: it exists for callers that cannot allocate device memory
+ * themselves (an FFI host that only passes in the tensors it owns, or a
+ * process whose GPU memory is held by another framework's allocator, where a
+ * direct cudaMalloc fails or fragments that allocator's pool).
+ *
+ * The split plan and split-K partials live in a static device array of
+ * PKV_NOALLOC_SCRATCH_BYTES inside the library; every GPU that loads the
+ * library's device code keeps that much memory for it until the process
+ * exits. Decodes whose workspace (pkv_decode_workspace_size) exceeds it are
+ * rejected with PKV_ERR_WORKSPACE. The first call on a device looks up the
+ * array's device address (once per device, with that device current); make
+ * that first call before any stream capture. All calls share the array:
+ * calls that run concurrently on the GPU race on it and must be serialised by
+ * the caller. Arguments and results are those of pkv_decode.
+ */
+#define PKV_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+int pkv_decode_noalloc(const void *q, const void *k_cache, const void *v_cache,
+                       const int32_t *block_tables, const int32_t *context_lens,
+                       float *out, int32_t batch, int32_t num_q_heads,
+                       int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                       int32_t num_blocks, int32_t max_blocks,
+                       const int64_t *q_strides, const int64_t *cache_strides,
+                       const int64_t *bt_strides, const int64_t *out_strides,
+                       int32_t q_dtype, int32_t kv_dtype, float scale,
+                       int32_t pages_per_split, int32_t flags, int32_t *status,
+                       void *stream);
+
+/*
  * Which decode kernel pkv_decode_run would launch for these arguments:
  * 1 = TMA + tensor-core kernel, 0 = CUDA-core kernel, <0 = error code.
  */
