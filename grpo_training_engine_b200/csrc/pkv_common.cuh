@@ -1,7 +1,6 @@
 // pkv_common.cuh — shared device helpers for the paged-KV kernels (sm_100a).
 //
-// Element conversion, bounded mbarrier waits, the bulk tensor (TMA) load,
-// ldmatrix / mma.sync wrappers and the host-side error plumbing used by every
+// Element conversion, bounded mbarrier waits, ldmatrix / mma.sync wrappers and the host-side error plumbing used by every
 // entry point of libpkv.so.
 #pragma once
 
@@ -71,7 +70,7 @@ __device__ __forceinline__ void flag_status(int32_t *status, int bits) {
 }
 
 // ---------------------------------------------------------------------------
-// shared-memory addresses, mbarriers, bulk tensor loads (PTX ISA 8.x)
+// shared-memory addresses and mbarriers (PTX ISA 8.x)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -82,23 +81,13 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
                : "memory");
 }
 
-// Make mbarrier initialisation visible to the async (TMA) proxy.
+// Make mbarrier initialisation visible before other threads use the barriers.
 __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
@@ -123,23 +112,6 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     if (mbar_try_wait(bar, parity)) return true;
   }
   return false;
-}
-
-// 4-D tiled bulk tensor load global -> shared, completion signalled on `bar`.
-// No multicast: the source is always this GPU's own memory.
-__device__ __forceinline__ void tma_load_4d(void *dst_smem, const void *tmap, uint64_t *bar,
-                                            int32_t c0, int32_t c1, int32_t c2, int32_t c3) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst_smem)),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
-      "r"(smem_u32(bar))
-      : "memory");
-}
-
-// Named barrier over `nthreads` threads (multiple of 32); id 0 is __syncthreads.
-__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // ---------------------------------------------------------------------------

@@ -24,19 +24,18 @@
 //
 // Two decode kernels:
 //   decode_tc_kernel      bf16/fp16 cache, block_size 16, head_dim 64/128.
-//                         One producer warp streams K and V pages with bulk
-//                         tensor copies (TMA, 128-byte swizzle) into
-//                         per-consumer-warp smem rings guarded by mbarriers;
-//                         consumer warps compute q.K^T and P.V with
+//                         A producer warp schedules units and publishes, per
+//                         consumer warp, the pages to read (plus staged
+//                         query rows); each of 8 consumer warps streams its
+//                         own K and V pages into a 3-deep smem ring with
+//                         16-byte cp.async (one commit group per page, issued
+//                         two pages ahead) and computes q.K^T and P.V with
 //                         m16n8k16 tensor-core MMAs (query heads on M).
 //   decode_generic_kernel any dtype (fp32/bf16/fp16), any block size,
 //                         head_dim <= 256: CUDA-core FMAs, plain coalesced
 //                         loads, per-warp online softmax.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
 #include <algorithm>
-#include <mutex>
+#include <climits>
 
 #include "pkv_common.cuh"
 
@@ -96,7 +95,7 @@ struct DecodeArgs {
   const int32_t *bt;
   const int32_t *ctx;
   float *out;
-  const void *kc;  // generic kernel only (the tensor-core kernel reads through TMA)
+  const void *kc;
   const void *vc;
   int32_t B, Hq, Hkv, G, GR, HG, D, bs, num_blocks, max_blocks, P, upi, part_floats;
   int32_t q_dtype, kv_dtype;
@@ -411,7 +410,7 @@ size_t generic_smem_bytes(int DJ, int GM) {
 }
 
 // ---------------------------------------------------------------------------
-// TMA + tensor-core kernel (bf16 / fp16 cache, block_size 16, head_dim 64/128)
+// cp.async + tensor-core kernel (bf16 / fp16 cache, block_size 16, head_dim 64/128)
 // ---------------------------------------------------------------------------
 enum : int32_t { kElemPage = 0, kElemEmpty = 1, kElemStop = 2 };
 
@@ -426,12 +425,12 @@ struct __align__(16) SlotMeta {
   int32_t qslot;   // smem slot holding the unit's query rows
   int32_t b, s, nsplit;
   int32_t kvh, hg, gcount, qh0;
-  int32_t pad[4];
+  int32_t page;    // physical page id (kElemPage only)
+  int32_t pad[3];
 };
 
 constexpr int kBoxRows = 16;               // tokens per page (block_size)
 constexpr int kBoxBytes = kBoxRows * 128;  // one [16][64] 16-bit box, 128-byte swizzled rows
-constexpr int kQSlots = 2;                 // query-row slots (units in flight per CTA)
 
 template <int D> struct TcShape {
   static constexpr int kBoxes = D / 64;
@@ -443,21 +442,46 @@ template <int D> struct TcShape {
   static constexpr int kQSlot = kTcRows * kQRow;
 };
 
+// Shared-memory plan of the kernel: per consumer warp a ring of S data slots
+// (one K+V page each, filled by the warp itself with cp.async) and a deeper
+// ring of MD metadata entries (filled by the producer warp); query rows of
+// QS = S + 1 units (the consumers' look-ahead of S - 1 elements can reach S - 1
+// units ahead, so the producer must be able to stage that many more).
 template <int D, int NW, int S>
 struct TcSmem {
+  static constexpr int MD = 2 * S;
+  static constexpr int QS = S + 1;
   static constexpr size_t kTiles = (size_t)NW * S * TcShape<D>::kSlot;
   static constexpr size_t kQ = kTiles;
-  static constexpr size_t kMeta = kQ + (size_t)kQSlots * TcShape<D>::kQSlot;
-  static constexpr size_t kFull = align_up(kMeta + sizeof(SlotMeta) * NW * S, 16);
-  static constexpr size_t kEmpty = kFull + 8 * NW * S;
-  static constexpr size_t kQEmpty = kEmpty + 8 * NW * S;
-  static constexpr size_t kGroup = kQEmpty + 8 * kQSlots;
+  static constexpr size_t kMeta = kQ + (size_t)QS * TcShape<D>::kQSlot;
+  static constexpr size_t kFull = align_up(kMeta + sizeof(SlotMeta) * NW * MD, 16);
+  static constexpr size_t kEmpty = kFull + 8 * NW * MD;
+  static constexpr size_t kQEmpty = kEmpty + 8 * NW * MD;
+  static constexpr size_t kGroup = kQEmpty + 8 * QS;
   static constexpr size_t kXSlot = kGroup + 8;  // [NW] slot holding each warp's exchange rows
   static constexpr size_t kXm = align_up(kXSlot + 4 * NW, 16);
   static constexpr size_t kXl = kXm + sizeof(float) * NW * kTcRows;
   static constexpr size_t kBt = kXl + sizeof(float) * NW * kTcRows;
   static size_t bytes(int32_t P) { return kBt + sizeof(int32_t) * (size_t)P + 1024; }
 };
+
+// Byte offset, inside a K or V tile, of 16-byte chunk c of a page slab
+// (16 rows of D contiguous 16-bit values): row r, chunk cc of the row, stored
+// in [D/64 boxes][16 rows][128 bytes] with chunk (cc % 8) ^ (r % 8).
+template <int D>
+__device__ __forceinline__ uint32_t slab_chunk_offset(int c) {
+  constexpr int kRowChunks = D / 8;
+  const int r = c / kRowChunks, cc = c % kRowChunks;
+  return (cc >> 3) * kBoxBytes + r * 128 + (((cc & 7) ^ (r & 7)) << 4);
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // Packs (x, y) into a 16-bit pair `hi` and the rounding remainders into `lo`.
 template <typename M>
@@ -472,8 +496,7 @@ constexpr int kBtRegs = 8;  // supports up to 256 pages per unit
 
 template <typename T, int D, int NW, int S>
 __global__ void __launch_bounds__((NW + 1) * 32, 1)
-decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-                 DecodeArgs a) {
+decode_tc_kernel(DecodeArgs a) {
   using Sh = TcShape<D>;
   using L = TcSmem<D, NW, S>;
   extern __shared__ uint8_t tc_raw[];
@@ -492,12 +515,13 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
   int32_t *btbuf = reinterpret_cast<int32_t *>(smem + L::kBt);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int MD = L::MD, QS = L::QS;
   if (tid == 0) {
-    for (int i = 0; i < NW * S; ++i) {
+    for (int i = 0; i < NW * MD; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    for (int i = 0; i < kQSlots; ++i) mbar_init(&qempty[i], 1);
+    for (int i = 0; i < QS; ++i) mbar_init(&qempty[i], 1);
     mbar_init(group, NW);
     fence_mbar_init();
   }
@@ -565,14 +589,14 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
 #pragma unroll
     for (int i = 0; i < NW; ++i) kcount[i] = 0;
     bool ok = true;
-    int32_t nunit = 0;  // units issued by this CTA (query slot = nunit % kQSlots)
+    int32_t nunit = 0;  // units issued by this CTA (query slot = nunit % QS)
     while (w1 < total && ok) {
       const Unit u = unit_from(a, w1, d1);
       const int32_t npages = u.p_end - u.p_begin;
-      const int qs = nunit % kQSlots;
+      const int qs = nunit % QS;
       // (1) the unit's block-table entries and query rows -> smem
-      if (nunit >= kQSlots) {
-        if (!mbar_wait_bounded(&qempty[qs], ((nunit / kQSlots) - 1) & 1)) {
+      if (nunit >= QS) {
+        if (!mbar_wait_bounded(&qempty[qs], ((nunit / QS) - 1) & 1)) {
           flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
           ok = false;
         }
@@ -603,7 +627,8 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
       const int32_t w3 = __shfl_sync(FULL, fetched, 0);
       const int4 d3 = w3 < total ? a.items[w3 / a.upi] : none;
       if (lane == 0 && w3 < total) fetched = atomicAdd(&a.sched[0], 1);
-      // (3) stream the unit's pages to the consumer warps (page p -> warp p % NW)
+      // (3) publish the unit's pages to the consumer warps (page p -> warp p % NW);
+      //     each consumer loads its pages itself with cp.async
       if (lane == 0 && ok) {
         const int32_t rounds = npages > 0 ? (npages + NW - 1) / NW : 1;
         for (int32_t j = 0; j < rounds && ok; ++j) {
@@ -614,8 +639,8 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
             const bool last = (j == rounds - 1);
             if (!has && !last) continue;
             const int32_t k = kcount[cw]++;
-            const int slot = cw * S + (k % S);
-            const int32_t use = k / S;
+            const int slot = cw * MD + (k % MD);
+            const int32_t use = k / MD;
             if (use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) {
               flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
               ok = false;
@@ -635,19 +660,9 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
             md.hg = u.hg;
             md.gcount = u.gcount;
             md.qh0 = u.qh0;
+            md.page = page;
             meta[slot] = md;
-            if (page >= 0) {
-              mbar_arrive_expect_tx(&full[slot], Sh::kSlot);
-              uint8_t *kt = tiles + (size_t)slot * Sh::kSlot;
-#pragma unroll
-              for (int bx = 0; bx < Sh::kBoxes; ++bx) {
-                tma_load_4d(kt + bx * kBoxBytes, &tmk, &full[slot], bx * 64, 0, u.kvh, page);
-                tma_load_4d(kt + Sh::kTile + bx * kBoxBytes, &tmv, &full[slot], bx * 64, 0,
-                            u.kvh, page);
-              }
-            } else {
-              mbar_arrive(&full[slot]);
-            }
+            mbar_arrive(&full[slot]);
           }
         }
       }
@@ -673,8 +688,8 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
 #pragma unroll
       for (int cw = 0; cw < NW; ++cw) {
         const int32_t k = kcount[cw]++;
-        const int slot = cw * S + (k % S);
-        const int32_t use = k / S;
+        const int slot = cw * MD + (k % MD);
+        const int32_t use = k / MD;
         if (use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) {
           flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
           break;
@@ -719,14 +734,58 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
   int32_t cur_work = -1;
   const float sl2 = a.scale_log2;
 
+  // Each consumer warp loads its own pages: element e's K and V slabs go into
+  // data slot e % S with 16-byte cp.async copies (each instruction moves 512
+  // contiguous bytes of one slab, written straight into the swizzled tile
+  // layout), one commit group per element, issued S - 1 elements ahead.
+  const uint8_t *kbase = reinterpret_cast<const uint8_t *>(a.kc);
+  const uint8_t *vbase = reinterpret_cast<const uint8_t *>(a.vc);
+  int32_t stop_at = INT32_MAX;
+  bool alive = true;
+  auto issue = [&](int32_t e) {
+    if (e <= stop_at && alive) {
+      const int ms = cw * MD + (e % MD);
+      if (!mbar_wait_bounded(&full[ms], (e / MD) & 1)) {
+        flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
+        alive = false;
+      } else {
+        const int32_t kind = meta[ms].kind;
+        if (kind == kElemStop) {
+          stop_at = e;
+        } else if (kind == kElemPage) {
+          const int64_t off = ((int64_t)meta[ms].page * a.c0 + (int64_t)meta[ms].kvh * a.c1) * 2;
+          const uint8_t *ks = kbase + off;
+          const uint8_t *vs = vbase + off;
+          const uint32_t dst = smem_u32(tiles + (size_t)(cw * S + (e % S)) * Sh::kSlot);
+#pragma unroll
+          for (int i = 0; i < D / 16; ++i) {
+            const int c = lane + 32 * i;
+            const uint32_t o = slab_chunk_offset<D>(c);
+            cp_async16(dst + o, ks + 16 * c);
+            cp_async16(dst + Sh::kTile + o, vs + 16 * c);
+          }
+        }
+      }
+    }
+    cp_async_commit();  // one group per element, possibly empty
+  };
+#pragma unroll 1
+  for (int32_t e = 0; e < S - 1; ++e) issue(e);
+
   for (int32_t k = 0;; ++k) {
-    const int slot = cw * S + (k % S);
-    if (!mbar_wait_bounded(&full[slot], (k / S) & 1)) {
-      flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
+    issue(k + S - 1);
+    if (!alive) {
+      cp_async_wait_all();
       return;
     }
-    const SlotMeta md = meta[slot];
+    cp_async_wait<S - 1>();  // element k's group (and all older) has landed
+    __syncwarp();
+    const int ms = cw * MD + (k % MD);
+    const SlotMeta md = meta[ms];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[ms]);  // metadata copied: the producer may reuse the entry
     if (md.kind == kElemStop) break;
+    const int slot = cw * S + (k % S);
     if (md.work != cur_work) {
       cur_work = md.work;
       const uint32_t qb = smem_u32(qbuf + md.qslot * Sh::kQSlot) + q_off;
@@ -825,11 +884,10 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
       }
     }
     __syncwarp();
-    // A unit's last element keeps its slot until the unit epilogue is done: the
-    // slot's 8 KB (4 KB for head_dim 64) holds this warp's exchange rows.
-    if (!md.last) {
-      if (lane == 0) mbar_arrive(&empty[slot]);
-    } else {
+    // A unit's last element: its data slot (8 KB, 4 KB for head_dim 64) holds
+    // this warp's exchange rows until the unit epilogue is done; the warp's next
+    // load into that slot is only issued in the next iteration.
+    if (md.last) {
       // ---- this warp is done with the unit: publish its state, then combine
       Unit u;
       u.b = md.b;
@@ -866,15 +924,20 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
         if (r2 < u.gcount)
           *reinterpret_cast<float2 *>(&xo[r2 * xd + d]) = make_float2(o[nt][2], o[nt][3]);
       }
-      if (!sync()) return;
+      if (!sync()) {
+        cp_async_wait_all();
+        return;
+      }
       const float *xo_w[NW];
 #pragma unroll
       for (int w = 0; w < NW; ++w)
         xo_w[w] = reinterpret_cast<const float *>(tiles + (size_t)xslot[w] * Sh::kSlot);
-      if (!unit_epilogue(a, u, NW, xr, xm, xl, xo_w, xd, tid, NW * 32, sync)) return;
+      if (!unit_epilogue(a, u, NW, xr, xm, xl, xo_w, xd, tid, NW * 32, sync)) {
+        cp_async_wait_all();
+        return;
+      }
       // every consumer warp has read the unit's query rows and all exchange
-      // rows: release the held slot and the query slot
-      if (lane == 0) mbar_arrive(&empty[slot]);
+      // rows: the query slot may be refilled
       if (tid == 0) mbar_arrive(&qempty[md.qslot]);
       m1 = m2 = -INFINITY;
       l1 = l2 = 0.f;
@@ -882,51 +945,12 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
       for (int i = 0; i < Sh::kNTiles; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     }
   }
+  cp_async_wait_all();
 }
 
 // ---------------------------------------------------------------------------
 // host helpers
 // ---------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void *p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
-int encode_cache_map(CUtensorMap *m, const void *base, int32_t kv_dtype, int32_t D, int32_t Hkv,
-                     int32_t num_blocks, const int64_t *cs) {
-  auto fn = encode_fn();
-  if (!fn) {
-    set_error_detail("cuTensorMapEncodeTiled entry point unavailable");
-    return PKV_ERR_TENSOR_MAP;
-  }
-  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)kBoxRows, (cuuint64_t)Hkv,
-                              (cuuint64_t)num_blocks};
-  const cuuint64_t strides[3] = {(cuuint64_t)cs[2] * 2, (cuuint64_t)cs[1] * 2,
-                                 (cuuint64_t)cs[0] * 2};
-  const cuuint32_t box[4] = {64, (cuuint32_t)kBoxRows, 1, 1};
-  const cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = fn(m,
-                  kv_dtype == PKV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                  4, const_cast<void *>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    set_error_detail("cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
-    return PKV_ERR_TENSOR_MAP;
-  }
-  return PKV_OK;
-}
-
 int device_sms() {
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
@@ -954,17 +978,19 @@ int32_t resolve_pps(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t max_b
   return (int32_t)std::min<int64_t>((P + 7) / 8 * 8, kMaxPagesPerSplit);
 }
 
-bool tc_eligible(const void *k_cache, int32_t Hq, int32_t Hkv, int32_t D, int32_t bs,
-                 const int64_t *cs, int32_t q_dtype, int32_t kv_dtype, int32_t flags) {
+// The tensor-core kernel copies whole (page, head) slabs of 16 x D 16-bit
+// values with 16-byte cp.async: rows must be contiguous and every slab
+// 16-byte aligned.
+bool tc_eligible(const void *k_cache, const void *v_cache, int32_t Hq, int32_t Hkv, int32_t D,
+                 int32_t bs, const int64_t *cs, int32_t q_dtype, int32_t kv_dtype, int32_t flags) {
   if (flags & PKV_DECODE_FORCE_GENERIC) return false;
   if (kv_dtype != PKV_DTYPE_BF16 && kv_dtype != PKV_DTYPE_F16) return false;
   if (q_dtype != kv_dtype) return false;
   if (bs != kBoxRows || (D != 64 && D != 128)) return false;
   if (Hq % Hkv != 0) return false;
-  if (cs[3] != 1) return false;
-  for (int i = 0; i < 3; ++i)
-    if ((cs[i] * 2) % 16 != 0 || cs[i] <= 0) return false;
-  if (!aligned_to(k_cache, 16)) return false;
+  if (cs[3] != 1 || cs[2] != D) return false;
+  if (cs[0] % 8 != 0 || cs[1] % 8 != 0 || cs[0] <= 0 || cs[1] <= 0) return false;
+  if (!aligned_to(k_cache, 16) || (v_cache != nullptr && !aligned_to(v_cache, 16))) return false;
   return true;
 }
 
@@ -1052,8 +1078,7 @@ int launch_generic_d(const DecodeArgs &a, cudaStream_t st, int64_t max_units) {
 constexpr int kTcWarps = 8;
 
 template <typename T, int D>
-int launch_tc_t(const DecodeArgs &a, const CUtensorMap &mk, const CUtensorMap &mv, cudaStream_t st,
-                int64_t max_units) {
+int launch_tc_t(const DecodeArgs &a, cudaStream_t st, int64_t max_units) {
   constexpr int S = D == 128 ? 3 : 6;
   using L = TcSmem<D, kTcWarps, S>;
   const size_t smem = L::bytes(a.P);
@@ -1069,7 +1094,7 @@ int launch_tc_t(const DecodeArgs &a, const CUtensorMap &mk, const CUtensorMap &m
   int64_t grid = (int64_t)device_sms() * per_sm;
   if (grid > max_units) grid = max_units;
   if (grid < 1) grid = 1;
-  kern<<<(unsigned)grid, (kTcWarps + 1) * 32, smem, st>>>(mk, mv, a);
+  kern<<<(unsigned)grid, (kTcWarps + 1) * 32, smem, st>>>(a);
   return check_launch("decode_tc_kernel");
 }
 
@@ -1103,8 +1128,8 @@ extern "C" int pkv_decode_kernel_kind(const void *k_cache, int32_t num_q_heads,
                                       const int64_t *cache_strides, int32_t q_dtype,
                                       int32_t kv_dtype, int32_t flags) {
   if (!cache_strides || num_kv_heads <= 0) return PKV_ERR_INVALID_ARG;
-  return tc_eligible(k_cache, num_q_heads, num_kv_heads, head_dim, block_size, cache_strides,
-                     q_dtype, kv_dtype, flags)
+  return tc_eligible(k_cache, nullptr, num_q_heads, num_kv_heads, head_dim, block_size,
+                     cache_strides, q_dtype, kv_dtype, flags)
              ? 1
              : 0;
 }
@@ -1207,22 +1232,14 @@ extern "C" int pkv_decode_run(const void *q, const void *k_cache, const void *v_
   const int64_t max_units = w.max_items * w.units_per_item;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 
-  if (tc_eligible(k_cache, num_q_heads, num_kv_heads, head_dim, block_size, cache_strides,
-                  q_dtype, kv_dtype, flags) &&
-      num_blocks > 0 && aligned_to(v_cache, 16)) {
-    CUtensorMap mk, mv;
-    if ((rc = encode_cache_map(&mk, k_cache, kv_dtype, head_dim, num_kv_heads, num_blocks,
-                               cache_strides)))
-      return rc;
-    if ((rc = encode_cache_map(&mv, v_cache, kv_dtype, head_dim, num_kv_heads, num_blocks,
-                               cache_strides)))
-      return rc;
+  if (tc_eligible(k_cache, v_cache, num_q_heads, num_kv_heads, head_dim, block_size,
+                  cache_strides, q_dtype, kv_dtype, flags)) {
     if (kv_dtype == PKV_DTYPE_BF16)
-      rc = head_dim == 128 ? launch_tc_t<__nv_bfloat16, 128>(a, mk, mv, st, max_units)
-                           : launch_tc_t<__nv_bfloat16, 64>(a, mk, mv, st, max_units);
+      rc = head_dim == 128 ? launch_tc_t<__nv_bfloat16, 128>(a, st, max_units)
+                           : launch_tc_t<__nv_bfloat16, 64>(a, st, max_units);
     else
-      rc = head_dim == 128 ? launch_tc_t<__half, 128>(a, mk, mv, st, max_units)
-                           : launch_tc_t<__half, 64>(a, mk, mv, st, max_units);
+      rc = head_dim == 128 ? launch_tc_t<__half, 128>(a, st, max_units)
+                           : launch_tc_t<__half, 64>(a, st, max_units);
   } else {
     switch (kv_dtype) {
       case PKV_DTYPE_BF16: rc = launch_generic_d<__nv_bfloat16>(a, st, max_units); break;
