@@ -32,6 +32,7 @@ DEV_PAGE_OUT_OF_RANGE = 2
 DEV_WAIT_TIMEOUT = 4
 
 DECODE_FORCE_GENERIC = 1
+DECODE_EXACT_P = 2
 NOALLOC_SCRATCH_BYTES = 32 << 20  # PKV_NOALLOC_SCRATCH_BYTES in include/pkv.h
 
 _i32 = C.c_int32

@@ -114,6 +114,21 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
   return false;
 }
 
+// Bounded wait for a thread that is usually AHEAD of the threads it waits for
+// (a producer whose ring is full): after a few polls it sleeps with growing
+// back-off, so it does not take issue slots from the warps it is waiting on.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t *bar, uint32_t parity) {
+  uint32_t sleep_ns = 32;
+  for (uint32_t i = 0; i < kMaxWaitTries; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (i >= 4) {
+      __nanosleep(sleep_ns);
+      if (sleep_ns < 512) sleep_ns <<= 1;
+    }
+  }
+  return false;
+}
+
 // ---------------------------------------------------------------------------
 // warp-level matrix helpers (bf16 / fp16 operands, fp32 accumulate)
 // ---------------------------------------------------------------------------
@@ -172,6 +187,14 @@ template <> struct Mma16816<__half> {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(v >> 16)));
   }
 };
+
+// 2^x with the hardware approximation (ex2.approx.ftz: relative error ~2^-22;
+// -inf -> 0, results below 2^-126 flush to 0).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 // exp2 that maps the fully-masked case (x = -inf) to 0 without NaNs.
 __device__ __forceinline__ float exp2_or_zero(float x) { return x == -INFINITY ? 0.f : exp2f(x); }

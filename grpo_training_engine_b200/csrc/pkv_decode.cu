@@ -36,6 +36,7 @@
 //                         loads, per-warp online softmax.
 #include <algorithm>
 #include <climits>
+#include <cstddef>
 
 #include "pkv_common.cuh"
 
@@ -429,6 +430,10 @@ struct __align__(16) SlotMeta {
   int32_t pad[3];
 };
 
+static_assert(sizeof(SlotMeta) == 64, "SlotMeta layout");
+static_assert(offsetof(SlotMeta, qslot) == 16 && offsetof(SlotMeta, kvh) == 32,
+              "SlotMeta fields read as 16-byte blocks must stay 16-byte aligned");
+
 constexpr int kBoxRows = 16;               // tokens per page (block_size)
 constexpr int kBoxBytes = kBoxRows * 128;  // one [16][64] 16-bit box, 128-byte swizzled rows
 
@@ -494,7 +499,7 @@ __device__ __forceinline__ void split_pair(float x, float y, uint32_t &hi, uint3
 // Block-table entries of a unit held in the producer's registers, lane-strided.
 constexpr int kBtRegs = 8;  // supports up to 256 pages per unit
 
-template <typename T, int D, int NW, int S>
+template <typename T, int D, int NW, int S, bool kExactP>
 __global__ void __launch_bounds__((NW + 1) * 32, 1)
 decode_tc_kernel(DecodeArgs a) {
   using Sh = TcShape<D>;
@@ -596,7 +601,7 @@ decode_tc_kernel(DecodeArgs a) {
       const int qs = nunit % QS;
       // (1) the unit's block-table entries and query rows -> smem
       if (nunit >= QS) {
-        if (!mbar_wait_bounded(&qempty[qs], ((nunit / QS) - 1) & 1)) {
+        if (!mbar_wait_backoff(&qempty[qs], ((nunit / QS) - 1) & 1)) {
           flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
           ok = false;
         }
@@ -641,7 +646,7 @@ decode_tc_kernel(DecodeArgs a) {
             const int32_t k = kcount[cw]++;
             const int slot = cw * MD + (k % MD);
             const int32_t use = k / MD;
-            if (use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) {
+            if (use > 0 && !mbar_wait_backoff(&empty[slot], (use - 1) & 1)) {
               flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
               ok = false;
               break;
@@ -690,7 +695,7 @@ decode_tc_kernel(DecodeArgs a) {
         const int32_t k = kcount[cw]++;
         const int slot = cw * MD + (k % MD);
         const int32_t use = k / MD;
-        if (use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) {
+        if (use > 0 && !mbar_wait_backoff(&empty[slot], (use - 1) & 1)) {
           flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
           break;
         }
@@ -742,6 +747,11 @@ decode_tc_kernel(DecodeArgs a) {
   const uint8_t *vbase = reinterpret_cast<const uint8_t *>(a.vc);
   int32_t stop_at = INT32_MAX;
   bool alive = true;
+  // destination offsets of this lane's chunks c = lane + 32 i: rows r and r + 8
+  // share the swizzle pattern, so chunk i + 4 lands 1024 bytes after chunk i
+  uint32_t dst_off[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dst_off[i] = slab_chunk_offset<D>(lane + 32 * i);
   auto issue = [&](int32_t e) {
     if (e <= stop_at && alive) {
       const int ms = cw * MD + (e % MD);
@@ -753,16 +763,16 @@ decode_tc_kernel(DecodeArgs a) {
         if (kind == kElemStop) {
           stop_at = e;
         } else if (kind == kElemPage) {
-          const int64_t off = ((int64_t)meta[ms].page * a.c0 + (int64_t)meta[ms].kvh * a.c1) * 2;
+          const int64_t off =
+              ((int64_t)meta[ms].page * a.c0 + (int64_t)meta[ms].kvh * a.c1) * 2 + 16 * lane;
           const uint8_t *ks = kbase + off;
           const uint8_t *vs = vbase + off;
           const uint32_t dst = smem_u32(tiles + (size_t)(cw * S + (e % S)) * Sh::kSlot);
 #pragma unroll
           for (int i = 0; i < D / 16; ++i) {
-            const int c = lane + 32 * i;
-            const uint32_t o = slab_chunk_offset<D>(c);
-            cp_async16(dst + o, ks + 16 * c);
-            cp_async16(dst + Sh::kTile + o, vs + 16 * c);
+            const uint32_t o = dst + dst_off[i & 3] + 1024 * (i >> 2);
+            cp_async16(o, ks + 512 * i);
+            cp_async16(o + Sh::kTile, vs + 512 * i);
           }
         }
       }
@@ -781,7 +791,27 @@ decode_tc_kernel(DecodeArgs a) {
     cp_async_wait<S - 1>();  // element k's group (and all older) has landed
     __syncwarp();
     const int ms = cw * MD + (k % MD);
-    const SlotMeta md = meta[ms];
+    // per page only the first 16 bytes are needed; the unit fields are read
+    // below for a unit's first and last element
+    const int4 head = *reinterpret_cast<const int4 *>(&meta[ms]);
+    SlotMeta md;
+    md.kind = head.x;
+    md.valid = head.y;
+    md.last = head.z;
+    md.work = head.w;
+    if (md.last || md.work != cur_work) {
+      // 16-byte aligned blocks of SlotMeta: bytes 16..31 and 32..47
+      const int4 m1v = *reinterpret_cast<const int4 *>(&meta[ms].qslot);
+      const int4 m2v = *reinterpret_cast<const int4 *>(&meta[ms].kvh);
+      md.qslot = m1v.x;
+      md.b = m1v.y;
+      md.s = m1v.z;
+      md.nsplit = m1v.w;
+      md.kvh = m2v.x;
+      md.hg = m2v.y;
+      md.gcount = m2v.z;
+      md.qh0 = m2v.w;
+    }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[ms]);  // metadata copied: the producer may reuse the entry
     if (md.kind == kElemStop) break;
@@ -841,14 +871,16 @@ decode_tc_kernel(DecodeArgs a) {
       mx2 = fmaxf(mx2, __shfl_xor_sync(0xffffffffu, mx2, 1));
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
       mx2 = fmaxf(mx2, __shfl_xor_sync(0xffffffffu, mx2, 2));
+      // A page element has at least one valid token, so n1, n2 are finite:
+      // masked logits (-inf) give exp2 = 0 and the first page's alpha is 0.
       const float n1 = fmaxf(m1, mx1), n2 = fmaxf(m2, mx2);
-      const float al1 = (n1 == m1) ? 1.f : exp2_or_zero(m1 - n1);
-      const float al2 = (n2 == m2) ? 1.f : exp2_or_zero(m2 - n2);
+      const float al1 = fast_exp2(m1 - n1);
+      const float al2 = fast_exp2(m2 - n2);
       float p1[4], p2[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        p1[i] = n1 == -INFINITY ? 0.f : exp2_or_zero(x1[i] - n1);
-        p2[i] = n2 == -INFINITY ? 0.f : exp2_or_zero(x2[i] - n2);
+        p1[i] = fast_exp2(x1[i] - n1);
+        p2[i] = fast_exp2(x2[i] - n2);
       }
       l1 = l1 * al1 + ((p1[0] + p1[1]) + (p1[2] + p1[3]));
       l2 = l2 * al2 + ((p2[0] + p2[1]) + (p2[2] + p2[3]));
@@ -864,14 +896,22 @@ decode_tc_kernel(DecodeArgs a) {
           o[i][3] *= al2;
         }
       }
-      // ---- O += P V, P as the A operand straight from the S fragments. P is split
-      // into a 16-bit head and a 16-bit remainder (P = hi + lo, |lo| <= 2^-9 |P|),
-      // so the product keeps ~17 significant bits of P instead of 8.
+      // ---- O += P V, P as the A operand straight from the S fragments, rounded
+      // to 16 bits (relative error <= 2^-9 per weight). With kExactP, P is split
+      // into a 16-bit head and a 16-bit remainder (P = hi + lo) and both are
+      // multiplied, keeping ~17 significant bits of P.
       uint32_t ph[4], pl[4];
-      split_pair<M>(p1[0], p1[1], ph[0], pl[0]);
-      split_pair<M>(p2[0], p2[1], ph[1], pl[1]);
-      split_pair<M>(p1[2], p1[3], ph[2], pl[2]);
-      split_pair<M>(p2[2], p2[3], ph[3], pl[3]);
+      if constexpr (kExactP) {
+        split_pair<M>(p1[0], p1[1], ph[0], pl[0]);
+        split_pair<M>(p2[0], p2[1], ph[1], pl[1]);
+        split_pair<M>(p1[2], p1[3], ph[2], pl[2]);
+        split_pair<M>(p2[2], p2[3], ph[3], pl[3]);
+      } else {
+        ph[0] = M::pack(p1[0], p1[1]);
+        ph[1] = M::pack(p2[0], p2[1]);
+        ph[2] = M::pack(p1[2], p1[3]);
+        ph[3] = M::pack(p2[2], p2[3]);
+      }
 #pragma unroll
       for (int np = 0; np < Sh::kNTiles / 2; ++np) {
         uint32_t b0, b1, b2, b3;
@@ -879,8 +919,10 @@ decode_tc_kernel(DecodeArgs a) {
         ldsm_x4_trans(vt + vo + (np >> 2) * kBoxBytes, b0, b1, b2, b3);
         M::run(o[2 * np], ph[0], ph[1], ph[2], ph[3], b0, b1);
         M::run(o[2 * np + 1], ph[0], ph[1], ph[2], ph[3], b2, b3);
-        M::run(o[2 * np], pl[0], pl[1], pl[2], pl[3], b0, b1);
-        M::run(o[2 * np + 1], pl[0], pl[1], pl[2], pl[3], b2, b3);
+        if constexpr (kExactP) {
+          M::run(o[2 * np], pl[0], pl[1], pl[2], pl[3], b0, b1);
+          M::run(o[2 * np + 1], pl[0], pl[1], pl[2], pl[3], b2, b3);
+        }
       }
     }
     __syncwarp();
@@ -972,7 +1014,10 @@ int32_t resolve_pps(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t max_b
   const int32_t rows = group_rows_for(G, D);
   const int64_t units = (int64_t)B * Hkv * ((G + rows - 1) / rows);
   const int64_t work = units * std::max<int32_t>(max_blocks, 1);
-  const int64_t target = (int64_t)device_sms() * 48;  // ~48 work units per SM
+  // ~24 work units per SM: measured on B200, bigger splits amortise the
+  // per-unit epilogue (config 4: 96 pages 82%, 152 86%, 256 88% of HBM peak)
+  // while dynamic scheduling keeps the tail to about one unit
+  const int64_t target = (int64_t)device_sms() * 24;
   int64_t P = (work + target - 1) / target;
   P = std::min<int64_t>(std::max<int64_t>(P, 8), kMaxPagesPerSplit);
   return (int32_t)std::min<int64_t>((P + 7) / 8 * 8, kMaxPagesPerSplit);
@@ -1077,12 +1122,12 @@ int launch_generic_d(const DecodeArgs &a, cudaStream_t st, int64_t max_units) {
 // head_dim 128, 8 x 6 x 4 KB for head_dim 64.
 constexpr int kTcWarps = 8;
 
-template <typename T, int D>
-int launch_tc_t(const DecodeArgs &a, cudaStream_t st, int64_t max_units) {
+template <typename T, int D, bool kExactP>
+int launch_tc_x(const DecodeArgs &a, cudaStream_t st, int64_t max_units) {
   constexpr int S = D == 128 ? 3 : 6;
   using L = TcSmem<D, kTcWarps, S>;
   const size_t smem = L::bytes(a.P);
-  auto kern = decode_tc_kernel<T, D, kTcWarps, S>;
+  auto kern = decode_tc_kernel<T, D, kTcWarps, S, kExactP>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return check_launch("cudaFuncSetAttribute(tc)");
@@ -1096,6 +1141,12 @@ int launch_tc_t(const DecodeArgs &a, cudaStream_t st, int64_t max_units) {
   if (grid < 1) grid = 1;
   kern<<<(unsigned)grid, (kTcWarps + 1) * 32, smem, st>>>(a);
   return check_launch("decode_tc_kernel");
+}
+
+template <typename T, int D>
+int launch_tc_t(const DecodeArgs &a, cudaStream_t st, int64_t max_units, int32_t flags) {
+  return (flags & PKV_DECODE_EXACT_P) ? launch_tc_x<T, D, true>(a, st, max_units)
+                                      : launch_tc_x<T, D, false>(a, st, max_units);
 }
 
 }  // namespace
@@ -1235,11 +1286,11 @@ extern "C" int pkv_decode_run(const void *q, const void *k_cache, const void *v_
   if (tc_eligible(k_cache, v_cache, num_q_heads, num_kv_heads, head_dim, block_size,
                   cache_strides, q_dtype, kv_dtype, flags)) {
     if (kv_dtype == PKV_DTYPE_BF16)
-      rc = head_dim == 128 ? launch_tc_t<__nv_bfloat16, 128>(a, st, max_units)
-                           : launch_tc_t<__nv_bfloat16, 64>(a, st, max_units);
+      rc = head_dim == 128 ? launch_tc_t<__nv_bfloat16, 128>(a, st, max_units, flags)
+                           : launch_tc_t<__nv_bfloat16, 64>(a, st, max_units, flags);
     else
-      rc = head_dim == 128 ? launch_tc_t<__half, 128>(a, st, max_units)
-                           : launch_tc_t<__half, 64>(a, st, max_units);
+      rc = head_dim == 128 ? launch_tc_t<__half, 128>(a, st, max_units, flags)
+                           : launch_tc_t<__half, 64>(a, st, max_units, flags);
   } else {
     switch (kv_dtype) {
       case PKV_DTYPE_BF16: rc = launch_generic_d<__nv_bfloat16>(a, st, max_units); break;

@@ -323,6 +323,7 @@ def paged_attention_decode(
     pages_per_split: int = 0,
     plan: Optional[DecodePlan] = None,
     force_generic: bool = False,
+    exact: bool = False,
     status: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
     """Single-query attention over the paged cache; returns fp32 [B, Hq, D].
@@ -334,6 +335,10 @@ def paged_attention_decode(
     (paged_kv.py:697,761,938); scale defaults to 1/sqrt(D) (paged_kv.py:681,900).
     num_splits > 0 caps the number of split-K chunks per sequence;
     pages_per_split > 0 sets the chunk length directly; both 0 = heuristic.
+    The tensor-core kernel multiplies the softmax weights by V in 16 bits
+    (max-abs error a few 1e-3 for N(0,1) data); exact=True keeps ~17
+    significant bits of the weights at some speed cost. The CUDA-core kernel
+    (fp32 caches, force_generic=True) is fp32 throughout.
     """
     _check_cache_pair(k_cache, v_cache)
     if q.ndim != 3:
@@ -361,7 +366,7 @@ def paged_attention_decode(
         raise ValueError("decode plan was made for a different geometry.")
     lib = _lib.load()
     ws = plan.workspace
-    flags = _lib.DECODE_FORCE_GENERIC if force_generic else 0
+    flags = (_lib.DECODE_FORCE_GENERIC if force_generic else 0) | (_lib.DECODE_EXACT_P if exact else 0)
     with torch.cuda.device(dev):
         _lib.check(
             "pkv_decode_run",

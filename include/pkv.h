@@ -68,8 +68,12 @@ enum {
 
 /* Decode flags. */
 enum {
-    PKV_DECODE_FORCE_GENERIC = 1 /* use the CUDA-core kernel even when the
-                                    TMA + tensor-core kernel could run */
+    PKV_DECODE_FORCE_GENERIC = 1, /* use the CUDA-core kernel even when the
+                                     tensor-core kernel could run            */
+    PKV_DECODE_EXACT_P = 2        /* tensor-core kernel: multiply the softmax
+                                     weights as a 16-bit head plus 16-bit
+                                     remainder (~17 significant bits instead
+                                     of 8); slower, closer to fp32           */
 };
 
 int pkv_abi_version(void);

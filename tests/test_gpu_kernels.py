@@ -46,8 +46,8 @@ def _maxabs(a: torch.Tensor, b) -> float:
 
 # ------------------------------------------------------------------ golden vectors
 @pytest.mark.parametrize("name", [c["name"] for c in cases.CASES])
-@pytest.mark.parametrize("force_generic", [False, True])
-def test_golden_append_and_decode(name, force_generic):
+@pytest.mark.parametrize("mode", ["fast", "exact", "generic"])
+def test_golden_append_and_decode(name, mode):
     case = cases.BY_NAME[name]
     ref_out, meta = load_golden(name)
     t = cases.to_torch(cases.make_inputs(case), case["dtype"], device=DEV)
@@ -57,9 +57,12 @@ def test_golden_append_and_decode(name, force_generic):
         ctx = ctx + 1
     assert _sha(t["k_cache"], t["v_cache"]) == meta["cache_after_append_sha"]
     out = paged_attention_decode(t["q"], t["k_cache"], t["v_cache"], t["block_tables"], ctx,
-                                 force_generic=force_generic)
+                                 force_generic=mode == "generic", exact=mode == "exact")
     torch.cuda.synchronize()
     assert _maxabs(out, ref_out) <= ATOL[case["dtype"]], _maxabs(out, ref_out)
+    if mode != "fast" or case["dtype"] == "float32":
+        # exact-P tensor-core kernel and the CUDA-core kernel track fp32 closely
+        assert _maxabs(out, ref_out) <= 2e-4, _maxabs(out, ref_out)
 
 
 @pytest.mark.parametrize("name", [c["name"] for c in cases.CASES if c.get("prompt_steps")])
@@ -119,6 +122,18 @@ def test_decode_matches_oracle(shape, splits):
         out = paged_attention_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), ctx.to(DEV),
                                      num_splits=splits, force_generic=force_generic)
         assert _maxabs(out, ref) <= tol, (force_generic, _maxabs(out, ref))
+
+
+def test_exact_mode_precision_and_fast_mode_error_size():
+    q, kc, vc, bt, ctx = _random_case(13, 8, 12, 2, 128, 16, [4000, 17, 900, 1, 2048, 300, 5000, 64],
+                                      torch.bfloat16)
+    ref = oracle.decode(q, kc, vc, bt, ctx)
+    args = [x.to(DEV) for x in (q, kc, vc, bt, ctx)]
+    exact = paged_attention_decode(*args, exact=True)
+    fast = paged_attention_decode(*args)
+    assert _maxabs(exact, ref) <= 2e-4
+    assert _maxabs(fast, ref) <= 2e-2
+    assert decode_kernel_kind(args[0], args[1]) == "tensor_core"
 
 
 @pytest.mark.parametrize("pages_per_split", [1, 2, 8, 64])
