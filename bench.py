@@ -41,6 +41,12 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 METRIC = "paged KV decode: KV-read HBM GB/s and seq-steps/s at 1/2/4/8 B200"
+
+# DRAM bytes (read + write) per algorithmic byte of one decode launch, from an
+# ncu capture of decode_tc_kernel on the config-4 geometry (512 sequences, one
+# layer; profiles/decode_tc_512seq_1layer_ncu.md). Traffic grows with the
+# pages read, so roofline.traffic scales it to the full launch.
+DECODE_DRAM_TRAFFIC_RATIO = 1.0063
 UNIT = "seq-steps/s"
 
 
@@ -387,7 +393,11 @@ def run_ours(args, rank, world, local):
                 "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else peak_kind,
                 "unit": "GB/s",
                 "frac": round(achieved / peak, 4),
-                "traffic": args.traffic_bytes,
+                "traffic": (args.traffic_bytes if args.traffic_bytes is not None else
+                            (int(DECODE_DRAM_TRAFFIC_RATIO * dec_bytes) if wl.config == 4 else None)),
+                "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of a reduced "
+                                   "capture (512 seqs, 1 layer), scaled by pages read"
+                                   if wl.config == 4 else None),
                 "algorithmic_bytes_per_launch": dec_bytes,
                 "avg_launch_ms": round(decode_avg_ms, 4),
             },
