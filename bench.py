@@ -618,20 +618,21 @@ def run_reference(args, rank, world):
         oracle.decode(q, k, v, bt, ctx, nthreads=threads)
         return time.perf_counter() - t
 
-    # size one step's sample to ~target seconds of CPU work
+    # size one step's sample to ~target seconds of CPU work, build it once,
+    # then time every step on it (the data does not change the work)
     n = max(1, threads // 2)
     while True:
-        dt = run(sample(n))
+        smp = sample(n)
+        dt = run(smp)
         if dt >= args.ref_step_seconds * 0.5 or n >= len(mine):
             break
         n = min(len(mine), max(n + 1, int(n * args.ref_step_seconds / max(dt, 1e-3))))
     for _ in range(args.warmup):
-        run(sample(n))
+        run(smp)
     times, seqs = [], 0
     for _ in range(args.steps):
-        s = sample(n)
-        times.append(run(s))
-        seqs += len(s[4])
+        times.append(run(smp))
+        seqs += len(smp[4])
     total = sum(times)
     value = seqs / (total * layers)
     line = {

@@ -47,6 +47,10 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kTcRows = 16;   // query heads per head group in the tensor-core kernel (MMA M)
 constexpr int kGenThreads = 128;
 constexpr int kGenWarps = kGenThreads / 32;
+// Block-table entries of a unit held in the tensor-core producer's registers,
+// lane-strided: kBtRegs per lane, so a split has at most kMaxPagesPerSplit pages.
+constexpr int kBtRegs = 8;
+constexpr int32_t kMaxPagesPerSplit = kBtRegs * 32;
 
 // ---------------------------------------------------------------------------
 // workspace layout
@@ -149,59 +153,122 @@ __device__ __forceinline__ Unit decode_unit(const DecodeArgs &a, int32_t w) {
 // ---------------------------------------------------------------------------
 constexpr int kPlanThreads = 1024;
 
+// Block-wide exclusive scan of one value per thread (kPlanThreads threads);
+// returns the thread's exclusive prefix, *total gets the block sum.
+__device__ __forceinline__ int32_t block_exclusive_scan(int32_t v, int32_t *warp_tot, int32_t *total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_tot[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int32_t t = warp_tot[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += y;
+    }
+    warp_tot[lane] = t;  // inclusive totals per warp
+  }
+  __syncthreads();
+  const int32_t excl = (warp > 0 ? warp_tot[warp - 1] : 0) + x - v;
+  *total = warp_tot[kPlanThreads / 32 - 1];
+  __syncthreads();  // warp_tot is reused by the next scan
+  return excl;
+}
+
+// Splits of sequence b: n in total, `full` of them P pages long; when n > full
+// the last split is partial with `rest` pages (an empty sequence is one
+// partial split of 0 pages).
+struct SeqSplits {
+  int32_t ctx, n, full, rest;
+};
+
+__device__ __forceinline__ SeqSplits seq_splits(const int32_t *ctx, int32_t b, int32_t bs,
+                                                int32_t cap, int32_t P, int32_t *status,
+                                                bool report) {
+  SeqSplits r;
+  int32_t c = ctx[b];
+  if (c < 0 || c > cap) {
+    if (report) flag_status(status, PKV_DEV_CTX_OUT_OF_RANGE);
+    c = c < 0 ? 0 : cap;
+  }
+  const int32_t pages = (c + bs - 1) / bs;
+  r.ctx = c;
+  r.n = pages > 0 ? (pages + P - 1) / P : 1;
+  r.rest = pages % P;
+  r.full = pages / P;
+  return r;
+}
+
+// Items are ordered for the dynamic scheduler: every full P-page split first
+// (sequence order), then the partial last splits by decreasing length, so the
+// units left for the end of a launch are the shortest. Partial-result slots do
+// not depend on this order (they are indexed by seq_off[b] + split).
 __global__ void __launch_bounds__(kPlanThreads)
 plan_kernel(const int32_t *__restrict__ ctx, int32_t B, int32_t bs, int32_t max_blocks, int32_t P,
             int32_t upi, int32_t *hdr, int32_t *seq_off, int32_t *seq_nsplit, int4 *items,
             int32_t *status) {
   __shared__ int32_t warp_tot[kPlanThreads / 32];
-  __shared__ int32_t carry;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) carry = 0;
+  __shared__ int32_t bucket[kMaxPagesPerSplit + 1];  // partial splits per length, then cursors
+  __shared__ int32_t carry_all, carry_full;
+  const int tid = threadIdx.x;
+  for (int i = tid; i <= P; i += kPlanThreads) bucket[i] = 0;
+  if (tid == 0) carry_all = carry_full = 0;
   __syncthreads();
   const int32_t cap = max_blocks * bs;
+  // pass 1: per-sequence offsets, full-split count, histogram of partial lengths
   for (int32_t base = 0; base < B; base += kPlanThreads) {
     const int32_t b = base + tid;
-    int32_t n = 0, c = 0;
+    SeqSplits q{0, 0, 0, 0};
+    if (b < B) q = seq_splits(ctx, b, bs, cap, P, status, true);
+    int32_t tot_n, tot_f;
+    const int32_t off = carry_all + block_exclusive_scan(q.n, warp_tot, &tot_n);
+    block_exclusive_scan(q.full, warp_tot, &tot_f);
     if (b < B) {
-      c = ctx[b];
-      if (c < 0 || c > cap) {
-        flag_status(status, PKV_DEV_CTX_OUT_OF_RANGE);
-        c = c < 0 ? 0 : cap;
-      }
-      const int32_t pages = (c + bs - 1) / bs;
-      n = pages > 0 ? (pages + P - 1) / P : 1;
-    }
-    // block-wide exclusive scan of n
-    int32_t x = n;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      int32_t y = __shfl_up_sync(0xffffffffu, x, o);
-      if (lane >= o) x += y;
-    }
-    if (lane == 31) warp_tot[warp] = x;
-    __syncthreads();
-    if (warp == 0) {
-      int32_t t = warp_tot[lane];
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        int32_t y = __shfl_up_sync(0xffffffffu, t, o);
-        if (lane >= o) t += y;
-      }
-      warp_tot[lane] = t;  // inclusive totals per warp
+      seq_off[b] = off;
+      seq_nsplit[b] = q.n;
+      if (q.n > q.full) atomicAdd(&bucket[q.rest], 1);
     }
     __syncthreads();
-    const int32_t excl = carry + (warp > 0 ? warp_tot[warp - 1] : 0) + x - n;
+    if (tid == 0) {
+      carry_all += tot_n;
+      carry_full += tot_f;
+    }
+    __syncthreads();
+  }
+  // bucket -> first item index of each partial length, longest first
+  if (tid == 0) {
+    int32_t pos = carry_full;
+    for (int32_t r = P; r >= 0; --r) {
+      const int32_t cnt = bucket[r];
+      bucket[r] = pos;
+      pos += cnt;
+    }
+    carry_full = 0;
+  }
+  __syncthreads();
+  // pass 2: write the items
+  for (int32_t base = 0; base < B; base += kPlanThreads) {
+    const int32_t b = base + tid;
+    SeqSplits q{0, 0, 0, 0};
+    if (b < B) q = seq_splits(ctx, b, bs, cap, P, status, false);
+    int32_t tot_f;
+    const int32_t foff = carry_full + block_exclusive_scan(q.full, warp_tot, &tot_f);
     if (b < B) {
-      seq_off[b] = excl;
-      seq_nsplit[b] = n;
-      for (int32_t s = 0; s < n; ++s) items[excl + s] = make_int4(b, s, c, n);
+      for (int32_t s = 0; s < q.full; ++s) items[foff + s] = make_int4(b, s, q.ctx, q.n);
+      if (q.n > q.full) items[atomicAdd(&bucket[q.rest], 1)] = make_int4(b, q.n - 1, q.ctx, q.n);
     }
     __syncthreads();
-    if (tid == 0) carry += warp_tot[kPlanThreads / 32 - 1];
+    if (tid == 0) carry_full += tot_f;
     __syncthreads();
   }
   if (tid == 0) {
-    hdr[0] = carry * upi;  // total work units
+    hdr[0] = carry_all * upi;  // total work units
     hdr[1] = P;
     hdr[2] = B;
     hdr[3] = upi;
@@ -496,8 +563,6 @@ __device__ __forceinline__ void split_pair(float x, float y, uint32_t &hi, uint3
   lo = M::pack(x - hx, y - hy);
 }
 
-// Block-table entries of a unit held in the producer's registers, lane-strided.
-constexpr int kBtRegs = 8;  // supports up to 256 pages per unit
 
 template <typename T, int D, int NW, int S, bool kExactP>
 __global__ void __launch_bounds__((NW + 1) * 32, 1)
@@ -1003,9 +1068,6 @@ int device_sms() {
   return sms;
 }
 
-// Largest split the kernels take (the tensor-core producer holds a unit's
-// block-table entries in kBtRegs registers per lane).
-constexpr int32_t kMaxPagesPerSplit = kBtRegs * 32;
 
 int32_t resolve_pps(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t max_blocks,
                     int32_t pps) {
