@@ -296,7 +296,8 @@ def run_ours(args, rank, world, local):
             pkv.paged_kv_append(wl.k_new[layer], wl.v_new[layer], kc, vc, wl.block_tables, wl.ctx_pre)
             if ev_pairs is not None:
                 ev_pairs[layer][0].record(stream)
-            pkv.paged_attention_decode(wl.q[layer], kc, vc, wl.block_tables, wl.ctx, out=wl.out[layer], plan=plan)
+            pkv.paged_attention_decode(wl.q[layer], kc, vc, wl.block_tables, wl.ctx, out=wl.out[layer], plan=plan,
+                                       exact=args.exact)
             if ev_pairs is not None:
                 ev_pairs[layer][1].record(stream)
         return plan
@@ -380,6 +381,7 @@ def run_ours(args, rank, world, local):
                 "block_size": wl.bs,
                 "pages_per_split": plan_pps(wl, args),
                 "step": "per layer: append 1 token/seq/kv-head + paged decode attention; 1 plan per step",
+                "softmax_weights": "16-bit hi+lo (exact)" if args.exact else "bf16",
                 "l2": "no flush: KV pool per GPU %.1f GB >> 126 MB L2" % (2 * wl.k_pool.numel() * 2 / 1e9),
                 "parallelism": f"dp{world} (sequence shards, LPT by context length, no collective)",
             },
@@ -471,7 +473,8 @@ def run_e2e(args, wl, world, device):
                 comp.wait_event(d2h[layer])  # previous step's output left the device
             kc, vc = wl.k_pool[layer], wl.v_pool[layer]
             pkv.paged_kv_append(kn_d[layer], vn_d[layer], kc, vc, wl.block_tables, ctx_pre)
-            pkv.paged_attention_decode(q_d[layer], kc, vc, wl.block_tables, ctx, out=out_d[layer], plan=plan)
+            pkv.paged_attention_decode(q_d[layer], kc, vc, wl.block_tables, ctx, out=out_d[layer], plan=plan,
+                                       exact=args.exact)
             done[layer].record(comp)
             with torch.cuda.stream(copy):
                 copy.wait_event(done[layer])
@@ -676,6 +679,7 @@ def main():
     ap.add_argument("--seqs", type=int, default=None, help="override sequences per GPU (diagnostics only)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--pages-per-split", type=int, default=0)
+    ap.add_argument("--exact", action="store_true", help="decode with PKV_DECODE_EXACT_P")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
