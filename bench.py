@@ -288,18 +288,21 @@ def run_ours(args, rank, world, local):
     L, B = wl.layers, wl.B
     stream = torch.cuda.current_stream(device)
 
+    ws = {"buf": None}  # one plan workspace, reused by every step
+
     def step(ev_pairs=None):
         plan = ops.plan_decode(wl.ctx, wl.hq, wl.hkv, wl.d, wl.bs, wl.max_blocks,
-                               pages_per_split=args.pages_per_split)
+                               pages_per_split=args.pages_per_split, workspace=ws["buf"])
+        ws["buf"] = plan.workspace
         for layer in range(L):
             kc, vc = wl.k_pool[layer], wl.v_pool[layer]
             pkv.paged_kv_append(wl.k_new[layer], wl.v_new[layer], kc, vc, wl.block_tables, wl.ctx_pre)
             if ev_pairs is not None:
-                ev_pairs[layer][0].record(stream)
+                ev_pairs[layer][0].record()
             pkv.paged_attention_decode(wl.q[layer], kc, vc, wl.block_tables, wl.ctx, out=wl.out[layer], plan=plan,
                                        exact=args.exact)
             if ev_pairs is not None:
-                ev_pairs[layer][1].record(stream)
+                ev_pairs[layer][1].record()
         return plan
 
     step()
@@ -308,18 +311,28 @@ def run_ours(args, rank, world, local):
         step()
     torch.cuda.synchronize()
 
+    # external events: inside a CUDA graph they become event-record nodes
+    ev_all = [[[torch.cuda.Event(enable_timing=True, external=args.graph) for _ in range(2)] for _ in range(L)]
+              for _ in range(args.steps)]
+    graph = None
+    if args.graph:
+        graph = capture_steps(lambda: [step(ev_all[s]) for s in range(args.steps)])
+        graph.replay()  # untimed: the first launch also uploads the graph
+        torch.cuda.synchronize()
+
     clocks = ClockSampler(physical_gpu(local))
     clocks.start()
     time.sleep(0.3)
-    ev_all = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(L)]
-              for _ in range(args.steps)]
     barrier(world)
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
-    for s in range(args.steps):
-        step(ev_all[s])
+    if graph is not None:
+        graph.replay()
+    else:
+        for s in range(args.steps):
+            step(ev_all[s])
     t1.record(stream)
     torch.cuda.synchronize()
     barrier(world)
@@ -381,6 +394,9 @@ def run_ours(args, rank, world, local):
                 "block_size": wl.bs,
                 "pages_per_split": plan_pps(wl, args),
                 "step": "per layer: append 1 token/seq/kv-head + paged decode attention; 1 plan per step",
+                "launch": (f"the {args.steps} timed steps captured as one CUDA graph, replayed once (after "
+                           f"{args.warmup} eager warm-up steps and one untimed replay)" if args.graph else
+                           "eager launches from Python"),
                 "softmax_weights": "16-bit hi+lo (exact)" if args.exact else "bf16",
                 "l2": "no flush: KV pool per GPU %.1f GB >> 126 MB L2" % (2 * wl.k_pool.numel() * 2 / 1e9),
                 "parallelism": f"dp{world} (sequence shards, LPT by context length, no collective)",
@@ -415,6 +431,18 @@ def run_ours(args, rank, world, local):
         print(json.dumps(line), flush=True)
 
 
+def capture_steps(fn):
+    """Capture the launches fn() makes on the current device into one CUDA graph.
+
+    The library's entry points only enqueue kernels on torch's current stream
+    (no allocation, no synchronisation when the plan workspace and outputs are
+    passed in), so a decode step captures as-is."""
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    return graph
+
+
 def plan_pps(wl, args) -> int:
     from grpo_training_engine_b200 import _lib
 
@@ -438,16 +466,16 @@ def run_e2e(args, wl, world, device):
     q_d, kn_d, vn_d = torch.empty_like(wl.q), torch.empty_like(wl.k_new), torch.empty_like(wl.v_new)
     ctx_d = [torch.empty_like(wl.ctx) for _ in range(2)]  # double-buffered across steps
     out_d = torch.empty_like(wl.out)
-    comp = torch.cuda.current_stream(device)
     copy = torch.cuda.Stream(device)
     h2d = [torch.cuda.Event() for _ in range(L)]
     done = [torch.cuda.Event() for _ in range(L)]
     d2h = [torch.cuda.Event() for _ in range(L)]
     ctx_ready = [torch.cuda.Event() for _ in range(2)]
     ctx_free = [torch.cuda.Event() for _ in range(2)]
-    state = {"step": 0}
+    state = {"step": 0, "ws": None}
 
     def step(first: bool):
+        comp = torch.cuda.current_stream(device)
         s = state["step"]
         state["step"] += 1
         buf = s % 2
@@ -466,7 +494,9 @@ def run_e2e(args, wl, world, device):
         comp.wait_event(ctx_ready[buf])
         ctx = ctx_d[buf]
         ctx_pre = ctx - 1
-        plan = ops.plan_decode(ctx, wl.hq, wl.hkv, wl.d, wl.bs, wl.max_blocks, pages_per_split=args.pages_per_split)
+        plan = ops.plan_decode(ctx, wl.hq, wl.hkv, wl.d, wl.bs, wl.max_blocks, pages_per_split=args.pages_per_split,
+                               workspace=state["ws"])
+        state["ws"] = plan.workspace
         for layer in range(L):
             comp.wait_event(h2d[layer])
             if not first:
@@ -487,12 +517,30 @@ def run_e2e(args, wl, world, device):
     for _ in range(max(1, args.warmup)):
         step(False)
     torch.cuda.synchronize()
+    graph = None
+    if args.graph:
+        state["step"] = 0
+
+        def body():
+            cap = torch.cuda.current_stream(device)
+            copy.wait_stream(cap)  # fork the copy stream into the capture
+            for i in range(args.steps):
+                step(i == 0)  # a replay starts after the previous one has finished
+            cap.wait_stream(copy)  # and join it back
+
+        graph = capture_steps(body)
+        graph.replay()
+        torch.cuda.synchronize()
+    comp = torch.cuda.current_stream(device)
     barrier(world)
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(comp)
-    for _ in range(args.steps):
-        step(False)
+    if graph is not None:
+        graph.replay()
+    else:
+        for _ in range(args.steps):
+            step(False)
     comp.wait_stream(copy)
     t1.record(comp)
     torch.cuda.synchronize()
@@ -508,6 +556,8 @@ def run_e2e(args, wl, world, device):
         "d2h_bytes_per_step": int(out_h.numel() * 4),
         "ms_per_step": round(ms, 4),
         "api": "grpo_training_engine_b200.paged_kv_append + paged_attention_decode (C ABI pkv_append / pkv_decode_run)",
+        "launch": ("the timed steps' copies and calls captured as one CUDA graph on two streams"
+                   if graph is not None else "eager launches from Python on two streams"),
         "output_matches_device_run": bool(ok),
     }
 
@@ -680,6 +730,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--pages-per-split", type=int, default=0)
     ap.add_argument("--exact", action="store_true", help="decode with PKV_DECODE_EXACT_P")
+    ap.add_argument("--no-graph", dest="graph", action="store_false",
+                    help="launch every kernel from Python instead of replaying a CUDA graph of the timed steps")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)

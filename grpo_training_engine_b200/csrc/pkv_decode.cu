@@ -60,7 +60,8 @@ struct WsLayout {
   int64_t max_items;
   int32_t units_per_item;  // num_kv_heads * head_groups
   int32_t group_rows;      // query heads per head group (partial row count)
-  int32_t part_floats;     // floats per partial unit
+  int32_t part_o;          // offset of the accumulator rows in a partial unit (16-byte aligned)
+  int32_t part_floats;     // floats per partial unit: [max GR][sum GR][pad][acc GR x D]
 };
 
 __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -80,7 +81,8 @@ WsLayout ws_layout(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t max_bl
   w.units_per_item = Hkv * HG;
   const int64_t per_seq = max_blocks > 0 ? (max_blocks + P - 1) / P : 1;
   w.max_items = (int64_t)B * per_seq;
-  w.part_floats = w.group_rows * (D + 2);
+  w.part_o = (int32_t)align_up(2 * (size_t)w.group_rows, 4);
+  w.part_floats = w.part_o + w.group_rows * D;
   size_t off = 0;
   w.hdr = off; off += 256;
   w.seq_off = off; off = align_up(off + sizeof(int32_t) * (size_t)B, 256);
@@ -102,9 +104,10 @@ struct DecodeArgs {
   float *out;
   const void *kc;
   const void *vc;
-  int32_t B, Hq, Hkv, G, GR, HG, D, bs, num_blocks, max_blocks, P, upi, part_floats;
+  int32_t B, Hq, Hkv, G, GR, HG, D, bs, num_blocks, max_blocks, P, upi, part_o, part_floats;
   int32_t q_dtype, kv_dtype;
-  int32_t q_vec;  // q rows are 16-byte aligned and contiguous in head_dim
+  int32_t q_vec;    // q rows are 16-byte aligned and contiguous in head_dim
+  int32_t out_vec;  // out rows are 16-byte aligned and contiguous in head_dim
   int64_t q0, q1, q2;
   int64_t c0, c1, c2, c3;
   int64_t bt0, bt1;
@@ -116,7 +119,6 @@ struct DecodeArgs {
   const int4 *items;  // per item {b, split, clamped ctx, splits of b}
   float *partials;
   int32_t *status;
-  int32_t *sched;  // {next unit, finished CTAs}: dynamic scheduling of the tensor-core kernel
 };
 
 struct Unit {
@@ -205,7 +207,7 @@ __device__ __forceinline__ SeqSplits seq_splits(const int32_t *ctx, int32_t b, i
   return r;
 }
 
-// Items are ordered for the dynamic scheduler: every full P-page split first
+// Items are ordered for the tensor-core kernel's snake schedule: every full P-page split first
 // (sequence order), then the partial last splits by decreasing length, so the
 // units left for the end of a launch are the shortest. Partial-result slots do
 // not depend on this order (they are indexed by seq_off[b] + split).
@@ -272,8 +274,8 @@ plan_kernel(const int32_t *__restrict__ ctx, int32_t B, int32_t bs, int32_t max_
     hdr[1] = P;
     hdr[2] = B;
     hdr[3] = upi;
-    hdr[4] = 0;  // next unit to hand out (dynamic scheduling)
-    hdr[5] = 0;  // CTAs that have finished fetching units
+    hdr[4] = 0;  // reserved
+    hdr[5] = 0;  // reserved
   }
 }
 
@@ -281,16 +283,19 @@ plan_kernel(const int32_t *__restrict__ ctx, int32_t B, int32_t bs, int32_t max_
 // split-K epilogue shared by both kernels.
 // xm/xl hold each warp's running max (log2 units) and sum per head row, xo
 // each warp's unnormalised accumulator; rows are [warp][row], xo rows padded
-// to xd floats. `sync` is a barrier over the participating threads.
+// to xd floats. `split_row` = seq_off[b] + split, the sequence's partial-result
+// row (unused when the sequence has one split); callers load it ahead of time
+// so no global load sits in the epilogue. `sync` is a barrier over the
+// participating threads.
 // ---------------------------------------------------------------------------
 template <typename Sync>
-__device__ bool unit_epilogue(const DecodeArgs &a, const Unit &u, int nwarps, int xr,
-                              const float *xm, const float *xl, const float *const *xo, int xd,
-                              int tid, int nthreads, Sync &sync) {
+__device__ bool unit_epilogue(const DecodeArgs &a, const Unit &u, int32_t split_row, int nwarps,
+                              int xr, const float *xm, const float *xl, const float *const *xo,
+                              int xd, int tid, int nthreads, Sync &sync) {
   const int32_t D = a.D;
   const int32_t GR = a.GR;
   const int32_t n = u.gcount * D;
-  const int64_t unit_idx = (int64_t)(a.seq_off[u.b] + u.s) * a.upi + u.kvh * a.HG + u.hg;
+  const int64_t unit_idx = (int64_t)split_row * a.upi + u.kvh * a.HG + u.hg;
   float *part = a.partials + unit_idx * a.part_floats;
   for (int32_t i = tid; i < n; i += nthreads) {
     const int32_t g = i / D, d = i - g * D;
@@ -307,7 +312,7 @@ __device__ bool unit_epilogue(const DecodeArgs &a, const Unit &u, int nwarps, in
     if (u.nsplit == 1) {
       a.out[u.b * a.o0 + (int64_t)(u.qh0 + g) * a.o1 + d * a.o2] = O / fmaxf(L, 1e-6f);
     } else {  // merged by merge_kernel after the launch
-      part[2 * GR + g * D + d] = O;
+      part[a.part_o + g * D + d] = O;
       if (d == 0) {
         part[g] = M;
         part[GR + g] = L;
@@ -345,7 +350,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(DecodeArgs a) {
         const float *p = base + s * stride;
         const float f = exp2_or_zero(p[g] - M);
         L += f * p[GR + g];
-        O += f * p[2 * GR + g * D + d];
+        O += f * p[a.part_o + g * D + d];
       }
     }
     a.out[b * a.o0 + (int64_t)(qh0 + g) * a.o1 + d * a.o2] = O / fmaxf(L, 1e-6f);
@@ -396,6 +401,7 @@ decode_generic_kernel(DecodeArgs a) {
 
   for (int32_t w = blockIdx.x; w < total; w += gridDim.x) {
     const Unit u = decode_unit(a, w);
+    const int32_t split_row = u.nsplit > 1 ? a.seq_off[u.b] + u.s : 0;  // used at the end
     for (int i = tid; i < GM * DP; i += kGenThreads) {
       const int g = i / DP, d = i - g * DP;
       float v = 0.f;
@@ -467,7 +473,7 @@ decode_generic_kernel(DecodeArgs a) {
     const float *xo_w[kGenWarps];
 #pragma unroll
     for (int w = 0; w < kGenWarps; ++w) xo_w[w] = xo + w * kTcRows * DP;
-    unit_epilogue(a, u, kGenWarps, kTcRows, xm, xl, xo_w, DP, tid, kGenThreads, sync);
+    unit_epilogue(a, u, split_row, kGenWarps, kTcRows, xm, xl, xo_w, DP, tid, kGenThreads, sync);
   }
 }
 
@@ -493,12 +499,14 @@ struct __align__(16) SlotMeta {
   int32_t qslot;   // smem slot holding the unit's query rows
   int32_t b, s, nsplit;
   int32_t kvh, hg, gcount, qh0;
-  int32_t page;    // physical page id (kElemPage only)
-  int32_t pad[3];
+  int32_t page;       // physical page id (kElemPage only)
+  int32_t split_row;  // seq_off[b] + s: the unit's partial-result row (nsplit > 1)
+  int32_t pad[2];
 };
 
 static_assert(sizeof(SlotMeta) == 64, "SlotMeta layout");
-static_assert(offsetof(SlotMeta, qslot) == 16 && offsetof(SlotMeta, kvh) == 32,
+static_assert(offsetof(SlotMeta, qslot) == 16 && offsetof(SlotMeta, kvh) == 32 &&
+                  offsetof(SlotMeta, page) == 48,
               "SlotMeta fields read as 16-byte blocks must stay 16-byte aligned");
 
 constexpr int kBoxRows = 16;               // tokens per page (block_size)
@@ -586,45 +594,44 @@ decode_tc_kernel(DecodeArgs a) {
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int MD = L::MD, QS = L::QS;
-  if (tid == 0) {
-    for (int i = 0; i < NW * MD; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
-    }
-    for (int i = 0; i < QS; ++i) mbar_init(&qempty[i], 1);
-    mbar_init(group, NW);
-    fence_mbar_init();
+  static_assert(NW * MD <= (NW + 1) * 32 && QS <= (NW + 1) * 32, "one thread per mbarrier");
+  if (tid < NW * MD) {
+    mbar_init(&full[tid], 1);
+    mbar_init(&empty[tid], 1);
   }
+  if (tid < QS) mbar_init(&qempty[tid], 1);
+  if (tid == 0) mbar_init(group, NW);
+  fence_mbar_init();
   __syncthreads();
 
   const int32_t total = a.hdr[0];
 
   if (warp == NW) {
     // =========================== producer warp ===========================
-    // Units come from a global counter (dynamic scheduling). The warp keeps a
-    // three-deep software pipeline so no global-load latency is exposed at a
-    // unit boundary: while lane 0 streams unit n, the unit id of n+3 is being
-    // fetched, the descriptor of n+2 loaded, and the block-table entries and
-    // query rows of n+1 loaded into registers.
+    // Static schedule: the plan numbers units longest first, and CTA c takes
+    // unit c in round 0, 2G-1-c in round 1, 2G+c in round 2, ... (G =
+    // gridDim.x, "snake" order), so the CTAs given the longest units of one
+    // round get the shortest of the next and every CTA ends within about one
+    // short unit of the others, with no atomics. Knowing its whole list, the
+    // warp runs a three-deep software pipeline so no global-load latency is
+    // exposed at a unit boundary: while lane 0 publishes unit r, the
+    // descriptor of r+2 is being loaded and the block-table entries and query
+    // rows of r+1 are in flight into registers.
     const uint32_t FULL = 0xffffffffu;
-    int32_t fetched = 0;
-    if (lane == 0) fetched = atomicAdd(&a.sched[0], 1);
-    int32_t w1 = __shfl_sync(FULL, fetched, 0);
-    if (lane == 0) fetched = atomicAdd(&a.sched[0], 1);
-    int32_t w2 = __shfl_sync(FULL, fetched, 0);
-    if (lane == 0) fetched = atomicAdd(&a.sched[0], 1);  // w3, broadcast at the first rotation
+    const int32_t G = (int32_t)gridDim.x;
     const int4 none = make_int4(0, 0, 0, 1);
-    int4 d1 = w1 < total ? a.items[w1 / a.upi] : none;
-    int4 d2 = w2 < total ? a.items[w2 / a.upi] : none;
 
-    // registers holding the NEXT unit's block-table entries and query rows
+    // registers holding the NEXT unit's block-table entries, query rows and
+    // partial-result row
     int32_t btr[kBtRegs];
     uint4 qr[(kTcRows * D * 2 / 16 + 31) / 32];
+    int32_t srow = 0;
     constexpr int kQVec = kTcRows * D * 2 / 16;  // 16-byte vectors of a query block
     constexpr int kQPerLane = (kQVec + 31) / 32;
     auto load_next = [&](int32_t w, int4 d) {
       Unit u = unit_from(a, w, d);
       const int32_t np = u.p_end - u.p_begin;
+      srow = (w < total && u.nsplit > 1) ? a.seq_off[u.b] + u.s : 0;
 #pragma unroll
       for (int i = 0; i < kBtRegs; ++i) {
         const int32_t pi = lane + 32 * i;
@@ -653,6 +660,16 @@ decode_tc_kernel(DecodeArgs a) {
         qr[i] = x;
       }
     };
+    const int32_t c = (int32_t)blockIdx.x;
+    // unit of round r (increasing in r, so the first one >= total ends the list)
+    auto unit_at = [&](int32_t r) -> int32_t {
+      const int64_t w = (int64_t)r * G + ((r & 1) ? G - 1 - c : c);
+      return w < total ? (int32_t)w : total;
+    };
+    int32_t round = 0;
+    int32_t w1 = unit_at(0), w2 = unit_at(1);
+    int4 d1 = w1 < total ? a.items[w1 / a.upi] : none;
+    int4 d2 = w2 < total ? a.items[w2 / a.upi] : none;
     load_next(w1, d1);
 
     int32_t kcount[NW];
@@ -664,6 +681,7 @@ decode_tc_kernel(DecodeArgs a) {
       const Unit u = unit_from(a, w1, d1);
       const int32_t npages = u.p_end - u.p_begin;
       const int qs = nunit % QS;
+      const int32_t split_row = srow;
       // (1) the unit's block-table entries and query rows -> smem
       if (nunit >= QS) {
         if (!mbar_wait_backoff(&qempty[qs], ((nunit / QS) - 1) & 1)) {
@@ -692,11 +710,11 @@ decode_tc_kernel(DecodeArgs a) {
         }
       }
       __syncwarp();
-      // (2) prefetch the next unit; fetch the unit after the one after
+      // (2) prefetch: the next unit's block-table entries and query rows, the
+      //     descriptor of the one after
       load_next(w2, d2);
-      const int32_t w3 = __shfl_sync(FULL, fetched, 0);
+      const int32_t w3 = unit_at(round + 2);
       const int4 d3 = w3 < total ? a.items[w3 / a.upi] : none;
-      if (lane == 0 && w3 < total) fetched = atomicAdd(&a.sched[0], 1);
       // (3) publish the unit's pages to the consumer warps (page p -> warp p % NW);
       //     each consumer loads its pages itself with cp.async
       if (lane == 0 && ok) {
@@ -731,6 +749,8 @@ decode_tc_kernel(DecodeArgs a) {
             md.gcount = u.gcount;
             md.qh0 = u.qh0;
             md.page = page;
+            md.split_row = split_row;
+            md.pad[0] = md.pad[1] = 0;
             meta[slot] = md;
             mbar_arrive(&full[slot]);
           }
@@ -739,20 +759,11 @@ decode_tc_kernel(DecodeArgs a) {
       ok = __shfl_sync(FULL, ok ? 1 : 0, 0) != 0;
       __syncwarp();  // btbuf / qbuf are rewritten for the next unit
       ++nunit;
+      ++round;
       w1 = w2;
       d1 = d2;
       w2 = w3;
       d2 = d3;
-    }
-    if (lane == 0) {
-      // This CTA will fetch no more units. The last CTA to get here resets the
-      // scheduling counters so the plan can drive the next launch.
-      __threadfence();
-      const int done = atomicAdd(&a.sched[1], 1);
-      if (done == (int)gridDim.x - 1) {
-        atomicExch(&a.sched[0], 0);
-        atomicExch(&a.sched[1], 0);
-      }
     }
     if (lane == 0 && ok) {
 #pragma unroll
@@ -876,6 +887,7 @@ decode_tc_kernel(DecodeArgs a) {
       md.hg = m2v.y;
       md.gcount = m2v.z;
       md.qh0 = m2v.w;
+      md.split_row = meta[ms].split_row;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[ms]);  // metadata copied: the producer may reuse the entry
@@ -1035,11 +1047,60 @@ decode_tc_kernel(DecodeArgs a) {
         cp_async_wait_all();
         return;
       }
-      const float *xo_w[NW];
+      // ---- combine the NW warps' states (same arithmetic as unit_epilogue):
+      // thread t owns query row g = t / (D/4) and columns 4c..4c+3, c = t % (D/4),
+      // so the exchange reads and the output stores are 16 bytes wide and a
+      // row's scale factors are computed once per thread for four columns
+      {
+        constexpr int kC4 = D / 4;
+        constexpr int kRowsPerPass = NW * 32 / kC4;
+        const int c4 = tid % kC4;
+        const float *xw[NW];  // each warp's exchange rows
 #pragma unroll
-      for (int w = 0; w < NW; ++w)
-        xo_w[w] = reinterpret_cast<const float *>(tiles + (size_t)xslot[w] * Sh::kSlot);
-      if (!unit_epilogue(a, u, NW, xr, xm, xl, xo_w, xd, tid, NW * 32, sync)) {
+        for (int w = 0; w < NW; ++w)
+          xw[w] = reinterpret_cast<const float *>(tiles + (size_t)xslot[w] * Sh::kSlot) + 4 * c4;
+        for (int g = tid / kC4; g < u.gcount; g += kRowsPerPass) {
+          float M = -INFINITY;
+#pragma unroll
+          for (int w = 0; w < NW; ++w) M = fmaxf(M, xm[w * xr + g]);
+          float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+          float Ls = 0.f;
+          if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < NW; ++w) {
+              const float f = exp2_or_zero(xm[w * xr + g] - M);
+              Ls += f * xl[w * xr + g];
+              const float4 x = *reinterpret_cast<const float4 *>(xw[w] + g * xd);
+              O.x += f * x.x;
+              O.y += f * x.y;
+              O.z += f * x.z;
+              O.w += f * x.w;
+            }
+          }
+          if (u.nsplit == 1) {
+            const float inv = 1.f / fmaxf(Ls, 1e-6f);
+            const float4 r = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
+            float *op = a.out + u.b * a.o0 + (int64_t)(u.qh0 + g) * a.o1;
+            if (a.out_vec) {
+              *reinterpret_cast<float4 *>(op + 4 * c4) = r;
+            } else {
+              op[(4 * c4 + 0) * a.o2] = r.x;
+              op[(4 * c4 + 1) * a.o2] = r.y;
+              op[(4 * c4 + 2) * a.o2] = r.z;
+              op[(4 * c4 + 3) * a.o2] = r.w;
+            }
+          } else {  // merged by merge_kernel after the launch
+            float *part = a.partials +
+                          ((int64_t)md.split_row * a.upi + u.kvh * a.HG + u.hg) * a.part_floats;
+            *reinterpret_cast<float4 *>(part + a.part_o + g * D + 4 * c4) = O;
+            if (c4 == 0) {
+              part[g] = M;
+              part[a.GR + g] = Ls;
+            }
+          }
+        }
+      }
+      if (!sync()) {
         cp_async_wait_all();
         return;
       }
@@ -1325,6 +1386,7 @@ extern "C" int pkv_decode_run(const void *q, const void *k_cache, const void *v_
   a.max_blocks = max_blocks;
   a.P = P;
   a.upi = w.units_per_item;
+  a.part_o = w.part_o;
   a.part_floats = w.part_floats;
   a.q_dtype = q_dtype;
   a.kv_dtype = kv_dtype;
@@ -1333,13 +1395,13 @@ extern "C" int pkv_decode_run(const void *q, const void *k_cache, const void *v_
   a.c0 = cache_strides[0]; a.c1 = cache_strides[1]; a.c2 = cache_strides[2]; a.c3 = cache_strides[3];
   a.bt0 = bt_strides[0]; a.bt1 = bt_strides[1];
   a.o0 = out_strides[0]; a.o1 = out_strides[1]; a.o2 = out_strides[2];
+  a.out_vec = (a.o2 == 1 && a.o0 % 4 == 0 && a.o1 % 4 == 0 && aligned_to(out, 16)) ? 1 : 0;
   a.scale = scale;
   a.scale_log2 = scale * kLog2e;
   a.hdr = reinterpret_cast<const int32_t *>(ws + w.hdr);
   a.seq_off = reinterpret_cast<const int32_t *>(ws + w.seq_off);
   a.seq_nsplit = reinterpret_cast<const int32_t *>(ws + w.seq_nsplit);
   a.items = reinterpret_cast<const int4 *>(ws + w.items);
-  a.sched = reinterpret_cast<int32_t *>(ws + w.hdr) + 4;
   a.partials = reinterpret_cast<float *>(ws + w.partials);
   a.status = status;
   const int64_t max_units = w.max_items * w.units_per_item;
