@@ -296,11 +296,17 @@ def run_ours(args, rank, world, local):
         ws["buf"] = plan.workspace
         for layer in range(L):
             kc, vc = wl.k_pool[layer], wl.v_pool[layer]
-            pkv.paged_kv_append(wl.k_new[layer], wl.v_new[layer], kc, vc, wl.block_tables, wl.ctx_pre)
+            if args.separate_append:
+                pkv.paged_kv_append(wl.k_new[layer], wl.v_new[layer], kc, vc, wl.block_tables, wl.ctx_pre)
             if ev_pairs is not None:
                 ev_pairs[layer][0].record()
-            pkv.paged_attention_decode(wl.q[layer], kc, vc, wl.block_tables, wl.ctx, out=wl.out[layer], plan=plan,
-                                       exact=args.exact)
+            if args.separate_append:
+                pkv.paged_attention_decode(wl.q[layer], kc, vc, wl.block_tables, wl.ctx, out=wl.out[layer],
+                                           plan=plan, exact=args.exact)
+            else:  # one launch: append the token at ctx - 1 and attend over ctx
+                pkv.paged_attention_decode(wl.q[layer], kc, vc, wl.block_tables, wl.ctx, out=wl.out[layer],
+                                           plan=plan, exact=args.exact, k_new=wl.k_new[layer],
+                                           v_new=wl.v_new[layer])
             if ev_pairs is not None:
                 ev_pairs[layer][1].record()
         return plan
@@ -355,10 +361,10 @@ def run_ours(args, rank, world, local):
     kv_gbs = total_kv / (ms_per_step / 1e3) / 1e9
 
     peak, peak_kind = measured_peaks()
-    dec_bytes = wl.decode_bytes_layer()
+    dec_bytes = wl.decode_bytes_layer() + (0 if args.separate_append else wl.append_bytes_layer())
     achieved = dec_bytes / (decode_avg_ms / 1e3) / 1e9
     merges = 1 if wl.max_blocks > plan_pps(wl, args) else 0  # split-K merge launch per layer
-    launches = args.steps * (1 + (2 + merges) * L)
+    launches = args.steps * (1 + ((2 if args.separate_append else 1) + merges) * L)
 
     # ---- end-to-end through the public ops with pinned host buffers
     e2e = None
@@ -393,7 +399,8 @@ def run_ours(args, rank, world, local):
                 "head_dim": wl.d,
                 "block_size": wl.bs,
                 "pages_per_split": plan_pps(wl, args),
-                "step": "per layer: append 1 token/seq/kv-head + paged decode attention; 1 plan per step",
+                "step": ("per layer: append 1 token/seq/kv-head + paged decode attention; 1 plan per step"
+                         + ("" if args.separate_append else " (append fused into the decode launch)")),
                 "launch": (f"the {args.steps} timed steps captured as one CUDA graph, replayed once (after "
                            f"{args.warmup} eager warm-up steps and one untimed replay)" if args.graph else
                            "eager launches from Python"),
@@ -404,7 +411,8 @@ def run_ours(args, rank, world, local):
             "kv_read_GBps": round(kv_gbs, 1),
             "kv_read_GBps_per_gpu": round(kv_gbs / world, 1),
             "roofline": {
-                "kernel": "decode_tc_kernel (one launch = one layer of all sequences)",
+                "kernel": ("decode_tc_kernel (one launch = one layer of all sequences"
+                           + (")" if args.separate_append else ", append included)")),
                 "bound": "hbm",
                 "achieved": round(achieved, 1),
                 "peak": peak,
@@ -493,7 +501,7 @@ def run_e2e(args, wl, world, device):
                 h2d[layer].record(copy)
         comp.wait_event(ctx_ready[buf])
         ctx = ctx_d[buf]
-        ctx_pre = ctx - 1
+        ctx_pre = ctx - 1 if args.separate_append else None
         plan = ops.plan_decode(ctx, wl.hq, wl.hkv, wl.d, wl.bs, wl.max_blocks, pages_per_split=args.pages_per_split,
                                workspace=state["ws"])
         state["ws"] = plan.workspace
@@ -502,9 +510,13 @@ def run_e2e(args, wl, world, device):
             if not first:
                 comp.wait_event(d2h[layer])  # previous step's output left the device
             kc, vc = wl.k_pool[layer], wl.v_pool[layer]
-            pkv.paged_kv_append(kn_d[layer], vn_d[layer], kc, vc, wl.block_tables, ctx_pre)
-            pkv.paged_attention_decode(q_d[layer], kc, vc, wl.block_tables, ctx, out=out_d[layer], plan=plan,
-                                       exact=args.exact)
+            if args.separate_append:
+                pkv.paged_kv_append(kn_d[layer], vn_d[layer], kc, vc, wl.block_tables, ctx_pre)
+                pkv.paged_attention_decode(q_d[layer], kc, vc, wl.block_tables, ctx, out=out_d[layer], plan=plan,
+                                           exact=args.exact)
+            else:
+                pkv.paged_attention_decode(q_d[layer], kc, vc, wl.block_tables, ctx, out=out_d[layer], plan=plan,
+                                           exact=args.exact, k_new=kn_d[layer], v_new=vn_d[layer])
             done[layer].record(comp)
             with torch.cuda.stream(copy):
                 copy.wait_event(done[layer])
@@ -555,7 +567,9 @@ def run_e2e(args, wl, world, device):
         "h2d_bytes_per_step": int(h2d_bytes),
         "d2h_bytes_per_step": int(out_h.numel() * 4),
         "ms_per_step": round(ms, 4),
-        "api": "grpo_training_engine_b200.paged_kv_append + paged_attention_decode (C ABI pkv_append / pkv_decode_run)",
+        "api": ("grpo_training_engine_b200.paged_kv_append + paged_attention_decode (C ABI pkv_append / "
+                "pkv_decode_run)" if args.separate_append else
+                "grpo_training_engine_b200.paged_attention_decode(k_new=, v_new=) (C ABI pkv_append_decode_run)"),
         "launch": ("the timed steps' copies and calls captured as one CUDA graph on two streams"
                    if graph is not None else "eager launches from Python on two streams"),
         "output_matches_device_run": bool(ok),
@@ -732,6 +746,8 @@ def main():
     ap.add_argument("--exact", action="store_true", help="decode with PKV_DECODE_EXACT_P")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="launch every kernel from Python instead of replaying a CUDA graph of the timed steps")
+    ap.add_argument("--separate-append", action="store_true",
+                    help="append with its own launch (pkv_append) instead of inside the decode launch")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)

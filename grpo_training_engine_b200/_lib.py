@@ -15,6 +15,8 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libpkv.so"
 
+ABI_VERSION = 2  # PKV_ABI_VERSION in include/pkv.h
+
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
 DTYPE_F16 = 2
@@ -66,6 +68,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
          _i64p, _i64p, _i64p, _i64p, _i32, _i32, C.c_float, _i32, _i32, _vp, _sz, _vp, _vp],
     ),
+    "pkv_append_decode_run": (
+        C.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
+         _i64p, _i64p, _i64p, _i64p, _i64p, _i32, _i32, C.c_float, _i32, _i32, _vp, _sz, _vp, _vp],
+    ),
     "pkv_decode": (
         C.c_int,
         [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
@@ -115,6 +122,9 @@ def load() -> C.CDLL:
                               "`python grpo_training_engine_b200/build.py`") from exc
         fn.restype = res
         fn.argtypes = args
+    if lib.pkv_abi_version() != ABI_VERSION:
+        raise ImportError(f"{path} has ABI {lib.pkv_abi_version()}, this package needs {ABI_VERSION}: "
+                          "rebuild it with `python grpo_training_engine_b200/build.py`")
     _LIB = lib
     return lib
 

@@ -18,6 +18,15 @@ namespace pkv {
 // ---------------------------------------------------------------------------
 void set_error_detail(const char *fmt, ...);
 
+// Launches the append kernel (pkv_copy.cu): writes k_new/v_new[b] at slot
+// context_lens[b] + ctx_offset of sequence b.
+int append_launch(const void *k_new, const void *v_new, void *k_cache, void *v_cache,
+                  const int32_t *block_tables, const int32_t *context_lens, int32_t ctx_offset,
+                  int32_t batch, int32_t num_heads, int32_t head_dim, int32_t block_size,
+                  int32_t num_blocks, int32_t max_blocks, const int64_t *new_strides,
+                  const int64_t *cache_strides, const int64_t *bt_strides, int32_t dtype,
+                  int32_t *status, void *stream);
+
 inline int check_launch(const char *what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {

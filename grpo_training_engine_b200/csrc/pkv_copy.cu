@@ -40,6 +40,7 @@ struct CopyGeom {
   int64_t s0, s1, s2, s3;  // dense-side strides (vector units) [B,H,(T),D]
   int64_t c0, c1, c2, c3;  // cache strides (vector units)
   int64_t bt0, bt1;        // block-table strides (elements)
+  int32_t ctx_offset;      // append: slot = context_lens[b] + ctx_offset (0: pre-append lengths)
 };
 
 // Looks up the page of position `pos` of sequence b; -1 if out of range.
@@ -69,7 +70,9 @@ append_kernel(const V *__restrict__ k_new, const V *__restrict__ v_new, V *__res
     const int64_t row = i / g.chunks;
     const int32_t h = (int32_t)(row % g.heads);
     const int32_t b = (int32_t)(row / g.heads);
-    const int32_t pos = ctx[b];
+    // with post-append lengths (ctx_offset -1) an empty sequence has no new token
+    if (g.ctx_offset < 0 && ctx[b] <= 0) continue;
+    const int32_t pos = ctx[b] + g.ctx_offset;
     const int32_t page = page_of(bt, g, b, pos, status, c == 0);
     if (page < 0) continue;
     const int64_t dst = page * g.c0 + h * g.c1 + (int64_t)(pos % g.block_size) * g.c2 + c * g.c3;
@@ -216,12 +219,16 @@ extern "C" const char *pkv_error_string(int status) {
 
 extern "C" const char *pkv_last_error_detail(void) { return g_detail; }
 
-extern "C" int pkv_append(const void *k_new, const void *v_new, void *k_cache, void *v_cache,
-                          const int32_t *block_tables, const int32_t *context_lens,
-                          int32_t batch, int32_t num_heads, int32_t head_dim, int32_t block_size,
-                          int32_t num_blocks, int32_t max_blocks, const int64_t *new_strides,
-                          const int64_t *cache_strides, const int64_t *bt_strides, int32_t dtype,
-                          int32_t *status, void *stream) {
+namespace pkv {
+
+// Append launcher shared by pkv_append (slot = pre-append length, ctx_offset 0)
+// and the fused append + decode fallback (post-append lengths, ctx_offset -1).
+int append_launch(const void *k_new, const void *v_new, void *k_cache, void *v_cache,
+                  const int32_t *block_tables, const int32_t *context_lens, int32_t ctx_offset,
+                  int32_t batch, int32_t num_heads, int32_t head_dim, int32_t block_size,
+                  int32_t num_blocks, int32_t max_blocks, const int64_t *new_strides,
+                  const int64_t *cache_strides, const int64_t *bt_strides, int32_t dtype,
+                  int32_t *status, void *stream) {
   int rc = check_common(dtype, batch, num_heads, head_dim, block_size, num_blocks, max_blocks,
                         cache_strides, bt_strides);
   if (rc) return rc;
@@ -247,6 +254,7 @@ extern "C" int pkv_append(const void *k_new, const void *v_new, void *k_cache, v
   g.block_size = block_size;
   g.num_blocks = num_blocks;
   g.max_blocks = max_blocks;
+  g.ctx_offset = ctx_offset;
   const int64_t e = vp.elems_per_vec;
   g.s0 = new_strides[0] / e; g.s1 = new_strides[1] / e; g.s2 = 0; g.s3 = vp.vec_bytes == 16 ? 1 : new_strides[2];
   g.c0 = cache_strides[0] / e; g.c1 = cache_strides[1] / e; g.c2 = cache_strides[2] / e;
@@ -272,6 +280,19 @@ extern "C" int pkv_append(const void *k_new, const void *v_new, void *k_cache, v
       break;
   }
   return check_launch("pkv_append");
+}
+
+}  // namespace pkv
+
+extern "C" int pkv_append(const void *k_new, const void *v_new, void *k_cache, void *v_cache,
+                          const int32_t *block_tables, const int32_t *context_lens,
+                          int32_t batch, int32_t num_heads, int32_t head_dim, int32_t block_size,
+                          int32_t num_blocks, int32_t max_blocks, const int64_t *new_strides,
+                          const int64_t *cache_strides, const int64_t *bt_strides, int32_t dtype,
+                          int32_t *status, void *stream) {
+  return pkv::append_launch(k_new, v_new, k_cache, v_cache, block_tables, context_lens, 0, batch,
+                            num_heads, head_dim, block_size, num_blocks, max_blocks, new_strides,
+                            cache_strides, bt_strides, dtype, status, stream);
 }
 
 extern "C" int pkv_append_prompt(const void *k_src, const void *v_src, void *k_cache,

@@ -119,6 +119,11 @@ struct DecodeArgs {
   const int4 *items;  // per item {b, split, clamped ctx, splits of b}
   float *partials;
   int32_t *status;
+  // fused append (tensor-core kernel): the new token of sequence b, written at
+  // position context_lens[b] - 1; kn == nullptr when there is none
+  const void *kn;
+  const void *vn;
+  int64_t n0, n1;  // k_new / v_new strides [B, Hkv, D] (elements; D contiguous)
 };
 
 struct Unit {
@@ -500,8 +505,9 @@ struct __align__(16) SlotMeta {
   int32_t b, s, nsplit;
   int32_t kvh, hg, gcount, qh0;
   int32_t page;       // physical page id (kElemPage only)
+  int32_t newrow;     // row of this page that takes the appended token, or -1
   int32_t split_row;  // seq_off[b] + s: the unit's partial-result row (nsplit > 1)
-  int32_t pad[2];
+  int32_t pad;
 };
 
 static_assert(sizeof(SlotMeta) == 64, "SlotMeta layout");
@@ -519,7 +525,8 @@ template <int D> struct TcShape {
   static constexpr int kKSteps = D / 16;
   static constexpr int kNTiles = D / 8;
   static constexpr int kQRow = D * 2 + 16;    // padded query row (bytes): conflict-free ldmatrix
-  static constexpr int kQSlot = kTcRows * kQRow;
+  static constexpr int kQNew = kTcRows * kQRow;  // then the appended token's K row and V row
+  static constexpr int kQSlot = kQNew + 2 * D * 2;
 };
 
 // Shared-memory plan of the kernel: per consumer warp a ring of S data slots
@@ -626,12 +633,19 @@ decode_tc_kernel(DecodeArgs a) {
     int32_t btr[kBtRegs];
     uint4 qr[(kTcRows * D * 2 / 16 + 31) / 32];
     int32_t srow = 0;
+    uint4 nkv = make_uint4(0, 0, 0, 0);  // appended token: lane < D/8 a K chunk, then V chunks
+    constexpr int kRowChunks = D / 8;    // 16-byte chunks of one K or V row
     constexpr int kQVec = kTcRows * D * 2 / 16;  // 16-byte vectors of a query block
     constexpr int kQPerLane = (kQVec + 31) / 32;
     auto load_next = [&](int32_t w, int4 d) {
       Unit u = unit_from(a, w, d);
       const int32_t np = u.p_end - u.p_begin;
       srow = (w < total && u.nsplit > 1) ? a.seq_off[u.b] + u.s : 0;
+      if (a.kn != nullptr && w < total && u.s == u.nsplit - 1 && u.ctx > 0 && lane < 2 * kRowChunks) {
+        const int which = lane / kRowChunks, cc = lane % kRowChunks;
+        const uint8_t *src = reinterpret_cast<const uint8_t *>(which ? a.vn : a.kn);
+        nkv = *reinterpret_cast<const uint4 *>(src + (u.b * a.n0 + (int64_t)u.kvh * a.n1) * 2 + 16 * cc);
+      }
 #pragma unroll
       for (int i = 0; i < kBtRegs; ++i) {
         const int32_t pi = lane + 32 * i;
@@ -709,7 +723,24 @@ decode_tc_kernel(DecodeArgs a) {
           *reinterpret_cast<uint4 *>(qbuf + qs * Sh::kQSlot + r * Sh::kQRow + 16 * c) = qr[i];
         }
       }
+      // fused append: this unit holds the sequence's last page (its last split)
+      const bool app = a.kn != nullptr && u.s == u.nsplit - 1 && u.ctx > 0;
+      const int32_t app_pi = app ? (u.ctx - 1) / kBoxRows - u.p_begin : -1;  // page within the unit
+      const int32_t app_row = (u.ctx - 1) % kBoxRows;
+      if (app && lane < 2 * kRowChunks)
+        *reinterpret_cast<uint4 *>(qbuf + qs * Sh::kQSlot + Sh::kQNew + 16 * lane) = nkv;
       __syncwarp();
+      if (app && u.hg == 0 && lane < 2 * kRowChunks) {
+        // one unit per (sequence, kv head) writes the token into the cache for
+        // later steps; every unit reading the page patches its own smem copy
+        const int32_t page = btbuf[app_pi];
+        if (page >= 0) {
+          const int which = lane / kRowChunks, cc = lane % kRowChunks;
+          uint8_t *dst = reinterpret_cast<uint8_t *>(const_cast<void *>(which ? a.vc : a.kc));
+          *reinterpret_cast<uint4 *>(dst + ((int64_t)page * a.c0 + (int64_t)u.kvh * a.c1 +
+                                            (int64_t)app_row * a.c2) * 2 + 16 * cc) = nkv;
+        }
+      }
       // (2) prefetch: the next unit's block-table entries and query rows, the
       //     descriptor of the one after
       load_next(w2, d2);
@@ -749,8 +780,9 @@ decode_tc_kernel(DecodeArgs a) {
             md.gcount = u.gcount;
             md.qh0 = u.qh0;
             md.page = page;
+            md.newrow = (pi == app_pi) ? app_row : -1;
             md.split_row = split_row;
-            md.pad[0] = md.pad[1] = 0;
+            md.pad = 0;
             meta[slot] = md;
             mbar_arrive(&full[slot]);
           }
@@ -812,7 +844,7 @@ decode_tc_kernel(DecodeArgs a) {
   float m1 = -INFINITY, m2 = -INFINITY, l1 = 0.f, l2 = 0.f;
 #pragma unroll
   for (int i = 0; i < Sh::kNTiles; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  int32_t cur_work = -1;
+  int32_t cur_work = -1, cur_qslot = 0;
   const float sl2 = a.scale_log2;
 
   // Each consumer warp loads its own pages: element e's K and V slabs go into
@@ -875,6 +907,9 @@ decode_tc_kernel(DecodeArgs a) {
     md.valid = head.y;
     md.last = head.z;
     md.work = head.w;
+    const int4 tailv = *reinterpret_cast<const int4 *>(&meta[ms].page);  // bytes 48..63
+    md.newrow = tailv.y;
+    md.split_row = tailv.z;
     if (md.last || md.work != cur_work) {
       // 16-byte aligned blocks of SlotMeta: bytes 16..31 and 32..47
       const int4 m1v = *reinterpret_cast<const int4 *>(&meta[ms].qslot);
@@ -887,7 +922,6 @@ decode_tc_kernel(DecodeArgs a) {
       md.hg = m2v.y;
       md.gcount = m2v.z;
       md.qh0 = m2v.w;
-      md.split_row = meta[ms].split_row;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[ms]);  // metadata copied: the producer may reuse the entry
@@ -895,10 +929,24 @@ decode_tc_kernel(DecodeArgs a) {
     const int slot = cw * S + (k % S);
     if (md.work != cur_work) {
       cur_work = md.work;
+      cur_qslot = md.qslot;
       const uint32_t qb = smem_u32(qbuf + md.qslot * Sh::kQSlot) + q_off;
 #pragma unroll
       for (int ks = 0; ks < Sh::kKSteps; ++ks)
         ldsm_x4(qb + ks * 32, qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
+    }
+    if (md.kind == kElemPage && md.newrow >= 0) {
+      // fused append: the page's copy in smem may predate the token (the cache
+      // write happens in whichever CTA owns it, unordered with this copy), so
+      // put the appended K and V rows, staged with the query rows, into the tile
+      constexpr int kRowChunks = D / 8;
+      if (lane < 2 * kRowChunks) {
+        const int which = lane / kRowChunks, cc = lane % kRowChunks;
+        const uint4 v = *reinterpret_cast<const uint4 *>(qbuf + cur_qslot * Sh::kQSlot + Sh::kQNew + 16 * lane);
+        *reinterpret_cast<uint4 *>(tiles + (size_t)slot * Sh::kSlot + which * Sh::kTile +
+                                   slab_chunk_offset<D>(md.newrow * kRowChunks + cc)) = v;
+      }
+      __syncwarp();
     }
 
     if (md.kind == kElemPage) {
@@ -1130,20 +1178,37 @@ int device_sms() {
 }
 
 
+// Default pages per split: the P in {8, 16, ..., 256} with the smallest
+// estimated launch time, assuming every sequence is max_blocks pages long (the
+// host does not see the lengths). With U units on `sms` persistent CTAs the
+// launch takes ceil(U / sms) rounds; a round costs its unit's pages plus a
+// fixed unit overhead (the cross-warp combine and pipeline refill, measured on
+// B200 at about 16 pages' worth of streaming), and any splitting adds the merge
+// launch (about 32 pages' worth). This keeps whole sequences in one unit when
+// there are enough of them to fill the GPU (config 3: 64 pages, 31 us per layer
+// vs 68 us with 8-page splits; config 5: 256 pages, 89% vs 85% of HBM peak
+// with 152) and splits just enough to fill every SM when there are few.
 int32_t resolve_pps(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t max_blocks,
                     int32_t pps) {
   if (pps > 0) return pps < kMaxPagesPerSplit ? pps : kMaxPagesPerSplit;
   const int32_t G = Hq / Hkv;
   const int32_t rows = group_rows_for(G, D);
-  const int64_t units = (int64_t)B * Hkv * ((G + rows - 1) / rows);
-  const int64_t work = units * std::max<int32_t>(max_blocks, 1);
-  // ~24 work units per SM: measured on B200, bigger splits amortise the
-  // per-unit epilogue (config 4: 96 pages 82%, 152 86%, 256 88% of HBM peak)
-  // while dynamic scheduling keeps the tail to about one unit
-  const int64_t target = (int64_t)device_sms() * 24;
-  int64_t P = (work + target - 1) / target;
-  P = std::min<int64_t>(std::max<int64_t>(P, 8), kMaxPagesPerSplit);
-  return (int32_t)std::min<int64_t>((P + 7) / 8 * 8, kMaxPagesPerSplit);
+  const int64_t u0 = std::max<int64_t>(1, (int64_t)B * Hkv * ((G + rows - 1) / rows));
+  const int64_t mb = std::max<int32_t>(max_blocks, 1);
+  const int64_t sms = device_sms();
+  constexpr int64_t kUnitCost = 16, kMergeCost = 32;
+  int64_t best_cost = INT64_MAX;
+  int32_t best = kMaxPagesPerSplit;
+  for (int32_t P = 8; P <= kMaxPagesPerSplit; P += 8) {
+    const int64_t per = (mb + P - 1) / P;
+    const int64_t rounds = (u0 * per + sms - 1) / sms;
+    const int64_t cost = rounds * (std::min<int64_t>(P, mb) + kUnitCost) + (per > 1 ? kMergeCost : 0);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = P;
+    }
+  }
+  return best;
 }
 
 // The tensor-core kernel copies whole (page, head) slabs of 16 x D 16-bit
@@ -1249,6 +1314,8 @@ template <typename T, int D, bool kExactP>
 int launch_tc_x(const DecodeArgs &a, cudaStream_t st, int64_t max_units) {
   constexpr int S = D == 128 ? 3 : 6;
   using L = TcSmem<D, kTcWarps, S>;
+  static_assert(L::kBt + sizeof(int32_t) * kMaxPagesPerSplit + 1024 <= 227 * 1024,
+                "tensor-core decode exceeds the 227 KB of shared memory per CTA");
   const size_t smem = L::bytes(a.P);
   auto kern = decode_tc_kernel<T, D, kTcWarps, S, kExactP>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
@@ -1342,21 +1409,35 @@ extern "C" int pkv_decode_plan(const int32_t *context_lens, int32_t batch, int32
   return check_launch("plan_kernel");
 }
 
-extern "C" int pkv_decode_run(const void *q, const void *k_cache, const void *v_cache,
-                              const int32_t *block_tables, const int32_t *context_lens,
-                              float *out, int32_t batch, int32_t num_q_heads,
-                              int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
-                              int32_t num_blocks, int32_t max_blocks, const int64_t *q_strides,
-                              const int64_t *cache_strides, const int64_t *bt_strides,
-                              const int64_t *out_strides, int32_t q_dtype, int32_t kv_dtype,
-                              float scale, int32_t pages_per_split, int32_t flags,
-                              void *workspace, size_t workspace_bytes, int32_t *status,
-                              void *stream) {
+namespace {
+
+// pkv_decode_run, optionally with the fused append of k_new / v_new (kn != nullptr).
+int decode_run_impl(const void *q, const void *kn, const void *vn, const void *k_cache,
+                    const void *v_cache, const int32_t *block_tables, const int32_t *context_lens,
+                    float *out, int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                    int32_t head_dim, int32_t block_size, int32_t num_blocks, int32_t max_blocks,
+                    const int64_t *q_strides, const int64_t *new_strides,
+                    const int64_t *cache_strides, const int64_t *bt_strides,
+                    const int64_t *out_strides, int32_t q_dtype, int32_t kv_dtype, float scale,
+                    int32_t pages_per_split, int32_t flags, void *workspace,
+                    size_t workspace_bytes, int32_t *status, void *stream) {
   int rc = validate_decode(q, k_cache, v_cache, block_tables, context_lens, out, batch,
                            num_q_heads, num_kv_heads, head_dim, block_size, num_blocks,
                            max_blocks, q_strides, cache_strides, bt_strides, out_strides, q_dtype,
                            kv_dtype);
   if (rc) return rc;
+  if (kn != nullptr || vn != nullptr) {
+    if (new_strides == nullptr) {
+      set_error_detail("new_strides must not be NULL");
+      return PKV_ERR_INVALID_ARG;
+    }
+    if (batch > 0 && (kn == nullptr || vn == nullptr)) {
+      set_error_detail("k_new and v_new must both be given");
+      return PKV_ERR_INVALID_ARG;
+    }
+    if (batch > 0 && (!aligned_to(kn, dtype_size(kv_dtype)) || !aligned_to(vn, dtype_size(kv_dtype))))
+      return PKV_ERR_ALIGNMENT;
+  }
   if (batch == 0) return PKV_OK;
   const int32_t P =
       resolve_pps(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, pages_per_split);
@@ -1406,9 +1487,27 @@ extern "C" int pkv_decode_run(const void *q, const void *k_cache, const void *v_
   a.status = status;
   const int64_t max_units = w.max_items * w.units_per_item;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const bool tc = tc_eligible(k_cache, v_cache, num_q_heads, num_kv_heads, head_dim, block_size,
+                              cache_strides, q_dtype, kv_dtype, flags);
+  if (kn != nullptr) {
+    // the tensor-core kernel takes the new token rows as 16-byte vectors;
+    // anything else appends with the append kernel first (slot = length - 1)
+    if (tc && new_strides[2] == 1 && new_strides[0] % 8 == 0 && new_strides[1] % 8 == 0 &&
+        aligned_to(kn, 16) && aligned_to(vn, 16)) {
+      a.kn = kn;
+      a.vn = vn;
+      a.n0 = new_strides[0];
+      a.n1 = new_strides[1];
+    } else {
+      rc = append_launch(kn, vn, const_cast<void *>(k_cache), const_cast<void *>(v_cache),
+                         block_tables, context_lens, -1, batch, num_kv_heads, head_dim,
+                         block_size, num_blocks, max_blocks, new_strides, cache_strides,
+                         bt_strides, kv_dtype, status, stream);
+      if (rc) return rc;
+    }
+  }
 
-  if (tc_eligible(k_cache, v_cache, num_q_heads, num_kv_heads, head_dim, block_size,
-                  cache_strides, q_dtype, kv_dtype, flags)) {
+  if (tc) {
     if (kv_dtype == PKV_DTYPE_BF16)
       rc = head_dim == 128 ? launch_tc_t<__nv_bfloat16, 128>(a, st, max_units, flags)
                            : launch_tc_t<__nv_bfloat16, 64>(a, st, max_units, flags);
@@ -1433,6 +1532,47 @@ extern "C" int pkv_decode_run(const void *q, const void *k_cache, const void *v_
     rc = check_launch("merge_kernel");
   }
   return rc;
+}
+
+}  // namespace
+
+extern "C" int pkv_decode_run(const void *q, const void *k_cache, const void *v_cache,
+                              const int32_t *block_tables, const int32_t *context_lens,
+                              float *out, int32_t batch, int32_t num_q_heads,
+                              int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                              int32_t num_blocks, int32_t max_blocks, const int64_t *q_strides,
+                              const int64_t *cache_strides, const int64_t *bt_strides,
+                              const int64_t *out_strides, int32_t q_dtype, int32_t kv_dtype,
+                              float scale, int32_t pages_per_split, int32_t flags,
+                              void *workspace, size_t workspace_bytes, int32_t *status,
+                              void *stream) {
+  return decode_run_impl(q, nullptr, nullptr, k_cache, v_cache, block_tables, context_lens, out,
+                         batch, num_q_heads, num_kv_heads, head_dim, block_size, num_blocks,
+                         max_blocks, q_strides, nullptr, cache_strides, bt_strides, out_strides,
+                         q_dtype, kv_dtype, scale, pages_per_split, flags, workspace,
+                         workspace_bytes, status, stream);
+}
+
+extern "C" int pkv_append_decode_run(const void *q, const void *k_new, const void *v_new,
+                                     void *k_cache, void *v_cache, const int32_t *block_tables,
+                                     const int32_t *context_lens, float *out, int32_t batch,
+                                     int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                     int32_t block_size, int32_t num_blocks, int32_t max_blocks,
+                                     const int64_t *q_strides, const int64_t *new_strides,
+                                     const int64_t *cache_strides, const int64_t *bt_strides,
+                                     const int64_t *out_strides, int32_t q_dtype,
+                                     int32_t kv_dtype, float scale, int32_t pages_per_split,
+                                     int32_t flags, void *workspace, size_t workspace_bytes,
+                                     int32_t *status, void *stream) {
+  if (batch > 0 && (k_new == nullptr || v_new == nullptr)) {
+    set_error_detail("pkv_append_decode_run: k_new and v_new must not be NULL");
+    return PKV_ERR_INVALID_ARG;
+  }
+  return decode_run_impl(q, k_new, v_new, k_cache, v_cache, block_tables, context_lens, out,
+                         batch, num_q_heads, num_kv_heads, head_dim, block_size, num_blocks,
+                         max_blocks, q_strides, new_strides, cache_strides, bt_strides,
+                         out_strides, q_dtype, kv_dtype, scale, pages_per_split, flags,
+                         workspace, workspace_bytes, status, stream);
 }
 
 extern "C" int pkv_decode(const void *q, const void *k_cache, const void *v_cache,

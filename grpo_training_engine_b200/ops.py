@@ -325,6 +325,8 @@ def paged_attention_decode(
     force_generic: bool = False,
     exact: bool = False,
     status: Optional[torch.Tensor] = None,
+    k_new: Optional[torch.Tensor] = None,
+    v_new: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
     """Single-query attention over the paged cache; returns fp32 [B, Hq, D].
 
@@ -339,6 +341,12 @@ def paged_attention_decode(
     (max-abs error a few 1e-3 for N(0,1) data); exact=True keeps ~17
     significant bits of the weights at some speed cost. The CUDA-core kernel
     (fp32 caches, force_generic=True) is fp32 throughout.
+
+    With k_new / v_new ([B, Hkv, D], cache dtype) the call is one decode step
+    of a layer including the append: the new token is written at position
+    context_lens[b] - 1 (context_lens stay POST-append) and attended to, in
+    a single launch on the tensor-core kernel (C ABI pkv_append_decode_run).
+    It writes the cache bytes paged_kv_append(..., context_lens - 1) writes.
     """
     _check_cache_pair(k_cache, v_cache)
     if q.ndim != 3:
@@ -367,6 +375,30 @@ def paged_attention_decode(
     lib = _lib.load()
     ws = plan.workspace
     flags = (_lib.DECODE_FORCE_GENERIC if force_generic else 0) | (_lib.DECODE_EXACT_P if exact else 0)
+    if k_new is not None or v_new is not None:
+        if k_new is None or v_new is None:
+            raise ValueError("k_new and v_new must be given together.")
+        if k_new.ndim != 3 or k_new.shape != v_new.shape or tuple(k_new.shape) != (batch, hkv, head_dim):
+            raise ValueError(f"k_new/v_new must be matching [batch, num_kv_heads, head_dim] = "
+                             f"{(batch, hkv, head_dim)} tensors.")
+        if k_new.stride() != v_new.stride():
+            raise ValueError("k_new and v_new must have identical strides.")
+        if k_new.dtype != k_cache.dtype or v_new.dtype != k_cache.dtype:
+            raise ValueError("k_new/v_new must have the cache dtype.")
+        _require_cuda(k_new, v_new, k_cache)
+        with torch.cuda.device(dev):
+            _lib.check(
+                "pkv_append_decode_run",
+                lib.pkv_append_decode_run(
+                    q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                    bt.data_ptr(), plan.context_lens.data_ptr(), out.data_ptr(), batch, hq, hkv, head_dim,
+                    block_size, num_blocks, max_blocks, _lib.i64_array(q.stride()), _lib.i64_array(k_new.stride()),
+                    _lib.i64_array(k_cache.stride()), _lib.i64_array(bt.stride()), _lib.i64_array(out.stride()),
+                    _dtype_code(q, "q"), _dtype_code(k_cache, "k_cache"), float(scale), plan.pages_per_split,
+                    flags, ws.data_ptr(), ws.numel() * ws.element_size(), _status_ptr(status), _stream(dev),
+                ),
+            )
+        return out
     with torch.cuda.device(dev):
         _lib.check(
             "pkv_decode_run",

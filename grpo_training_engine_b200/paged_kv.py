@@ -340,9 +340,9 @@ def paged_kv_decode_model(
             k1 = k[:, :, 0, :].to(torch.bfloat16).contiguous()
             v1 = v[:, :, 0, :].to(torch.bfloat16).contiguous()
             k_cache, v_cache = pool.layer(layer_idx)
-            ops.paged_kv_append(k1, v1, k_cache, v_cache, block_tables, context_lens)
+            # append at context_lens and attend over new_context_lens: one fused call
             attn_out = ops.paged_attention_decode(q1, k_cache, v_cache, block_tables, new_context_lens,
-                                                  scale=scale, plan=plan)
+                                                  scale=scale, plan=plan, k_new=k1, v_new=v1)
             attn_out = attn_out.to(hidden.dtype).reshape(batch_size, 1, num_heads * head_dim)
             hidden = residual + attn.o_proj(attn_out)
             residual = hidden

@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define PKV_ABI_VERSION 1
+#define PKV_ABI_VERSION 2  /* 2: pkv_append_decode_run */
 
 /* Element types. The reference stores the cache in bfloat16
  * (paged_kv.py:409-410, 629-633); float32 is accepted because the reference
@@ -156,9 +156,10 @@ int pkv_gather(const void *k_cache, const void *v_cache,
  * grouped-query layout (one cache head serves G consecutive query heads).
  *
  * Long contexts are split into chunks of pages_per_split pages; partial
- * (max, sum, acc) triples go to the caller's workspace and are merged by
- * the last chunk to finish. pages_per_split == 0 selects the library's
- * heuristic for the current device.
+ * (max, sum, acc) triples go to the caller's workspace and a merge kernel,
+ * launched on the same stream, combines them in chunk order.
+ * pages_per_split == 0 selects the library's heuristic for the current
+ * device.
  *
  * pkv_decode = pkv_decode_plan + pkv_decode_run. The plan depends only on
  * context_lens (and the sizes), so a caller that runs many layers with the
@@ -188,6 +189,33 @@ int pkv_decode_run(const void *q, const void *k_cache, const void *v_cache,
                    int32_t q_dtype, int32_t kv_dtype, float scale,
                    int32_t pages_per_split, int32_t flags, void *workspace,
                    size_t workspace_bytes, int32_t *status, void *stream);
+
+/*
+ * pkv_append_decode_run: one decode step of one layer, the append included.
+ * Writes k_new[b] / v_new[b] ([batch, num_kv_heads, head_dim], cache dtype)
+ * into the cache at position context_lens[b] - 1, then decodes exactly as
+ * pkv_decode_run over context_lens[b] positions (POST-append lengths; a
+ * sequence of length 0 appends nothing). The pair it replaces is the
+ * reference's per-layer _paged_kv_update_kernel launch with the pre-append
+ * lengths followed by _paged_attention_decode_kernel with the post-append
+ * ones (src/triton_kernels/paged_kv.py:730-783). On the tensor-core kernel
+ * (and D-contiguous, 16-byte aligned k_new / v_new rows) this is one launch:
+ * the kernel writes the token into its page and uses it in the same pass;
+ * otherwise the append kernel runs first on the same stream. The cache
+ * bytes written are those pkv_append would write.
+ */
+int pkv_append_decode_run(const void *q, const void *k_new, const void *v_new,
+                          void *k_cache, void *v_cache,
+                          const int32_t *block_tables, const int32_t *context_lens,
+                          float *out, int32_t batch, int32_t num_q_heads,
+                          int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                          int32_t num_blocks, int32_t max_blocks,
+                          const int64_t *q_strides, const int64_t *new_strides,
+                          const int64_t *cache_strides, const int64_t *bt_strides,
+                          const int64_t *out_strides, int32_t q_dtype, int32_t kv_dtype,
+                          float scale, int32_t pages_per_split, int32_t flags,
+                          void *workspace, size_t workspace_bytes, int32_t *status,
+                          void *stream);
 
 int pkv_decode(const void *q, const void *k_cache, const void *v_cache,
                const int32_t *block_tables, const int32_t *context_lens,

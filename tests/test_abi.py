@@ -22,7 +22,7 @@ def _declared() -> set[str]:
 
 def test_library_loads():
     lib = _lib.load()
-    assert lib.pkv_abi_version() == 1
+    assert lib.pkv_abi_version() == _lib.ABI_VERSION == 2
 
 
 def test_every_declared_symbol_is_exported():
@@ -74,6 +74,7 @@ def test_decode_checks_and_workspace_query():
     assert lib.pkv_decode_pages_per_split(4, 12, 2, 128, 32, 16) == 16
     p = lib.pkv_decode_pages_per_split(1024, 12, 2, 128, 513, 0)
     assert 8 <= p <= 256 and p % 8 == 0
+
     # plan without a workspace is refused before any launch
     rc = lib.pkv_decode_plan(None, 4, 12, 2, 128, 16, 32, 0, None, 0, None, None)
     assert rc == _lib.ERR_WORKSPACE
@@ -82,6 +83,17 @@ def test_decode_checks_and_workspace_query():
                         1, 1, 0.1, 0, 0, None, 0, None, None)
     assert rc == _lib.ERR_INVALID_ARG
     assert "multiple" in _lib.last_detail()
+
+
+def test_default_split_length_cost_model():
+    """Without a GPU the library assumes a B200's 148 SMs."""
+    pps = _lib.load().pkv_decode_pages_per_split
+    assert pps(128, 12, 2, 128, 64, 0) == 64      # config 3: 256 whole sequences fill 148 SMs, no split
+    assert pps(1024, 12, 2, 128, 512, 0) == 256   # config 4: longest splits
+    assert pps(64, 28, 4, 128, 2048, 0) == 256    # config 5
+    p = pps(4, 12, 2, 128, 2048, 0)               # 8 long sequences: split to fill the SMs once
+    assert 8 * -(-2048 // p) <= 148 and 8 * -(-2048 // (p + 8)) < 148 <= 8 * -(-2048 // (p - 8))
+    assert pps(4, 12, 2, 128, 33, 0) >= 33        # short contexts are never split
 
 
 def test_kernel_kind_selection():

@@ -236,6 +236,90 @@ def test_out_of_range_inputs_are_flagged_not_faulted():
     assert torch.equal(before, after)
 
 
+# ------------------------------------------------------- fused append + decode
+FUSED_SHAPES = [
+    # (batch, hq, hkv, head_dim, block_size, dtype, post-append ctxs)
+    (4, 12, 2, 128, 16, torch.bfloat16, [1, 16, 17, 777]),    # token opens / fills / first page
+    (3, 28, 4, 128, 16, torch.bfloat16, [5000, 33, 2048]),     # 7B geometry, long splits
+    (2, 40, 2, 64, 16, torch.float16, [500, 1]),               # two head groups read the page
+    (2, 16, 2, 64, 16, torch.bfloat16, [0, 95]),               # an empty sequence appends nothing
+    (3, 12, 2, 128, 16, torch.float32, [37, 128, 300]),        # fp32: append kernel + CUDA cores
+    (2, 6, 3, 96, 8, torch.bfloat16, [50, 9]),                 # CUDA-core kernel shape
+]
+
+
+def _separate_append_then_decode(q, kn, vn, kc, vc, bt, ctx, **kw):
+    """The reference's per-layer pair: append at the pre-append length, decode over ctx."""
+    live = (ctx > 0).nonzero().flatten()
+    if live.numel():
+        paged_kv_append(kn[live], vn[live], kc, vc, bt[live], (ctx - 1)[live])
+    return paged_attention_decode(q, kc, vc, bt, ctx, **kw)
+
+
+@pytest.mark.parametrize("shape", FUSED_SHAPES, ids=lambda s: f"b{s[0]}q{s[1]}kv{s[2]}d{s[3]}bs{s[4]}")
+@pytest.mark.parametrize("splits", [0, 3])
+def test_fused_append_decode_equals_separate_calls(shape, splits):
+    batch, hq, hkv, d, bs, dtype, ctxs = shape
+    q, kc, vc, bt, ctx = _random_case(21, batch, hq, hkv, d, bs, ctxs, dtype)
+    g = torch.Generator().manual_seed(5)
+    kn = torch.randn(batch, hkv, d, generator=g).to(dtype)
+    vn = torch.randn(batch, hkv, d, generator=g).to(dtype)
+    q, kn, vn, bt, ctx = (t.to(DEV) for t in (q, kn, vn, bt, ctx))
+    kc1, vc1 = kc.to(DEV), vc.to(DEV)
+    kc2, vc2 = kc1.clone(), vc1.clone()
+    out1 = _separate_append_then_decode(q, kn, vn, kc1, vc1, bt, ctx, num_splits=splits)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out2 = paged_attention_decode(q, kc2, vc2, bt, ctx, num_splits=splits, k_new=kn, v_new=vn, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert _sha(kc1, vc1) == _sha(kc2, vc2)  # the same cache bytes
+    assert torch.equal(out1, out2)           # the same tiles in smem, the same arithmetic
+    ref = oracle.decode(q.cpu(), kc1.cpu(), vc1.cpu(), bt.cpu(), ctx.cpu())
+    assert _maxabs(out2, ref) <= ATOL[str(dtype).split(".")[1]]
+
+
+def test_fused_append_decode_with_strided_new_rows_and_plan_reuse():
+    # new rows with a padded head stride (head_dim contiguous) take the one-launch
+    # route, head_dim-strided rows the append-kernel route; one plan, 3 layers
+    batch, hq, hkv, d = 5, 12, 2, 128
+    ctxs = [300, 1, 64, 65, 1000]
+    q, kc, vc, bt, ctx = _random_case(8, batch, hq, hkv, d, 16, ctxs, torch.bfloat16)
+    pool_k = torch.stack([kc, kc.roll(1, 0), kc.roll(2, 0)]).to(DEV)
+    pool_v = torch.stack([vc, vc.roll(3, 0), vc.roll(1, 0)]).to(DEV)
+    g = torch.Generator().manual_seed(9)
+    padded = torch.randn(3, batch, hkv, 2 * d, generator=g).to(torch.bfloat16).to(DEV)[..., :d]
+    strided = torch.randn(3, batch, d, hkv, generator=g).to(torch.bfloat16).to(DEV).transpose(2, 3)
+    q, bt, ctx = q.to(DEV), bt.to(DEV), ctx.to(DEV)
+    plan = plan_decode(ctx, hq, hkv, d, 16, bt.shape[1], pages_per_split=8)
+    for layer in range(3):
+        for new in (padded[layer], strided[layer]):
+            pk, pv = pool_k[layer].clone(), pool_v[layer].clone()
+            out = paged_attention_decode(q, pk, pv, bt, ctx, plan=plan, k_new=new, v_new=new)
+            rk, rv = pool_k[layer].clone(), pool_v[layer].clone()
+            ref = _separate_append_then_decode(q, new.contiguous(), new.contiguous(), rk, rv, bt, ctx,
+                                               pages_per_split=8)
+            assert _sha(pk, pv) == _sha(rk, rv)
+            assert torch.equal(out, ref)
+
+
+def test_fused_append_out_of_range_page_is_flagged_and_skipped():
+    q, kc, vc, bt, ctx = _random_case(3, 3, 12, 2, 128, 16, [40, 17, 5], torch.bfloat16)
+    bad = bt.clone()
+    bad[0, 2] = 10_000  # page of sequence 0's new token (position 39)
+    kn = torch.randn(3, 2, 128).to(torch.bfloat16)
+    kd, vd = kc.to(DEV), vc.to(DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = paged_attention_decode(q.to(DEV), kd, vd, bad.to(DEV), ctx.to(DEV), k_new=kn.to(DEV),
+                                 v_new=kn.to(DEV), status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) & _lib.DEV_PAGE_OUT_OF_RANGE
+    # sequences 1 and 2 got their tokens; sequence 0's bad page is skipped in both cache and decode
+    kc2, vc2 = kc.clone(), vc.clone()
+    oracle.append(kn[1:], kn[1:], kc2, vc2, bad[1:], ctx[1:] - 1)
+    assert _sha(kd, vd) == _sha(kc2, vc2)
+    assert _maxabs(out, oracle.decode(q, kc2, vc2, bad, ctx)) <= 2e-2
+
+
 # ---------------------------------------------------------------- append / gather
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("d", [8, 6, 128])
