@@ -141,6 +141,14 @@ __device__ __forceinline__ bool mbar_wait_backoff(uint64_t *bar, uint32_t parity
 // ---------------------------------------------------------------------------
 // warp-level matrix helpers (bf16 / fp16 operands, fp32 accumulate)
 // ---------------------------------------------------------------------------
+// In-register transpose of an 8x8 matrix of 16-bit values held as m16n8k16
+// fragments (lane 4r + c holds row r, columns 2c and 2c + 1).
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2,
                                         uint32_t &r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"

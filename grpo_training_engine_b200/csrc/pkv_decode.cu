@@ -49,7 +49,7 @@ constexpr int kGenThreads = 128;
 constexpr int kGenWarps = kGenThreads / 32;
 // Block-table entries of a unit held in the tensor-core producer's registers,
 // lane-strided: kBtRegs per lane, so a split has at most kMaxPagesPerSplit pages.
-constexpr int kBtRegs = 8;
+constexpr int kBtRegs = 16;
 constexpr int32_t kMaxPagesPerSplit = kBtRegs * 32;
 
 // ---------------------------------------------------------------------------
@@ -523,7 +523,7 @@ template <int D> struct TcShape {
   static constexpr int kTile = kBoxes * kBoxBytes;  // one K (or V) page of one head
   static constexpr int kSlot = 2 * kTile;           // K + V
   static constexpr int kKSteps = D / 16;
-  static constexpr int kNTiles = D / 8;
+  static constexpr int kMTiles = D / 16;
   static constexpr int kQRow = D * 2 + 16;    // padded query row (bytes): conflict-free ldmatrix
   static constexpr int kQNew = kTcRows * kQRow;  // then the appended token's K row and V row
   static constexpr int kQSlot = kQNew + 2 * D * 2;
@@ -579,9 +579,10 @@ __device__ __forceinline__ void split_pair(float x, float y, uint32_t &hi, uint3
 }
 
 
-template <typename T, int D, int NW, int S, bool kExactP>
+template <typename T, int D, int NW, int S, bool kExactP, int NT>
 __global__ void __launch_bounds__((NW + 1) * 32, 1)
 decode_tc_kernel(DecodeArgs a) {
+  static_assert(NT == 1 || NT == 2, "one or two tiles of 8 query heads");
   using Sh = TcShape<D>;
   using L = TcSmem<D, NW, S>;
   extern __shared__ uint8_t tc_raw[];
@@ -821,29 +822,42 @@ decode_tc_kernel(DecodeArgs a) {
   // =========================== consumer warps ===========================
   using M = Mma16816<T>;
   const int cw = warp;
-  const int r1 = lane >> 2, r2 = r1 + 8, cq = 2 * (lane & 3);
+  // m16n8k16 fragment coordinates: lane = 4 * fr + fq
+  const int fr = lane >> 2, fq = lane & 3;
   GroupSync sync{group, 0u, a.status};
 
-  // per-lane byte offsets inside a swizzled tile (128-byte rows, 16-byte
-  // chunk c of row r stored at chunk c ^ (r % 8)); the remaining parts of the
-  // addresses are compile-time constants
-  const uint32_t c0 = (uint32_t)((lane >> 3) ^ (lane & 7));
-  const uint32_t k_off0 = (lane & 7) * 128 + (c0 << 4);
-  const uint32_t k_off1 = (lane & 7) * 128 + ((c0 ^ 4u) << 4);
-  const uint32_t cv = (uint32_t)((lane >> 4) ^ (lane & 7));
-  const uint32_t v_row = ((lane >> 3) & 1) * 1024 + (lane & 7) * 128;
-  const uint32_t v_off0 = v_row + ((cv ^ 0u) << 4);
-  const uint32_t v_off1 = v_row + ((cv ^ 2u) << 4);
-  const uint32_t v_off2 = v_row + ((cv ^ 4u) << 4);
-  const uint32_t v_off3 = v_row + ((cv ^ 6u) << 4);
-  // query rows: lane -> row (lane % 8) + 8 * ((lane / 8) % 2), column 8 * (lane / 16)
-  const uint32_t q_off = ((lane & 7) + 8 * ((lane >> 3) & 1)) * Sh::kQRow + 16 * (lane >> 4);
-
-  uint32_t qa[Sh::kKSteps][4];
-  float o[Sh::kNTiles][4];
-  float m1 = -INFINITY, m2 = -INFINITY, l1 = 0.f, l2 = 0.f;
+  // A page is processed transposed: S^T = K Q^T (the 16 tokens on M, up to 8
+  // query heads per head tile on N) and O^T = V^T P^T (head_dim on M), so one
+  // page costs 2 * D/16 MMAs per head tile. Per-lane byte offsets inside a
+  // swizzled tile (128-byte rows, 16-byte chunk c of row r stored at chunk
+  // c ^ (r % 8)) for the ldmatrix.x4 of k-step / m-tile j; the box offset
+  // (j / 4) * 2 KB is a compile-time constant:
+  //   K, A operand, plain:      token (lane & 7) + 8 ((lane >> 3) & 1), chunk 2j + (lane >> 4)
+  //   V, A operand, transposed: token (lane & 7) + 8 (lane >> 4),       chunk 2j + ((lane >> 3) & 1)
+  uint32_t k_off[4], v_off[4];
+  {
+    const uint32_t kr = (lane & 7) + 8 * ((lane >> 3) & 1), kh = lane >> 4;
+    const uint32_t vr = (lane & 7) + 8 * (lane >> 4), vh = (lane >> 3) & 1;
 #pragma unroll
-  for (int i = 0; i < Sh::kNTiles; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    for (int j = 0; j < 4; ++j) {
+      k_off[j] = kr * 128 + (((2 * j + kh) ^ (lane & 7)) << 4);
+      v_off[j] = vr * 128 + (((2 * j + vh) ^ (lane & 7)) << 4);
+    }
+  }
+  // query rows, B operand, plain ldmatrix.x4 over two k-steps: head (lane & 7)
+  // (+8 for the second head tile), chunk 2 ks + (lane >> 3)
+  const uint32_t q_off = (lane & 7) * Sh::kQRow + 16 * (lane >> 3);
+
+  uint32_t qb[NT][Sh::kKSteps][2];
+  float o[NT][Sh::kMTiles][4];  // O^T: d = 16 mt + fr (+8), head 8 nt + 2 fq (+1)
+  float m[NT][2], l[NT][2];     // running max and this lane's partial sum, head 8 nt + 2 fq + j
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    m[nt][0] = m[nt][1] = -INFINITY;
+    l[nt][0] = l[nt][1] = 0.f;
+#pragma unroll
+    for (int i = 0; i < Sh::kMTiles; ++i) o[nt][i][0] = o[nt][i][1] = o[nt][i][2] = o[nt][i][3] = 0.f;
+  }
   int32_t cur_work = -1, cur_qslot = 0;
   const float sl2 = a.scale_log2;
 
@@ -930,10 +944,13 @@ decode_tc_kernel(DecodeArgs a) {
     if (md.work != cur_work) {
       cur_work = md.work;
       cur_qslot = md.qslot;
-      const uint32_t qb = smem_u32(qbuf + md.qslot * Sh::kQSlot) + q_off;
+      const uint32_t qs0 = smem_u32(qbuf + md.qslot * Sh::kQSlot) + q_off;
 #pragma unroll
-      for (int ks = 0; ks < Sh::kKSteps; ++ks)
-        ldsm_x4(qb + ks * 32, qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int kp = 0; kp < Sh::kKSteps / 2; ++kp)
+          ldsm_x4(qs0 + nt * 8 * Sh::kQRow + kp * 64, qb[nt][2 * kp][0], qb[nt][2 * kp][1],
+                  qb[nt][2 * kp + 1][0], qb[nt][2 * kp + 1][1]);
     }
     if (md.kind == kElemPage && md.newrow >= 0) {
       // fused append: the page's copy in smem may predate the token (the cache
@@ -952,101 +969,89 @@ decode_tc_kernel(DecodeArgs a) {
     if (md.kind == kElemPage) {
       const uint32_t kt = smem_u32(tiles + (size_t)slot * Sh::kSlot);
       const uint32_t vt = kt + Sh::kTile;
-      const uint32_t kb0 = kt + k_off0, kb1 = kt + k_off1;
-      // ---- S = Q K^T for the 16 tokens of the page (two n-tiles of 8 tokens)
-      float sacc[2][4];
+      // ---- S^T = K Q^T; even and odd k-steps accumulate separately (two
+      // short MMA chains) and are added
+      float st[NT][2][4];
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int kp = 0; kp < Sh::kKSteps / 2; ++kp) {
-          uint32_t b0, b1, b2, b3;
-          const uint32_t base = (kp & 1) ? kb1 : kb0;
-          ldsm_x4(base + nt * 1024 + (kp >> 1) * kBoxBytes, b0, b1, b2, b3);
-          M::run(sacc[nt], qa[2 * kp][0], qa[2 * kp][1], qa[2 * kp][2], qa[2 * kp][3], b0, b1);
-          M::run(sacc[nt], qa[2 * kp + 1][0], qa[2 * kp + 1][1], qa[2 * kp + 1][2],
-                 qa[2 * kp + 1][3], b2, b3);
+        for (int c = 0; c < 2; ++c) st[nt][c][0] = st[nt][c][1] = st[nt][c][2] = st[nt][c][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < Sh::kKSteps; ++ks) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(kt + (ks >> 2) * kBoxBytes + k_off[ks & 3], a0, a1, a2, a3);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+          M::run(st[nt][ks & 1], a0, a1, a2, a3, qb[nt][ks][0], qb[nt][ks][1]);
+      }
+      // ---- online softmax of each head over the page: this lane holds tokens
+      // fr and fr + 8 of heads 2 fq, 2 fq + 1; the 8 lanes with the same fq
+      // hold the other tokens
+      bool moved = false;
+      float al[NT][2];
+      uint32_t pb[NT][2], pbl[NT][2];  // P^T as B fragments: tokens 2 fq (+1), +8; head fr
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        float x[4], p[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const bool in = (i < 2 ? fr : fr + 8) < md.valid;
+          x[i] = in ? (st[nt][0][i] + st[nt][1][i]) * sl2 : -INFINITY;
         }
-      }
-      // ---- online softmax over the page (rows r1, r2; four tokens per lane)
-      float x1[4], x2[4];
-      if (md.valid == kBoxRows) {
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            x1[nt * 2 + j] = sacc[nt][j] * sl2;
-            x2[nt * 2 + j] = sacc[nt][2 + j] * sl2;
-          }
+        for (int j = 0; j < 2; ++j) {
+          float mx = fmaxf(x[j], x[2 + j]);
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+          // a page element has a valid token, so n is finite: masked logits
+          // (-inf) give exp2 = 0 and the first page's alpha is 0
+          const float n = fmaxf(m[nt][j], mx);
+          al[nt][j] = fast_exp2(m[nt][j] - n);
+          p[j] = fast_exp2(x[j] - n);
+          p[2 + j] = fast_exp2(x[2 + j] - n);
+          l[nt][j] = l[nt][j] * al[nt][j] + (p[j] + p[2 + j]);
+          m[nt][j] = n;
+          moved |= al[nt][j] != 1.f;
         }
-      } else {
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const bool in = nt * 8 + cq + j < md.valid;
-            x1[nt * 2 + j] = in ? sacc[nt][j] * sl2 : -INFINITY;
-            x2[nt * 2 + j] = in ? sacc[nt][2 + j] * sl2 : -INFINITY;
-          }
-        }
-      }
-      float mx1 = fmaxf(fmaxf(x1[0], x1[1]), fmaxf(x1[2], x1[3]));
-      float mx2 = fmaxf(fmaxf(x2[0], x2[1]), fmaxf(x2[2], x2[3]));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-      mx2 = fmaxf(mx2, __shfl_xor_sync(0xffffffffu, mx2, 1));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-      mx2 = fmaxf(mx2, __shfl_xor_sync(0xffffffffu, mx2, 2));
-      // A page element has at least one valid token, so n1, n2 are finite:
-      // masked logits (-inf) give exp2 = 0 and the first page's alpha is 0.
-      const float n1 = fmaxf(m1, mx1), n2 = fmaxf(m2, mx2);
-      const float al1 = fast_exp2(m1 - n1);
-      const float al2 = fast_exp2(m2 - n2);
-      float p1[4], p2[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        p1[i] = fast_exp2(x1[i] - n1);
-        p2[i] = fast_exp2(x2[i] - n2);
-      }
-      l1 = l1 * al1 + ((p1[0] + p1[1]) + (p1[2] + p1[3]));
-      l2 = l2 * al2 + ((p2[0] + p2[1]) + (p2[2] + p2[3]));
-      m1 = n1;
-      m2 = n2;
-      // the running max settles after a few pages: rescale only when it moved
-      if (__any_sync(0xffffffffu, (al1 != 1.f) || (al2 != 1.f))) {
-#pragma unroll
-        for (int i = 0; i < Sh::kNTiles; ++i) {
-          o[i][0] *= al1;
-          o[i][1] *= al1;
-          o[i][2] *= al2;
-          o[i][3] *= al2;
-        }
-      }
-      // ---- O += P V, P as the A operand straight from the S fragments, rounded
-      // to 16 bits (relative error <= 2^-9 per weight). With kExactP, P is split
-      // into a 16-bit head and a 16-bit remainder (P = hi + lo) and both are
-      // multiplied, keeping ~17 significant bits of P.
-      uint32_t ph[4], pl[4];
-      if constexpr (kExactP) {
-        split_pair<M>(p1[0], p1[1], ph[0], pl[0]);
-        split_pair<M>(p2[0], p2[1], ph[1], pl[1]);
-        split_pair<M>(p1[2], p1[3], ph[2], pl[2]);
-        split_pair<M>(p2[2], p2[3], ph[3], pl[3]);
-      } else {
-        ph[0] = M::pack(p1[0], p1[1]);
-        ph[1] = M::pack(p2[0], p2[1]);
-        ph[2] = M::pack(p1[2], p1[3]);
-        ph[3] = M::pack(p2[2], p2[3]);
-      }
-#pragma unroll
-      for (int np = 0; np < Sh::kNTiles / 2; ++np) {
-        uint32_t b0, b1, b2, b3;
-        const uint32_t vo = (np & 3) == 0 ? v_off0 : (np & 3) == 1 ? v_off1 : (np & 3) == 2 ? v_off2 : v_off3;
-        ldsm_x4_trans(vt + vo + (np >> 2) * kBoxBytes, b0, b1, b2, b3);
-        M::run(o[2 * np], ph[0], ph[1], ph[2], ph[3], b0, b1);
-        M::run(o[2 * np + 1], ph[0], ph[1], ph[2], ph[3], b2, b3);
+        // P rounded to 16 bits (relative error <= 2^-9 per weight); with
+        // kExactP also the 16-bit remainder (P = hi + lo, ~17 significant
+        // bits). The accumulator rows (tokens fr, fr + 8) become the B
+        // operand's columns by an in-register 8x8 transpose.
         if constexpr (kExactP) {
-          M::run(o[2 * np], pl[0], pl[1], pl[2], pl[3], b0, b1);
-          M::run(o[2 * np + 1], pl[0], pl[1], pl[2], pl[3], b2, b3);
+          uint32_t h0, l0, h1, l1;
+          split_pair<M>(p[0], p[1], h0, l0);
+          split_pair<M>(p[2], p[3], h1, l1);
+          pb[nt][0] = movmatrix_trans(h0);
+          pb[nt][1] = movmatrix_trans(h1);
+          pbl[nt][0] = movmatrix_trans(l0);
+          pbl[nt][1] = movmatrix_trans(l1);
+        } else {
+          pb[nt][0] = movmatrix_trans(M::pack(p[0], p[1]));
+          pb[nt][1] = movmatrix_trans(M::pack(p[2], p[3]));
+        }
+      }
+      // the running max settles after a few pages: rescale only when it moved
+      if (__any_sync(0xffffffffu, moved)) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int mt = 0; mt < Sh::kMTiles; ++mt) {
+            o[nt][mt][0] *= al[nt][0];
+            o[nt][mt][1] *= al[nt][1];
+            o[nt][mt][2] *= al[nt][0];
+            o[nt][mt][3] *= al[nt][1];
+          }
+      }
+      // ---- O^T += V^T P^T, one m-tile per 16 columns of head_dim
+#pragma unroll
+      for (int mt = 0; mt < Sh::kMTiles; ++mt) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_trans(vt + (mt >> 2) * kBoxBytes + v_off[mt & 3], a0, a1, a2, a3);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          M::run(o[nt][mt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+          if constexpr (kExactP) M::run(o[nt][mt], a0, a1, a2, a3, pbl[nt][0], pbl[nt][1]);
         }
       }
     }
@@ -1069,27 +1074,33 @@ decode_tc_kernel(DecodeArgs a) {
       const int xd = (a.GR * (D + 4) * 4 <= Sh::kSlot) ? D + 4 : D;
       float *xo = reinterpret_cast<float *>(tiles + (size_t)slot * Sh::kSlot);
       if (lane == 0) xslot[cw] = slot;
-      float s1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
-      s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-      float s2 = l2 + __shfl_xor_sync(0xffffffffu, l2, 1);
-      s2 += __shfl_xor_sync(0xffffffffu, s2, 2);
-      if ((lane & 3) == 0) {
-        if (r1 < u.gcount) {
-          xm[cw * xr + r1] = m1;
-          xl[cw * xr + r1] = s1;
-        }
-        if (r2 < u.gcount) {
-          xm[cw * xr + r2] = m2;
-          xl[cw * xr + r2] = s2;
-        }
-      }
 #pragma unroll
-      for (int nt = 0; nt < Sh::kNTiles; ++nt) {
-        const int d = nt * 8 + cq;
-        if (r1 < u.gcount)
-          *reinterpret_cast<float2 *>(&xo[r1 * xd + d]) = make_float2(o[nt][0], o[nt][1]);
-        if (r2 < u.gcount)
-          *reinterpret_cast<float2 *>(&xo[r2 * xd + d]) = make_float2(o[nt][2], o[nt][3]);
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          float ls = l[nt][j];
+          ls += __shfl_xor_sync(0xffffffffu, ls, 4);
+          ls += __shfl_xor_sync(0xffffffffu, ls, 8);
+          ls += __shfl_xor_sync(0xffffffffu, ls, 16);
+          const int h = 8 * nt + 2 * fq + j;
+          if (fr == 0 && h < u.gcount) {
+            xm[cw * xr + h] = m[nt][j];
+            xl[cw * xr + h] = ls;
+          }
+        }
+        const int h0 = 8 * nt + 2 * fq;
+#pragma unroll
+        for (int mt = 0; mt < Sh::kMTiles; ++mt) {
+          const int d = 16 * mt + fr;
+          if (h0 < u.gcount) {
+            xo[h0 * xd + d] = o[nt][mt][0];
+            xo[h0 * xd + d + 8] = o[nt][mt][2];
+          }
+          if (h0 + 1 < u.gcount) {
+            xo[(h0 + 1) * xd + d] = o[nt][mt][1];
+            xo[(h0 + 1) * xd + d + 8] = o[nt][mt][3];
+          }
+        }
       }
       if (!sync()) {
         cp_async_wait_all();
@@ -1155,10 +1166,13 @@ decode_tc_kernel(DecodeArgs a) {
       // every consumer warp has read the unit's query rows and all exchange
       // rows: the query slot may be refilled
       if (tid == 0) mbar_arrive(&qempty[md.qslot]);
-      m1 = m2 = -INFINITY;
-      l1 = l2 = 0.f;
 #pragma unroll
-      for (int i = 0; i < Sh::kNTiles; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+      for (int nt = 0; nt < NT; ++nt) {
+        m[nt][0] = m[nt][1] = -INFINITY;
+        l[nt][0] = l[nt][1] = 0.f;
+#pragma unroll
+        for (int i = 0; i < Sh::kMTiles; ++i) o[nt][i][0] = o[nt][i][1] = o[nt][i][2] = o[nt][i][3] = 0.f;
+      }
     }
   }
   cp_async_wait_all();
@@ -1178,7 +1192,7 @@ int device_sms() {
 }
 
 
-// Default pages per split: the P in {8, 16, ..., 256} with the smallest
+// Default pages per split: the P in {8, 16, ..., 512} with the smallest
 // estimated launch time, assuming every sequence is max_blocks pages long (the
 // host does not see the lengths). With U units on `sms` persistent CTAs the
 // launch takes ceil(U / sms) rounds; a round costs its unit's pages plus a
@@ -1310,14 +1324,14 @@ int launch_generic_d(const DecodeArgs &a, cudaStream_t st, int64_t max_units) {
 // head_dim 128, 8 x 6 x 4 KB for head_dim 64.
 constexpr int kTcWarps = 8;
 
-template <typename T, int D, bool kExactP>
+template <typename T, int D, bool kExactP, int NT>
 int launch_tc_x(const DecodeArgs &a, cudaStream_t st, int64_t max_units) {
   constexpr int S = D == 128 ? 3 : 6;
   using L = TcSmem<D, kTcWarps, S>;
   static_assert(L::kBt + sizeof(int32_t) * kMaxPagesPerSplit + 1024 <= 227 * 1024,
                 "tensor-core decode exceeds the 227 KB of shared memory per CTA");
   const size_t smem = L::bytes(a.P);
-  auto kern = decode_tc_kernel<T, D, kTcWarps, S, kExactP>;
+  auto kern = decode_tc_kernel<T, D, kTcWarps, S, kExactP, NT>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return check_launch("cudaFuncSetAttribute(tc)");
@@ -1335,8 +1349,11 @@ int launch_tc_x(const DecodeArgs &a, cudaStream_t st, int64_t max_units) {
 
 template <typename T, int D>
 int launch_tc_t(const DecodeArgs &a, cudaStream_t st, int64_t max_units, int32_t flags) {
-  return (flags & PKV_DECODE_EXACT_P) ? launch_tc_x<T, D, true>(a, st, max_units)
-                                      : launch_tc_x<T, D, false>(a, st, max_units);
+  // query heads of a head group: up to 8 in one MMA n-tile, up to 16 in two
+  const bool two = a.GR > 8;
+  if (flags & PKV_DECODE_EXACT_P)
+    return two ? launch_tc_x<T, D, true, 2>(a, st, max_units) : launch_tc_x<T, D, true, 1>(a, st, max_units);
+  return two ? launch_tc_x<T, D, false, 2>(a, st, max_units) : launch_tc_x<T, D, false, 1>(a, st, max_units);
 }
 
 }  // namespace

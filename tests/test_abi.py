@@ -73,7 +73,7 @@ def test_decode_checks_and_workspace_query():
     assert lib.pkv_decode_workspace_size(4, 12, 5, 128, 32, 0) == 0  # 12 % 5 != 0
     assert lib.pkv_decode_pages_per_split(4, 12, 2, 128, 32, 16) == 16
     p = lib.pkv_decode_pages_per_split(1024, 12, 2, 128, 513, 0)
-    assert 8 <= p <= 256 and p % 8 == 0
+    assert 8 <= p <= 512 and p % 8 == 0
 
     # plan without a workspace is refused before any launch
     rc = lib.pkv_decode_plan(None, 4, 12, 2, 128, 16, 32, 0, None, 0, None, None)
@@ -89,8 +89,8 @@ def test_default_split_length_cost_model():
     """Without a GPU the library assumes a B200's 148 SMs."""
     pps = _lib.load().pkv_decode_pages_per_split
     assert pps(128, 12, 2, 128, 64, 0) == 64      # config 3: 256 whole sequences fill 148 SMs, no split
-    assert pps(1024, 12, 2, 128, 512, 0) == 256   # config 4: longest splits
-    assert pps(64, 28, 4, 128, 2048, 0) == 256    # config 5
+    assert pps(1024, 12, 2, 128, 512, 0) == 512   # config 4: every sequence one unit, no merge
+    assert pps(64, 28, 4, 128, 2048, 0) == 512    # config 5: the longest splits
     p = pps(4, 12, 2, 128, 2048, 0)               # 8 long sequences: split to fill the SMs once
     assert 8 * -(-2048 // p) <= 148 and 8 * -(-2048 // (p + 8)) < 148 <= 8 * -(-2048 // (p - 8))
     assert pps(4, 12, 2, 128, 33, 0) >= 33        # short contexts are never split
