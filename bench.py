@@ -46,7 +46,7 @@ METRIC = "paged KV decode: KV-read HBM GB/s and seq-steps/s at 1/2/4/8 B200"
 # ncu capture of decode_tc_kernel on the config-4 geometry (512 sequences, one
 # layer; profiles/decode_tc_512seq_1layer_ncu.md). Traffic grows with the
 # pages read, so roofline.traffic scales it to the full launch.
-DECODE_DRAM_TRAFFIC_RATIO = 1.0063
+DECODE_DRAM_TRAFFIC_RATIO = 1.0033
 UNIT = "seq-steps/s"
 
 
@@ -474,7 +474,8 @@ def run_e2e(args, wl, world, device):
     q_d, kn_d, vn_d = torch.empty_like(wl.q), torch.empty_like(wl.k_new), torch.empty_like(wl.v_new)
     ctx_d = [torch.empty_like(wl.ctx) for _ in range(2)]  # double-buffered across steps
     out_d = torch.empty_like(wl.out)
-    copy = torch.cuda.Stream(device)
+    copy = torch.cuda.Stream(device)  # host -> device
+    back = torch.cuda.Stream(device)  # device -> host (the other PCIe direction, concurrently)
     h2d = [torch.cuda.Event() for _ in range(L)]
     done = [torch.cuda.Event() for _ in range(L)]
     d2h = [torch.cuda.Event() for _ in range(L)]
@@ -518,10 +519,10 @@ def run_e2e(args, wl, world, device):
                 pkv.paged_attention_decode(q_d[layer], kc, vc, wl.block_tables, ctx, out=out_d[layer], plan=plan,
                                            exact=args.exact, k_new=kn_d[layer], v_new=vn_d[layer])
             done[layer].record(comp)
-            with torch.cuda.stream(copy):
-                copy.wait_event(done[layer])
+            with torch.cuda.stream(back):
+                back.wait_event(done[layer])
                 out_h[layer].copy_(out_d[layer], non_blocking=True)
-                d2h[layer].record(copy)
+                d2h[layer].record(back)
         ctx_free[buf].record(comp)
 
     step(True)
@@ -535,10 +536,12 @@ def run_e2e(args, wl, world, device):
 
         def body():
             cap = torch.cuda.current_stream(device)
-            copy.wait_stream(cap)  # fork the copy stream into the capture
+            copy.wait_stream(cap)  # fork the copy streams into the capture
+            back.wait_stream(cap)
             for i in range(args.steps):
                 step(i == 0)  # a replay starts after the previous one has finished
-            cap.wait_stream(copy)  # and join it back
+            cap.wait_stream(copy)  # and join them back
+            cap.wait_stream(back)
 
         graph = capture_steps(body)
         graph.replay()
@@ -554,6 +557,7 @@ def run_e2e(args, wl, world, device):
         for _ in range(args.steps):
             step(False)
     comp.wait_stream(copy)
+    comp.wait_stream(back)
     t1.record(comp)
     torch.cuda.synchronize()
     barrier(world)
@@ -570,8 +574,9 @@ def run_e2e(args, wl, world, device):
         "api": ("grpo_training_engine_b200.paged_kv_append + paged_attention_decode (C ABI pkv_append / "
                 "pkv_decode_run)" if args.separate_append else
                 "grpo_training_engine_b200.paged_attention_decode(k_new=, v_new=) (C ABI pkv_append_decode_run)"),
-        "launch": ("the timed steps' copies and calls captured as one CUDA graph on two streams"
-                   if graph is not None else "eager launches from Python on two streams"),
+        "launch": ("the timed steps' copies and calls captured as one CUDA graph on three streams "
+                   "(compute, host->device, device->host)" if graph is not None else
+                   "eager launches from Python on three streams (compute, host->device, device->host)"),
         "output_matches_device_run": bool(ok),
     }
 
