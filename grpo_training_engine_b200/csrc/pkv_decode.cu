@@ -119,6 +119,7 @@ struct DecodeArgs {
   const int4 *items;  // per item {b, split, clamped ctx, splits of b}
   float *partials;
   int32_t *status;
+  int32_t *sched;  // {next tail unit, CTAs done claiming}: the dynamic tail of the schedule
   // fused append (tensor-core kernel): the new token of sequence b, written at
   // position context_lens[b] - 1; kn == nullptr when there is none
   const void *kn;
@@ -279,8 +280,8 @@ plan_kernel(const int32_t *__restrict__ ctx, int32_t B, int32_t bs, int32_t max_
     hdr[1] = P;
     hdr[2] = B;
     hdr[3] = upi;
-    hdr[4] = 0;  // reserved
-    hdr[5] = 0;  // reserved
+    hdr[4] = 0;  // next tail unit to hand out (tensor-core kernel)
+    hdr[5] = 0;  // CTAs done claiming tail units
   }
 }
 
@@ -616,15 +617,18 @@ decode_tc_kernel(DecodeArgs a) {
 
   if (warp == NW) {
     // =========================== producer warp ===========================
-    // Static schedule: the plan numbers units longest first, and CTA c takes
-    // unit c in round 0, 2G-1-c in round 1, 2G+c in round 2, ... (G =
-    // gridDim.x, "snake" order), so the CTAs given the longest units of one
-    // round get the shortest of the next and every CTA ends within about one
-    // short unit of the others, with no atomics. Knowing its whole list, the
-    // warp runs a three-deep software pipeline so no global-load latency is
-    // exposed at a unit boundary: while lane 0 publishes unit r, the
-    // descriptor of r+2 is being loaded and the block-table entries and query
-    // rows of r+1 are in flight into registers.
+    // Schedule: the plan numbers units longest first. CTA c takes unit c in
+    // round 0, 2G-1-c in round 1, 2G+c in round 2, ... (G = gridDim.x, "snake"
+    // order: the CTAs given the longest units of one round get the shortest of
+    // the next). With at least six rounds of units, only the first R = U/G - 1
+    // rounds are assigned this way; the remaining, shortest units are handed
+    // out in order by a global counter, so the CTAs that run ahead take more of
+    // them and the launch ends within about one short unit. The warp runs a
+    // three-deep software pipeline so no global-load latency is exposed at a
+    // unit boundary: while lane 0 publishes unit r, the descriptor of r+2 is
+    // being loaded, the block-table entries and query rows of r+1 are in flight
+    // into registers, and the claim of round r+3 (if it is a counted one) is
+    // outstanding.
     const uint32_t FULL = 0xffffffffu;
     const int32_t G = (int32_t)gridDim.x;
     const int4 none = make_int4(0, 0, 0, 1);
@@ -676,11 +680,21 @@ decode_tc_kernel(DecodeArgs a) {
       }
     };
     const int32_t c = (int32_t)blockIdx.x;
-    // unit of round r (increasing in r, so the first one >= total ends the list)
+    // rounds assigned statically; claims run three rounds ahead of use, so a
+    // counted tail only pays off once the CTAs have progressed for a few rounds
+    const int32_t R = total / G >= 6 ? total / G - 1 : INT32_MAX;
+    // unit of static round r < R (r * G + ... < total)
     auto unit_at = [&](int32_t r) -> int32_t {
       const int64_t w = (int64_t)r * G + ((r & 1) ? G - 1 - c : c);
       return w < total ? (int32_t)w : total;
     };
+    // unit of counted round r >= R from the counter value f claimed for it
+    auto tail_unit = [&](int32_t f) -> int32_t {
+      const int64_t w = (int64_t)R * G + f;
+      return w < total ? (int32_t)w : total;
+    };
+    int32_t fetched = 0;  // lane 0: the outstanding claim
+    if (lane == 0 && R <= 2) fetched = atomicAdd(&a.sched[0], 1);  // round 2 is counted
     int32_t round = 0;
     int32_t w1 = unit_at(0), w2 = unit_at(1);
     int4 d1 = w1 < total ? a.items[w1 / a.upi] : none;
@@ -745,7 +759,14 @@ decode_tc_kernel(DecodeArgs a) {
       // (2) prefetch: the next unit's block-table entries and query rows, the
       //     descriptor of the one after
       load_next(w2, d2);
-      const int32_t w3 = unit_at(round + 2);
+      int32_t w3;
+      if (round + 2 < R) {
+        w3 = unit_at(round + 2);
+      } else {
+        w3 = tail_unit(__shfl_sync(FULL, fetched, 0));
+      }
+      // the claim for round r + 3 is consumed at the next iteration
+      if (lane == 0 && round + 3 >= R && w3 < total) fetched = atomicAdd(&a.sched[0], 1);
       const int4 d3 = w3 < total ? a.items[w3 / a.upi] : none;
       // (3) publish the unit's pages to the consumer warps (page p -> warp p % NW);
       //     each consumer loads its pages itself with cp.async
@@ -797,6 +818,16 @@ decode_tc_kernel(DecodeArgs a) {
       d1 = d2;
       w2 = w3;
       d2 = d3;
+    }
+    if (lane == 0) {
+      // This CTA claims no more units. The last CTA to get here resets the
+      // counters so the plan can drive the next launch.
+      __threadfence();
+      const int done = atomicAdd(&a.sched[1], 1);
+      if (done == (int)gridDim.x - 1) {
+        atomicExch(&a.sched[0], 0);
+        atomicExch(&a.sched[1], 0);
+      }
     }
     if (lane == 0 && ok) {
 #pragma unroll
@@ -1501,6 +1532,7 @@ int decode_run_impl(const void *q, const void *kn, const void *vn, const void *k
   a.seq_nsplit = reinterpret_cast<const int32_t *>(ws + w.seq_nsplit);
   a.items = reinterpret_cast<const int4 *>(ws + w.items);
   a.partials = reinterpret_cast<float *>(ws + w.partials);
+  a.sched = reinterpret_cast<int32_t *>(ws + w.hdr) + 4;
   a.status = status;
   const int64_t max_units = w.max_items * w.units_per_item;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
