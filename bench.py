@@ -642,6 +642,56 @@ def _cpu_name() -> str:
     return "unknown"
 
 
+# ----------------------------------------------------------------------------- model-level rollout
+def run_rollout(args):
+    """Model-level decode steps of paged_kv_decode (the trainer's rollout call) on the
+    DeepSeek-R1-Distill-Qwen-1.5B geometry with random bf16 weights: eager steps vs
+    steps replayed as one CUDA graph. Per-step time = difference of two rollouts of
+    different lengths (the prefill and setup cancel), CUDA events, 1 GPU."""
+    import grpo_training_engine_b200 as pkv
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    device = torch.device("cuda", 0)
+    cfg = Qwen2Config(hidden_size=1536, intermediate_size=8960, num_hidden_layers=28, num_attention_heads=12,
+                      num_key_value_heads=2, vocab_size=151936, max_position_embeddings=4096,
+                      rope_theta=10000.0, tie_word_embeddings=True, attn_implementation="sdpa")
+    torch.manual_seed(0)
+    with torch.device(device):
+        model = Qwen2ForCausalLM(cfg).to(torch.bfloat16).eval()
+    batch, prompt = 128, 512
+    ids = torch.randint(0, cfg.vocab_size, (batch, prompt), device=device)
+    mask = torch.ones_like(ids)
+    short, long_ = 4, 4 + max(args.steps, 8)
+    kw = dict(do_sample=True, temperature=0.7, top_p=0.9, seed=7, pad_token_id=0)
+
+    def timed(n, graph):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        pkv.paged_kv_decode(model, ids, mask, max_new_tokens=n, use_cuda_graph=graph, **kw)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1)
+
+    res = {}
+    for graph in (False, True):
+        timed(short, graph)  # warm-up (cuBLAS handles, kernels loaded)
+        t_s, t_l = timed(short, graph), timed(long_, graph)
+        ms = (t_l - t_s) / (long_ - short)
+        res["graph" if graph else "eager"] = {"ms_per_step": round(ms, 3), "seq_steps_per_s": round(batch / ms * 1e3, 1)}
+    print(json.dumps({
+        "metric": "model-level rollout decode step (paged_kv_decode), seq-steps/s",
+        "unit": "seq-steps/s",
+        "n_gpus": 1,
+        "data": "synthetic: random bf16 weights of the 1.5B geometry, random prompt ids",
+        "config": {"model": "DeepSeek-R1-Distill-Qwen-1.5B geometry (28 L, hidden 1536, 12q/2kv, D 128, "
+                            "vocab 151936), random weights", "batch": batch, "prompt_len": prompt,
+                   "sampling": "temperature 0.7, top-p 0.9", "steps_timed": long_ - short},
+        "eager": res["eager"], "graph": res["graph"],
+        "speedup": round(res["eager"]["ms_per_step"] / res["graph"]["ms_per_step"], 3),
+    }), flush=True)
+
+
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args, rank, world):
     """CPU restatement of the reference algorithm on the host cores (the reference is
@@ -753,6 +803,8 @@ def main():
                     help="launch every kernel from Python instead of replaying a CUDA graph of the timed steps")
     ap.add_argument("--separate-append", action="store_true",
                     help="append with its own launch (pkv_append) instead of inside the decode launch")
+    ap.add_argument("--rollout", action="store_true",
+                    help="time the model-level rollout step (eager vs CUDA graph) instead of the decode path")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
@@ -762,6 +814,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.rollout:
+        run_rollout(args)
+        return
     rank, world, local = dist_setup(args)
     if args.impl == "reference":
         run_reference(args, rank, world)

@@ -105,6 +105,7 @@ def paged_kv_decode(model, input_ids, attention_mask=None, max_new_tokens: int =
         pad_token_id=int(kwargs.pop("pad_token_id", 0)),
         eos_token_id=kwargs.pop("eos_token_id", None),
         seed=kwargs.pop("seed", None),
+        use_cuda_graph=bool(kwargs.pop("use_cuda_graph", True)),
     )
 
 

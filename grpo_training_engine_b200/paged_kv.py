@@ -284,14 +284,24 @@ def paged_kv_decode_model(
     pad_token_id: int,
     eos_token_id: Optional[int],
     seed: Optional[int],
+    use_cuda_graph: bool = True,
 ) -> torch.Tensor:
     """Rollout of an HF Qwen2-style decoder over a paged cache; returns [B, max_new_tokens].
 
     The prompt minus its last token is prefilled with an HF forward and
     written into pages; each step then embeds the last token, and per layer
-    runs norm -> q/k/v projection + RoPE -> page append -> paged decode
-    attention -> o_proj -> MLP, then samples the next token
+    runs norm -> q/k/v projection + RoPE -> page append + paged decode
+    attention (one launch) -> o_proj -> MLP, then samples the next token
     (paged_kv.py:690-837).
+
+    With use_cuda_graph (the default), the step's model forward -- embedding,
+    every layer, final norm and LM head -- is captured once as a CUDA graph
+    after the first (eager) step and replayed for the others, so a step costs
+    one launch instead of ~15 per layer from Python; sampling stays eager.
+    This is the graph capture the reference leaves disabled
+    (``use_cuda_graph = False``, paged_kv.py:687). A model whose forward
+    cannot be captured falls back to eager steps; the tokens are identical
+    either way (the same kernels run on the same buffers).
     """
     if max_new_tokens <= 0:
         raise ValueError(f"max_new_tokens must be > 0, got {max_new_tokens}.")
@@ -315,19 +325,27 @@ def paged_kv_decode_model(
 
     generated = torch.full((batch_size, max_new_tokens), pad_token_id, device=device, dtype=input_ids.dtype)
     generator = _make_generator(device, seed)
-    last_tokens = input_ids[:, -1]
     finished = torch.zeros(batch_size, device=device, dtype=torch.bool)
     scale = 1.0 / math.sqrt(head_dim)
     from transformers.models.qwen2.modeling_qwen2 import apply_rotary_pos_emb
 
-    def _step() -> tuple[torch.Tensor, torch.Tensor]:
-        hidden = cast(torch.Tensor, embeddings(last_tokens))
+    # The forward reads the step's inputs from fixed buffers (the last tokens
+    # and the pre-append context lengths), so a CUDA graph of it can be
+    # replayed with new values; its outputs are the logits and the post-append
+    # lengths.
+    tokens_buf = input_ids[:, -1].clone()
+    ctx_buf = context_lens
+    plan_ws = ops.plan_decode(ctx_buf + 1, num_heads, num_kv_heads, head_dim, block_size,
+                              block_tables.shape[1]).workspace
+
+    def _forward() -> tuple[torch.Tensor, torch.Tensor]:
+        hidden = cast(torch.Tensor, embeddings(tokens_buf))
         if hidden.ndim == 2:
             hidden = hidden.unsqueeze(1)
-        cos, sin = rotary_emb(hidden, context_lens.unsqueeze(1))
-        new_context_lens = context_lens + 1
+        cos, sin = rotary_emb(hidden, ctx_buf.unsqueeze(1))
+        new_context_lens = ctx_buf + 1
         plan = ops.plan_decode(new_context_lens, num_heads, num_kv_heads, head_dim, block_size,
-                               block_tables.shape[1])
+                               block_tables.shape[1], workspace=plan_ws)
         for layer_idx, layer in enumerate(layers):
             attn = layer.self_attn
             residual = hidden
@@ -348,20 +366,41 @@ def paged_kv_decode_model(
             residual = hidden
             hidden = residual + layer.mlp(layer.post_attention_layernorm(hidden))
         hidden = norm(hidden)
-        logits = lm_head(hidden[:, -1, :])
-        return _sample_tokens(logits, do_sample, temperature, top_p, generator), new_context_lens
+        return lm_head(hidden[:, -1, :]), new_context_lens
 
+    graph: Optional[torch.cuda.CUDAGraph] = None
+    graph_out: Optional[tuple[torch.Tensor, torch.Tensor]] = None
     for step in range(max_new_tokens):
         if finished.all():
             break
-        next_tokens, new_context_lens = _step()
+        if graph is not None:
+            graph.replay()
+            logits, new_context_lens = graph_out
+        else:
+            logits, new_context_lens = _forward()
+        next_tokens = _sample_tokens(logits, do_sample, temperature, top_p, generator)
         next_tokens = torch.where(finished, torch.full_like(next_tokens, pad_token_id), next_tokens)
         generated[:, step] = next_tokens
-        last_tokens = next_tokens
         if eos_token_id is not None and eos_token_id >= 0:
             finished = finished | (next_tokens == eos_token_id)
-        context_lens = new_context_lens
+        tokens_buf.copy_(next_tokens)
+        ctx_buf.copy_(new_context_lens)
+        if step == 0 and use_cuda_graph and device.type == "cuda" and max_new_tokens > 1:
+            # the eager first step was the warm-up; capture the forward for the rest
+            graph, graph_out = _capture_forward(_forward)
     return generated
+
+
+def _capture_forward(forward):
+    """CUDA graph of forward() and its output tensors, or (None, None) if it cannot be captured."""
+    graph = torch.cuda.CUDAGraph()
+    try:
+        with torch.cuda.graph(graph):
+            out = forward()
+    except RuntimeError:
+        torch.cuda.synchronize()
+        return None, None
+    return graph, out
 
 
 __all__ = ["paged_kv_decode", "paged_kv_decode_model"]

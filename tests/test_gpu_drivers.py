@@ -248,6 +248,20 @@ def test_model_level_matches_dense_rollout():
             assert float(gaps[row, first]) < 0.05, (row, first, float(gaps[row, first]))
 
 
+@pytest.mark.parametrize("do_sample", [False, True])
+def test_model_level_cuda_graph_steps_equal_eager_steps(do_sample):
+    """The graph-replayed step runs the same kernels on the same buffers as the
+    eager step: identical tokens, greedy or seeded sampling, EOS handling included."""
+    model = _tiny_qwen2()
+    torch.manual_seed(11)
+    ids = torch.randint(0, 96, (6, 17), device=DEV)
+    kw = dict(max_new_tokens=12, do_sample=do_sample, temperature=0.9, top_p=0.9, seed=1234,
+              pad_token_id=0, eos_token_id=7)
+    eager = pkg.paged_kv_decode(model, ids, torch.ones_like(ids), use_cuda_graph=False, **kw)
+    graph = pkg.paged_kv_decode(model, ids, torch.ones_like(ids), use_cuda_graph=True, **kw)
+    assert torch.equal(eager, graph)
+
+
 def test_model_level_rows_do_not_share_pages():
     """Each row owns its pages (defect D1): a batched greedy rollout of different
     prompts equals each prompt rolled out alone. With one block table shared by
