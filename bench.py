@@ -661,7 +661,8 @@ def run_rollout(args):
     batch, prompt = 128, 512
     ids = torch.randint(0, cfg.vocab_size, (batch, prompt), device=device)
     mask = torch.ones_like(ids)
-    short, long_ = 4, 4 + max(args.steps, 8)
+    # long enough that the per-call graph capture (tens of ms) is small next to the steps
+    short, long_ = 4, 4 + max(args.steps, 256)
     kw = dict(do_sample=True, temperature=0.7, top_p=0.9, seed=7, pad_token_id=0)
 
     def timed(n, graph):

@@ -414,6 +414,46 @@ def paged_attention_decode(
     return out
 
 
+# ---------------------------------------------------------------------------
+# sampling
+# ---------------------------------------------------------------------------
+def sample_top_p(
+    logits: torch.Tensor,
+    temperature: float,
+    top_p: float,
+    generator: Optional[torch.Generator] = None,
+) -> torch.Tensor:
+    """One token per row of logits [B, V]: temperature + nucleus (top-p) sampling.
+
+    The nucleus is the reference's (paged_kv.py:418-450): softmax(logits / T)
+    in descending order, tokens kept while their running probability stays
+    <= top_p, the most likely token always kept; top_p >= 1 keeps all. One
+    launch per call (C ABI pkv_sample_top_p) instead of a sort of the whole
+    vocabulary. The draw uses one uniform per row from ``generator`` (so a
+    seeded generator reproduces the tokens) and the inverse CDF of the kept
+    tokens in index order. Returns int64 [B].
+    """
+    if logits.ndim != 2:
+        raise ValueError(f"logits must be [batch, vocab], got {tuple(logits.shape)}.")
+    if not temperature > 0.0 or not top_p > 0.0:
+        raise ValueError("temperature and top_p must be > 0 for sampling.")
+    dev = _require_cuda(logits)
+    if logits.stride(1) != 1:
+        logits = logits.contiguous()
+    batch, vocab = logits.shape
+    u = torch.rand(batch, device=dev, dtype=torch.float32, generator=generator)
+    out = torch.empty(batch, dtype=torch.int64, device=dev)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        _lib.check(
+            "pkv_sample_top_p",
+            lib.pkv_sample_top_p(logits.data_ptr(), _dtype_code(logits, "logits"), batch, vocab, logits.stride(0),
+                                 float(max(temperature, 1e-6)), float(top_p if top_p < 1.0 else 2.0),
+                                 u.data_ptr(), out.data_ptr(), _stream(dev)),
+        )
+    return out
+
+
 def decode_kernel_kind(q: torch.Tensor, k_cache: torch.Tensor, force_generic: bool = False) -> str:
     """'tensor_core' or 'cuda_core': which decode kernel these tensors select."""
     hq, head_dim = q.shape[1], q.shape[2]

@@ -97,9 +97,15 @@ def _sample_tokens(
     top_p: float,
     generator: Optional[torch.Generator],
 ) -> torch.Tensor:
-    """Greedy when not sampling (or temperature <= 0), else temperature + top-p multinomial."""
+    """Greedy when not sampling (or temperature <= 0), else temperature + top-p multinomial.
+
+    CUDA logits with top_p > 0 go through one launch of the sampling kernel
+    (ops.sample_top_p) instead of a sort of the vocabulary.
+    """
     if not do_sample or temperature <= 0.0:
         return torch.argmax(logits, dim=-1)
+    if logits.is_cuda and top_p > 0.0:
+        return ops.sample_top_p(logits, temperature, top_p, generator)
     probs = torch.softmax(_apply_top_p(logits / max(temperature, 1e-6), top_p), dim=-1)
     return torch.multinomial(probs, num_samples=1, generator=generator).squeeze(-1)
 

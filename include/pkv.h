@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define PKV_ABI_VERSION 2  /* 2: pkv_append_decode_run */
+#define PKV_ABI_VERSION 3  /* 2: pkv_append_decode_run, 3: pkv_sample_top_p */
 
 /* Element types. The reference stores the cache in bfloat16
  * (paged_kv.py:409-410, 629-633); float32 is accepted because the reference
@@ -216,6 +216,20 @@ int pkv_append_decode_run(const void *q, const void *k_new, const void *v_new,
                           float scale, int32_t pages_per_split, int32_t flags,
                           void *workspace, size_t workspace_bytes, int32_t *status,
                           void *stream);
+
+/*
+ * pkv_sample_top_p: one token per row of logits [batch, vocab] (row stride
+ * row_stride elements, any dtype code), sampled from softmax(logits / T)
+ * restricted to the nucleus the reference keeps: tokens in descending order
+ * while their running probability is <= top_p, and always the most likely
+ * one (src/triton_kernels/paged_kv.py:418-450). Ties at the cut are kept in
+ * index order. uniforms[b] in [0, 1) picks the token by the inverse CDF of the
+ * kept tokens in index order. out_tokens is int64 [batch]. temperature and
+ * top_p must be > 0; top_p >= 1 keeps every token. One launch, no sort.
+ */
+int pkv_sample_top_p(const void *logits, int32_t dtype, int32_t batch, int32_t vocab,
+                     int64_t row_stride, float temperature, float top_p,
+                     const float *uniforms, int64_t *out_tokens, void *stream);
 
 int pkv_decode(const void *q, const void *k_cache, const void *v_cache,
                const int32_t *block_tables, const int32_t *context_lens,

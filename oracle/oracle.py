@@ -10,7 +10,11 @@ What it restates (reference = src/triton_kernels/paged_kv.py):
                    restatement on small cases;
   append        -> _paged_kv_update_kernel (:253-319): slot = pre-append length;
   append_prompt -> the prefill scatter of _prefill_paged_cache (:576-586);
-  gather        -> the decode kernel's addressing (:98-131) written densely.
+  gather        -> the decode kernel's addressing (:98-131) written densely;
+  sample_top_p  -> _sample_tokens / _apply_top_p (:418-450): scaled logits in the
+                   logits dtype, stable descending sort, running probability,
+                   nucleus cut, then the draw for a given uniform by the inverse
+                   CDF of the kept tokens in index order (the CUDA op's draw).
 The byte-moving functions work on raw-bit numpy views, so they are exact for
 every dtype. Parity of this oracle with the reference itself is pinned by
 tests/golden/ (fixtures produced by running the reference's own kernels).
@@ -190,3 +194,43 @@ def gather(k_cache, v_cache, block_tables, context_lens, max_tokens=None):
 
 if __name__ == "__main__":  # pragma: no cover
     print(build(force=True), max_threads(), os.cpu_count())
+
+
+def sample_top_p(logits, temperature: float, top_p: float, uniforms):
+    """Token per row and the two margins that decide it, for uniforms u in [0, 1).
+
+    Follows paged_kv.py:418-450: scaled = logits / max(T, 1e-6) rounded to the
+    logits dtype, probabilities softmax(scaled) (here in float64), the sorted
+    order descending with ties in index order (a stable sort), tokens kept
+    while their running probability is <= top_p, the first always kept. The
+    draw inverts the CDF of the kept tokens in index order at u * kept mass.
+    Returns (tokens int64 [B], cut_margin [B], draw_margin [B]): the distance
+    of the running probability from top_p at the cut and of the target from
+    the nearest CDF step, so a test can skip rows that float rounding decides.
+    """
+    lg = _cpu(logits)
+    scaled = (lg.float() / max(float(temperature), 1e-6)).to(lg.dtype).double().numpy()
+    u = np.asarray(_cpu(torch.as_tensor(uniforms)).double())
+    B, V = scaled.shape
+    toks = np.zeros(B, dtype=np.int64)
+    cut_margin = np.full(B, np.inf)
+    draw_margin = np.full(B, np.inf)
+    for b in range(B):
+        x = scaled[b]
+        p = np.exp(x - x.max())
+        p /= p.sum()
+        order = np.argsort(-x, kind="stable")
+        run = np.cumsum(p[order])
+        keep_sorted = run <= top_p if top_p < 1.0 else np.ones(V, dtype=bool)
+        keep_sorted[0] = True
+        if top_p < 1.0:
+            cut_margin[b] = float(np.min(np.abs(run - top_p)))
+        keep = np.zeros(V, dtype=bool)
+        keep[order[keep_sorted]] = True
+        idx = np.nonzero(keep)[0]
+        cdf = np.cumsum(p[idx])
+        target = u[b] * cdf[-1]
+        j = int(np.searchsorted(cdf, target, side="right"))
+        toks[b] = idx[min(j, len(idx) - 1)]
+        draw_margin[b] = float(np.min(np.abs(cdf - target)))
+    return torch.from_numpy(toks), cut_margin, draw_margin

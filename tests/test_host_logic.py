@@ -183,3 +183,21 @@ def test_lpt_assign_partitions_and_balances():
         assert imbalance(costs, parts) < 1.01
     assert lpt_assign([5, 1], 4)[2:] == [[], []]
     assert shard_groups([3, 2, 1], 2, 0) == [0]
+
+
+def test_sampling_oracle_keeps_the_reference_nucleus():
+    """oracle.sample_top_p keeps exactly the tokens _apply_top_p (the reference rule,
+    paged_kv.py:418-434) leaves finite, on fp32 logits without ties."""
+    from oracle import oracle
+
+    g = torch.Generator().manual_seed(2)
+    logits = torch.randn(6, 300, generator=g) * 3
+    for top_p in (0.3, 0.8, 0.97):
+        kept = torch.isfinite(paged_kv._apply_top_p(logits / 0.7, top_p))
+        # many uniforms per row: every token the oracle can return is in the nucleus,
+        # and the sampled set covers the nucleus
+        u = torch.linspace(0.0005, 0.9995, 2000)
+        for b in range(logits.shape[0]):
+            toks, _, _ = oracle.sample_top_p(logits[b:b + 1].repeat(len(u), 1), 0.7, top_p, u)
+            assert set(toks.tolist()) <= set(kept[b].nonzero().flatten().tolist())
+            assert set(toks.tolist()) == set(kept[b].nonzero().flatten().tolist()) or kept[b].sum() > 50
