@@ -15,7 +15,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libpkv.so"
 
-ABI_VERSION = 3  # PKV_ABI_VERSION in include/pkv.h
+ABI_VERSION = 4  # PKV_ABI_VERSION in include/pkv.h
 
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
@@ -73,6 +73,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
          _i64p, _i64p, _i64p, _i64p, _i64p, _i32, _i32, C.c_float, _i32, _i32, _vp, _sz, _vp, _vp],
     ),
+    "pkv_add_rmsnorm": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, C.c_int64, C.c_int64, C.c_int64,
+                                  C.c_int64, C.c_float, _i32, _vp]),
+    "pkv_rope_qk": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, C.c_int64, C.c_int64,
+                              C.c_int64, _i32, _vp]),
     "pkv_sample_top_p": (C.c_int, [_vp, _i32, _i32, _i32, C.c_int64, C.c_float, C.c_float, _vp, _vp, _vp]),
     "pkv_decode": (
         C.c_int,

@@ -415,6 +415,79 @@ def paged_attention_decode(
 
 
 # ---------------------------------------------------------------------------
+# decode-step element-wise steps
+# ---------------------------------------------------------------------------
+def add_rmsnorm(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    eps: float,
+    residual: Optional[torch.Tensor] = None,
+) -> tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """RMSNorm of x [rows, hidden] (after adding residual, if given) in one launch.
+
+    Returns (normed, x + residual or None), with the rounding points of HF's
+    Qwen2RMSNorm: the sum rounded to the dtype, fp32 statistics,
+    dtype(s * rsqrt(mean(s^2) + eps)) scaled by weight (C ABI pkv_add_rmsnorm).
+    """
+    if x.ndim != 2 or x.stride(1) != 1:
+        raise ValueError("x must be [rows, hidden] with contiguous rows.")
+    rows, hidden = x.shape
+    if weight.shape != (hidden,) or weight.dtype != x.dtype or not weight.is_contiguous():
+        raise ValueError("weight must be a contiguous [hidden] tensor of x's dtype.")
+    if residual is not None and (residual.shape != x.shape or residual.dtype != x.dtype or residual.stride(1) != 1):
+        raise ValueError("residual must match x.")
+    dev = _require_cuda(x, weight, residual)
+    out = torch.empty_like(x, memory_format=torch.contiguous_format)
+    total = torch.empty_like(out) if residual is not None else None
+    with torch.cuda.device(dev):
+        _lib.check(
+            "pkv_add_rmsnorm",
+            _lib.load().pkv_add_rmsnorm(
+                x.data_ptr(), residual.data_ptr() if residual is not None else None, weight.data_ptr(),
+                total.data_ptr() if total is not None else None, out.data_ptr(), rows, hidden, x.stride(0),
+                residual.stride(0) if residual is not None else 0, hidden, hidden, float(eps),
+                _dtype_code(x, "x"), _stream(dev)),
+        )
+    return out, total
+
+
+def rope_qk(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    num_q_heads: int,
+    num_kv_heads: int,
+    head_dim: int,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """RoPE of one new query / key row per sequence, one launch.
+
+    q [rows, Hq * D], k [rows, Hkv * D] (the projections' outputs), cos / sin
+    [rows, D]; returns contiguous q [rows, Hq, D] and k [rows, Hkv, D] equal to
+    HF's apply_rotary_pos_emb of the same rows (C ABI pkv_rope_qk).
+    """
+    rows = q.shape[0]
+    if (q.shape != (rows, num_q_heads * head_dim) or k.shape != (rows, num_kv_heads * head_dim)
+            or q.stride(1) != 1 or k.stride(1) != 1):
+        raise ValueError("q / k must be [rows, heads * head_dim] with contiguous rows.")
+    if cos.shape != (rows, head_dim) or sin.shape != cos.shape or cos.stride() != sin.stride() or cos.stride(1) != 1:
+        raise ValueError("cos / sin must be matching [rows, head_dim] tensors with contiguous rows.")
+    if not (q.dtype == k.dtype == cos.dtype == sin.dtype):
+        raise ValueError("q, k, cos and sin must share one dtype.")
+    dev = _require_cuda(q, k, cos, sin)
+    qo = torch.empty(rows, num_q_heads, head_dim, dtype=q.dtype, device=dev)
+    ko = torch.empty(rows, num_kv_heads, head_dim, dtype=k.dtype, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(
+            "pkv_rope_qk",
+            _lib.load().pkv_rope_qk(q.data_ptr(), k.data_ptr(), cos.data_ptr(), sin.data_ptr(), qo.data_ptr(),
+                                    ko.data_ptr(), rows, num_q_heads, num_kv_heads, head_dim, q.stride(0),
+                                    k.stride(0), cos.stride(0), _dtype_code(q, "q"), _stream(dev)),
+        )
+    return qo, ko
+
+
+# ---------------------------------------------------------------------------
 # sampling
 # ---------------------------------------------------------------------------
 def sample_top_p(

@@ -344,7 +344,17 @@ def paged_kv_decode_model(
     plan_ws = ops.plan_decode(ctx_buf + 1, num_heads, num_kv_heads, head_dim, block_size,
                               block_tables.shape[1]).workspace
 
-    def _forward() -> tuple[torch.Tensor, torch.Tensor]:
+    # The element-wise steps around the projections (residual add + RMSNorm,
+    # RoPE of the new q / k rows) run as one launch each (ops.add_rmsnorm,
+    # ops.rope_qk) for a bf16 model (the cache dtype) whose norms are plain
+    # weight-scaled RMSNorms; otherwise through the model's own modules.
+    norms = [norm] + [m for layer in layers for m in (layer.input_layernorm, layer.post_attention_layernorm)]
+    fused_glue = all(
+        isinstance(getattr(m, "weight", None), torch.Tensor) and getattr(m, "variance_epsilon", None) is not None
+        and m.weight.dtype == embeddings.weight.dtype and m.weight.ndim == 1 and m.weight.numel() <= 4096
+        for m in norms) and head_dim % 2 == 0 and embeddings.weight.dtype == torch.bfloat16
+
+    def _forward_modules() -> tuple[torch.Tensor, torch.Tensor]:
         hidden = cast(torch.Tensor, embeddings(tokens_buf))
         if hidden.ndim == 2:
             hidden = hidden.unsqueeze(1)
@@ -373,6 +383,36 @@ def paged_kv_decode_model(
             hidden = residual + layer.mlp(layer.post_attention_layernorm(hidden))
         hidden = norm(hidden)
         return lm_head(hidden[:, -1, :]), new_context_lens
+
+    def _forward_fused() -> tuple[torch.Tensor, torch.Tensor]:
+        hidden = cast(torch.Tensor, embeddings(tokens_buf))  # [B, hidden]
+        cos, sin = rotary_emb(hidden.unsqueeze(1), ctx_buf.unsqueeze(1))
+        cos, sin = cos.reshape(batch_size, head_dim), sin.reshape(batch_size, head_dim)
+        new_context_lens = ctx_buf + 1
+        plan = ops.plan_decode(new_context_lens, num_heads, num_kv_heads, head_dim, block_size,
+                               block_tables.shape[1], workspace=plan_ws)
+        pending = None  # the previous layer's MLP output, added in the next norm
+        for layer_idx, layer in enumerate(layers):
+            attn = layer.self_attn
+            ln = layer.input_layernorm
+            h, total = ops.add_rmsnorm(hidden if pending is None else pending, ln.weight, ln.variance_epsilon,
+                                       residual=None if pending is None else hidden)
+            if total is not None:
+                hidden = total
+            q1, k1 = ops.rope_qk(attn.q_proj(h), attn.k_proj(h), cos, sin, num_heads, num_kv_heads, head_dim)
+            v1 = attn.v_proj(h).view(batch_size, num_kv_heads, head_dim)
+            k_cache, v_cache = pool.layer(layer_idx)
+            # append at context_lens and attend over new_context_lens: one fused call
+            attn_out = ops.paged_attention_decode(q1, k_cache, v_cache, block_tables, new_context_lens,
+                                                  scale=scale, plan=plan, k_new=k1, v_new=v1)
+            o = attn.o_proj(attn_out.to(hidden.dtype).reshape(batch_size, num_heads * head_dim))
+            ln = layer.post_attention_layernorm
+            h2, hidden = ops.add_rmsnorm(o, ln.weight, ln.variance_epsilon, residual=hidden)
+            pending = layer.mlp(h2)
+        h, _ = ops.add_rmsnorm(pending, norm.weight, norm.variance_epsilon, residual=hidden)
+        return lm_head(h), new_context_lens
+
+    _forward = _forward_fused if fused_glue else _forward_modules
 
     graph: Optional[torch.cuda.CUDAGraph] = None
     graph_out: Optional[tuple[torch.Tensor, torch.Tensor]] = None

@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define PKV_ABI_VERSION 3  /* 2: pkv_append_decode_run, 3: pkv_sample_top_p */
+#define PKV_ABI_VERSION 4  /* 2: pkv_append_decode_run, 3: pkv_sample_top_p, 4: rmsnorm, rope */
 
 /* Element types. The reference stores the cache in bfloat16
  * (paged_kv.py:409-410, 629-633); float32 is accepted because the reference
@@ -230,6 +230,30 @@ int pkv_append_decode_run(const void *q, const void *k_new, const void *v_new,
 int pkv_sample_top_p(const void *logits, int32_t dtype, int32_t batch, int32_t vocab,
                      int64_t row_stride, float temperature, float top_p,
                      const float *uniforms, int64_t *out_tokens, void *stream);
+
+/*
+ * Decode-step element-wise steps around the decode launch (one launch each).
+ *
+ * pkv_add_rmsnorm: for each row, s = x + residual (rounded to dtype; skipped
+ * when residual is NULL; written to sum_out when that is not NULL), then
+ * out = weight * dtype(s * rsqrt(mean(s^2) + eps)) with fp32 statistics, the
+ * rounding points of HF's Qwen2RMSNorm (the reference's fused_ops rmsnorm).
+ * hidden <= 4096. Strides are in elements.
+ *
+ * pkv_rope_qk: RoPE of one new query row [num_q_heads * head_dim] and key row
+ * [num_kv_heads * head_dim] per sequence with cos/sin [rows, head_dim] (row
+ * stride cs_stride), written as contiguous q_out [rows, Hq, D] and
+ * k_out [rows, Hkv, D] (the layout pkv_append_decode_run reads), with the
+ * element-wise rounding of HF's apply_rotary_pos_emb.
+ */
+int pkv_add_rmsnorm(const void *x, const void *residual, const void *weight, void *sum_out, void *out,
+                    int32_t rows, int32_t hidden, int64_t x_stride, int64_t residual_stride,
+                    int64_t sum_stride, int64_t out_stride, float eps, int32_t dtype, void *stream);
+
+int pkv_rope_qk(const void *q, const void *k, const void *cos_, const void *sin_, void *q_out,
+                void *k_out, int32_t rows, int32_t num_q_heads, int32_t num_kv_heads,
+                int32_t head_dim, int64_t q_stride, int64_t k_stride, int64_t cs_stride,
+                int32_t dtype, void *stream);
 
 int pkv_decode(const void *q, const void *k_cache, const void *v_cache,
                const int32_t *block_tables, const int32_t *context_lens,
