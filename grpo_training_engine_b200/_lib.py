@@ -75,6 +75,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "pkv_add_rmsnorm": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, C.c_int64, C.c_int64, C.c_int64,
                                   C.c_int64, C.c_float, _i32, _vp]),
+    "pkv_silu_mul": (C.c_int, [_vp, _vp, _vp, _i32, _i32, C.c_int64, C.c_int64, _i32, _vp]),
     "pkv_rope_qk": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, C.c_int64, C.c_int64,
                               C.c_int64, _i32, _vp]),
     "pkv_sample_top_p": (C.c_int, [_vp, _i32, _i32, _i32, C.c_int64, C.c_float, C.c_float, _vp, _vp, _vp]),

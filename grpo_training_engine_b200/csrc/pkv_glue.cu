@@ -5,14 +5,18 @@
 // fused_ops.py's rmsnorm and q/k/v + RoPE) and in an HF Qwen2 layer these are
 // each a handful of small torch kernels per layer (pow, mean, add, rsqrt, two
 // multiplies and a cast for one RMSNorm; a concatenation, four multiplies and
-// adds and two copies for RoPE). Here each is one launch. The arithmetic keeps
+// adds and two copies for RoPE, SiLU and a multiply in the MLP). Here each is
+// one launch. The arithmetic keeps
 // the HF module's rounding points:
 //   RMSNorm (Qwen2RMSNorm): s = x + r rounded to the dtype when there is a
 //     residual; v = fp32(s); y = dtype(v * rsqrt(mean(v^2) + eps));
 //     out = dtype(w * y);
+//   SiLU * up (Qwen2MLP): out = dtype(dtype(silu(gate)) * up);
 //   RoPE (apply_rotary_pos_emb): out = dtype(dtype(q * cos) + dtype(rot(q) * sin)),
 //     rot(q) = (-q[D/2:], q[:D/2]), every product and sum rounded to the dtype
 //     as torch's bf16 element-wise ops do.
+#include <algorithm>
+
 #include "pkv_common.cuh"
 
 namespace pkv {
@@ -33,31 +37,46 @@ template <> struct Cvt<float> {
 };
 
 constexpr int kNormThreads = 256;
-constexpr int kNormPerThread = 16;  // hidden sizes up to 4096
+constexpr int kNormVecs = 2;  // 16-byte vectors per thread: hidden sizes up to 256 x 2 x 16 B
+
+// Loads / stores of 16 bytes as kV elements of T (the row offsets used are
+// multiples of kV, and the host checks 16-byte alignment of rows).
+template <typename T> struct Vec16 {
+  static constexpr int kV = 16 / (int)sizeof(T);
+  T e[kV];
+};
 
 template <typename T>
 __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(const T *x, const T *res, const T *w,
                                                                     T *sum_out, T *out, int H, int64_t xs,
                                                                     int64_t rs, int64_t ss, int64_t os,
                                                                     float eps) {
+  using V = Vec16<T>;
+  constexpr int kV = V::kV;
   __shared__ float red[kNormThreads / 32];
   const int64_t b = blockIdx.x;
   const int tid = threadIdx.x;
-  float v[kNormPerThread];
+  float v[kNormVecs][kV];
   float acc = 0.f;
 #pragma unroll
-  for (int j = 0; j < kNormPerThread; ++j) {
-    const int i = tid + j * kNormThreads;
-    v[j] = 0.f;
+  for (int j = 0; j < kNormVecs; ++j) {
+    const int i = (tid + j * kNormThreads) * kV;
     if (i < H) {
-      float s = Cvt<T>::f(x[b * xs + i]);
-      if (res != nullptr) {
-        const T st = Cvt<T>::t(s + Cvt<T>::f(res[b * rs + i]));
-        if (sum_out != nullptr) sum_out[b * ss + i] = st;
-        s = Cvt<T>::f(st);
+      const V xv = *reinterpret_cast<const V *>(x + b * xs + i);
+      V rv;
+      if (res != nullptr) rv = *reinterpret_cast<const V *>(res + b * rs + i);
+      V sv;
+#pragma unroll
+      for (int e = 0; e < kV; ++e) {
+        float s = Cvt<T>::f(xv.e[e]);
+        if (res != nullptr) {
+          sv.e[e] = Cvt<T>::t(s + Cvt<T>::f(rv.e[e]));  // the residual sum, rounded to T
+          s = Cvt<T>::f(sv.e[e]);
+        }
+        v[j][e] = s;
+        acc += s * s;
       }
-      v[j] = s;
-      acc += s * s;
+      if (sum_out != nullptr) *reinterpret_cast<V *>(sum_out + b * ss + i) = sv;
     }
   }
 #pragma unroll
@@ -69,9 +88,37 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(const T *x, c
   for (int k = 0; k < kNormThreads / 32; ++k) tot += red[k];
   const float r = rsqrtf(tot / (float)H + eps);
 #pragma unroll
-  for (int j = 0; j < kNormPerThread; ++j) {
-    const int i = tid + j * kNormThreads;
-    if (i < H) out[b * os + i] = Cvt<T>::t(Cvt<T>::f(w[i]) * Cvt<T>::f(Cvt<T>::t(v[j] * r)));
+  for (int j = 0; j < kNormVecs; ++j) {
+    const int i = (tid + j * kNormThreads) * kV;
+    if (i < H) {
+      const V wv = *reinterpret_cast<const V *>(w + i);
+      V ov;
+#pragma unroll
+      for (int e = 0; e < kV; ++e) ov.e[e] = Cvt<T>::t(Cvt<T>::f(wv.e[e]) * Cvt<T>::f(Cvt<T>::t(v[j][e] * r)));
+      *reinterpret_cast<V *>(out + b * os + i) = ov;
+    }
+  }
+}
+
+// out = dtype(dtype(silu(gate)) * up), the rounding of HF's act_fn(gate) * up.
+template <typename T>
+__global__ void silu_mul_kernel(const T *gate, const T *up, T *out, int64_t n_vec, int cols, int64_t gs,
+                                int64_t us) {
+  using V = Vec16<T>;
+  constexpr int kV = V::kV;
+  const int vpr = cols / kV;  // vectors per row
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < n_vec; v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = v / vpr, c = (v - r * vpr) * kV;
+    const V g = *reinterpret_cast<const V *>(gate + r * gs + c);
+    const V u = *reinterpret_cast<const V *>(up + r * us + c);
+    V o;
+#pragma unroll
+    for (int e = 0; e < kV; ++e) {
+      const float x = Cvt<T>::f(g.e[e]);
+      const float a = Cvt<T>::f(Cvt<T>::t(x / (1.f + expf(-x))));
+      o.e[e] = Cvt<T>::t(a * Cvt<T>::f(u.e[e]));
+    }
+    *reinterpret_cast<V *>(out + r * (int64_t)cols + c) = o;
   }
 }
 
@@ -107,9 +154,12 @@ extern "C" int pkv_add_rmsnorm(const void *x, const void *residual, const void *
                                void *out, int32_t rows, int32_t hidden, int64_t x_stride,
                                int64_t residual_stride, int64_t sum_stride, int64_t out_stride, float eps,
                                int32_t dtype, void *stream) {
-  if (rows < 0 || hidden <= 0 || hidden > kNormThreads * kNormPerThread) {
-    set_error_detail("pkv_add_rmsnorm: rows %d, hidden %d (at most %d)", rows, hidden,
-                     kNormThreads * kNormPerThread);
+  const int es = dtype_size(dtype);
+  if (es == 0) return PKV_ERR_UNSUPPORTED;
+  const int max_hidden = kNormThreads * kNormVecs * 16 / es;
+  if (rows < 0 || hidden <= 0 || hidden > max_hidden || (hidden * es) % 16 != 0) {
+    set_error_detail("pkv_add_rmsnorm: rows %d, hidden %d (a multiple of 16 bytes, at most %d elements)", rows,
+                     hidden, max_hidden);
     return PKV_ERR_INVALID_ARG;
   }
   if (rows == 0) return PKV_OK;
@@ -117,11 +167,13 @@ extern "C" int pkv_add_rmsnorm(const void *x, const void *residual, const void *
     set_error_detail("pkv_add_rmsnorm: NULL pointer");
     return PKV_ERR_INVALID_ARG;
   }
-  const int es = dtype_size(dtype);
-  if (es == 0) return PKV_ERR_UNSUPPORTED;
+  // rows are read and written as 16-byte vectors
   const void *ptrs[] = {x, residual, weight, sum_out, out};
   for (const void *p : ptrs)
-    if (p && !aligned_to(p, es)) return PKV_ERR_ALIGNMENT;
+    if (p && !aligned_to(p, 16)) return PKV_ERR_ALIGNMENT;
+  const int64_t strides[] = {x_stride, residual ? residual_stride : 0, sum_out ? sum_stride : 0, out_stride};
+  for (int64_t st : strides)
+    if ((st * es) % 16 != 0) return PKV_ERR_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   switch (dtype) {
     case PKV_DTYPE_BF16:
@@ -142,6 +194,47 @@ extern "C" int pkv_add_rmsnorm(const void *x, const void *residual, const void *
       break;
   }
   return check_launch("pkv_add_rmsnorm");
+}
+
+extern "C" int pkv_silu_mul(const void *gate, const void *up, void *out, int32_t rows, int32_t cols,
+                            int64_t gate_stride, int64_t up_stride, int32_t dtype, void *stream) {
+  const int es = dtype_size(dtype);
+  if (es == 0) return PKV_ERR_UNSUPPORTED;
+  if (rows < 0 || cols <= 0 || (cols * es) % 16 != 0) {
+    set_error_detail("pkv_silu_mul: rows %d, cols %d (a multiple of 16 bytes)", rows, cols);
+    return PKV_ERR_INVALID_ARG;
+  }
+  if (rows == 0) return PKV_OK;
+  if (!gate || !up || !out) {
+    set_error_detail("pkv_silu_mul: NULL pointer");
+    return PKV_ERR_INVALID_ARG;
+  }
+  const void *ptrs[] = {gate, up, out};
+  for (const void *p : ptrs)
+    if (!aligned_to(p, 16)) return PKV_ERR_ALIGNMENT;
+  if ((gate_stride * es) % 16 != 0 || (up_stride * es) % 16 != 0) return PKV_ERR_ALIGNMENT;
+  const int64_t n_vec = (int64_t)rows * cols * es / 16;
+  const int threads = 256;
+  const int64_t blocks = std::min<int64_t>((n_vec + threads - 1) / threads, 148 * 16);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case PKV_DTYPE_BF16:
+      silu_mul_kernel<__nv_bfloat16><<<(unsigned)blocks, threads, 0, st>>>(
+          (const __nv_bfloat16 *)gate, (const __nv_bfloat16 *)up, (__nv_bfloat16 *)out, n_vec, cols, gate_stride,
+          up_stride);
+      break;
+    case PKV_DTYPE_F16:
+      silu_mul_kernel<__half><<<(unsigned)blocks, threads, 0, st>>>((const __half *)gate, (const __half *)up,
+                                                                    (__half *)out, n_vec, cols, gate_stride,
+                                                                    up_stride);
+      break;
+    default:
+      silu_mul_kernel<float><<<(unsigned)blocks, threads, 0, st>>>((const float *)gate, (const float *)up,
+                                                                   (float *)out, n_vec, cols, gate_stride,
+                                                                   up_stride);
+      break;
+  }
+  return check_launch("pkv_silu_mul");
 }
 
 extern "C" int pkv_rope_qk(const void *q, const void *k, const void *cos_, const void *sin_, void *q_out,

@@ -451,6 +451,22 @@ def add_rmsnorm(
     return out, total
 
 
+def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """dtype(dtype(silu(gate)) * up) for [rows, cols] tensors in one launch (C ABI pkv_silu_mul):
+    the gated activation of a Qwen2 MLP with the rounding of F.silu(gate) * up."""
+    if gate.ndim != 2 or gate.shape != up.shape or gate.dtype != up.dtype or gate.stride(1) != 1 or up.stride(1) != 1:
+        raise ValueError("gate and up must be matching [rows, cols] tensors with contiguous rows.")
+    dev = _require_cuda(gate, up)
+    out = torch.empty(gate.shape, dtype=gate.dtype, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(
+            "pkv_silu_mul",
+            _lib.load().pkv_silu_mul(gate.data_ptr(), up.data_ptr(), out.data_ptr(), gate.shape[0], gate.shape[1],
+                                     gate.stride(0), up.stride(0), _dtype_code(gate, "gate"), _stream(dev)),
+        )
+    return out
+
+
 def rope_qk(
     q: torch.Tensor,
     k: torch.Tensor,

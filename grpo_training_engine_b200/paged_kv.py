@@ -352,7 +352,18 @@ def paged_kv_decode_model(
     fused_glue = all(
         isinstance(getattr(m, "weight", None), torch.Tensor) and getattr(m, "variance_epsilon", None) is not None
         and m.weight.dtype == embeddings.weight.dtype and m.weight.ndim == 1 and m.weight.numel() <= 4096
-        for m in norms) and head_dim % 2 == 0 and embeddings.weight.dtype == torch.bfloat16
+        for m in norms) and head_dim % 2 == 0 and embeddings.weight.dtype == torch.bfloat16 \
+        and embeddings.weight.shape[1] % 8 == 0
+    # a plain SiLU-gated MLP: its activation and product run as one launch (ops.silu_mul)
+    silu_mlp = all(type(getattr(layer.mlp, "act_fn", None)).__name__ in ("SiLUActivation", "SiLU")
+                   and all(hasattr(layer.mlp, n) for n in ("gate_proj", "up_proj", "down_proj"))
+                   and layer.mlp.gate_proj.out_features % 8 == 0 for layer in layers)
+
+    def _mlp(layer, h):
+        mlp = layer.mlp
+        if silu_mlp:
+            return mlp.down_proj(ops.silu_mul(mlp.gate_proj(h), mlp.up_proj(h)))
+        return mlp(h)
 
     def _forward_modules() -> tuple[torch.Tensor, torch.Tensor]:
         hidden = cast(torch.Tensor, embeddings(tokens_buf))
@@ -408,7 +419,7 @@ def paged_kv_decode_model(
             o = attn.o_proj(attn_out.to(hidden.dtype).reshape(batch_size, num_heads * head_dim))
             ln = layer.post_attention_layernorm
             h2, hidden = ops.add_rmsnorm(o, ln.weight, ln.variance_epsilon, residual=hidden)
-            pending = layer.mlp(h2)
+            pending = _mlp(layer, h2)
         h, _ = ops.add_rmsnorm(pending, norm.weight, norm.variance_epsilon, residual=hidden)
         return lm_head(h), new_context_lens
 

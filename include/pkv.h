@@ -238,7 +238,8 @@ int pkv_sample_top_p(const void *logits, int32_t dtype, int32_t batch, int32_t v
  * when residual is NULL; written to sum_out when that is not NULL), then
  * out = weight * dtype(s * rsqrt(mean(s^2) + eps)) with fp32 statistics, the
  * rounding points of HF's Qwen2RMSNorm (the reference's fused_ops rmsnorm).
- * hidden <= 4096. Strides are in elements.
+ * Rows are read as 16-byte vectors: 16-byte aligned rows whose byte length is a
+ * multiple of 16, hidden <= 8192 bytes' worth (4096 bf16). Strides in elements.
  *
  * pkv_rope_qk: RoPE of one new query row [num_q_heads * head_dim] and key row
  * [num_kv_heads * head_dim] per sequence with cos/sin [rows, head_dim] (row
@@ -249,6 +250,11 @@ int pkv_sample_top_p(const void *logits, int32_t dtype, int32_t batch, int32_t v
 int pkv_add_rmsnorm(const void *x, const void *residual, const void *weight, void *sum_out, void *out,
                     int32_t rows, int32_t hidden, int64_t x_stride, int64_t residual_stride,
                     int64_t sum_stride, int64_t out_stride, float eps, int32_t dtype, void *stream);
+
+/* pkv_silu_mul: out [rows, cols] (contiguous) = dtype(dtype(silu(gate)) * up), the
+ * gated activation of a Qwen2 MLP; rows of 16-byte multiples, 16-byte aligned. */
+int pkv_silu_mul(const void *gate, const void *up, void *out, int32_t rows, int32_t cols,
+                 int64_t gate_stride, int64_t up_stride, int32_t dtype, void *stream);
 
 int pkv_rope_qk(const void *q, const void *k, const void *cos_, const void *sin_, void *q_out,
                 void *k_out, int32_t rows, int32_t num_q_heads, int32_t num_kv_heads,

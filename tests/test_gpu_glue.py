@@ -1,6 +1,7 @@
-"""Decode-step element-wise kernels (C ABI pkv_add_rmsnorm / pkv_rope_qk) against
-the HF modules they replace in the rollout step: Qwen2RMSNorm (with the residual
-add in front, as in a decoder layer) and apply_rotary_pos_emb."""
+"""Decode-step element-wise kernels (C ABI pkv_add_rmsnorm / pkv_silu_mul /
+pkv_rope_qk) against the HF modules they replace in the rollout step:
+Qwen2RMSNorm (with the residual add in front, as in a decoder layer), the SiLU
+gate of Qwen2MLP, and apply_rotary_pos_emb."""
 
 from __future__ import annotations
 
@@ -13,7 +14,7 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
-@pytest.mark.parametrize("hidden", [1536, 3584, 896, 4096, 100])
+@pytest.mark.parametrize("hidden", [1536, 3584, 896, 4096, 104])
 @pytest.mark.parametrize("with_residual", [False, True])
 def test_add_rmsnorm_matches_qwen2_rmsnorm(hidden, with_residual):
     from transformers.models.qwen2.modeling_qwen2 import Qwen2RMSNorm
@@ -55,3 +56,20 @@ def test_rope_qk_matches_apply_rotary_pos_emb(hq, hkv, d):
     qo, ko = ops.rope_qk(q, k, cos.reshape(b, d), sin.reshape(b, d), hq, hkv, d)
     assert torch.equal(qo, q_ref[:, :, 0, :])
     assert torch.equal(ko, k_ref[:, :, 0, :])
+
+
+def test_silu_mul_matches_qwen2_mlp_gate():
+    g = torch.Generator(device=DEV).manual_seed(1)
+    gate = (torch.randn(128, 8960, device=DEV, generator=g) * 3).to(torch.bfloat16)
+    up = (torch.randn(128, 8960, device=DEV, generator=g) * 3).to(torch.bfloat16)
+    ref = torch.nn.functional.silu(gate) * up
+    out = ops.silu_mul(gate, up)
+    diff = (out.float() - ref.float()).abs()
+    assert bool((diff <= ref.float().abs() * 2.0 ** -7 + 1e-30).all())
+    assert float((out != ref).float().mean()) < 0.01
+
+
+def test_glue_rejects_unaligned_rows():
+    x = torch.randn(4, 100, device=DEV).to(torch.bfloat16)  # 200-byte rows
+    with pytest.raises(RuntimeError):
+        ops.add_rmsnorm(x, torch.ones(100, device=DEV, dtype=torch.bfloat16), 1e-6)
