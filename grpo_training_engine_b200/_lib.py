@@ -15,7 +15,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libpkv.so"
 
-ABI_VERSION = 4  # PKV_ABI_VERSION in include/pkv.h
+ABI_VERSION = 5  # PKV_ABI_VERSION in include/pkv.h
 
 DTYPE_F32 = 0
 DTYPE_BF16 = 1

@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define PKV_ABI_VERSION 4  /* 2: pkv_append_decode_run, 3: pkv_sample_top_p, 4: rmsnorm, rope */
+#define PKV_ABI_VERSION 5  /* 2: pkv_append_decode_run, 3: pkv_sample_top_p, 4: rmsnorm, rope, 5: silu_mul */
 
 /* Element types. The reference stores the cache in bfloat16
  * (paged_kv.py:409-410, 629-633); float32 is accepted because the reference
