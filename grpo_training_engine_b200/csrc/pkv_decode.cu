@@ -118,6 +118,7 @@ struct DecodeArgs {
   const int32_t *seq_off;
   const int32_t *seq_nsplit;
   const int4 *items;  // per item {b, split, clamped ctx, splits of b}
+  int64_t max_items;  // entries the item array holds (the plan fills the first total / upi)
   float *partials;
   int32_t *status;
   int32_t *sched;  // {next tail unit, CTAs done claiming}: the dynamic tail of the schedule
@@ -681,6 +682,11 @@ decode_tc_kernel(DecodeArgs a) {
       }
     };
     const int32_t c = (int32_t)blockIdx.x;
+    // the descriptors of rounds 0 and 1 are loaded together with the unit
+    // count instead of after it (indices clamped into the item array; a
+    // descriptor past the count is never used)
+    const int4 r0 = a.items[min((int64_t)c / a.upi, a.max_items - 1)];
+    const int4 r1 = a.items[min((int64_t)(2 * G - 1 - c) / a.upi, a.max_items - 1)];
     // rounds assigned statically; claims run three rounds ahead of use, so a
     // counted tail only pays off once the CTAs have progressed for a few rounds
     const int32_t R = total / G >= 6 ? total / G - 1 : INT32_MAX;
@@ -698,8 +704,8 @@ decode_tc_kernel(DecodeArgs a) {
     if (lane == 0 && R <= 2) fetched = atomicAdd(&a.sched[0], 1);  // round 2 is counted
     int32_t round = 0;
     int32_t w1 = unit_at(0), w2 = unit_at(1);
-    int4 d1 = w1 < total ? a.items[w1 / a.upi] : none;
-    int4 d2 = w2 < total ? a.items[w2 / a.upi] : none;
+    int4 d1 = w1 < total ? r0 : none;
+    int4 d2 = w2 < total ? r1 : none;
     load_next(w1, d1);
 
     int32_t kcount[NW];
@@ -1533,6 +1539,7 @@ int decode_run_impl(const void *q, const void *kn, const void *vn, const void *k
   a.seq_off = reinterpret_cast<const int32_t *>(ws + w.seq_off);
   a.seq_nsplit = reinterpret_cast<const int32_t *>(ws + w.seq_nsplit);
   a.items = reinterpret_cast<const int4 *>(ws + w.items);
+  a.max_items = w.max_items;
   a.partials = reinterpret_cast<float *>(ws + w.partials);
   a.sched = reinterpret_cast<int32_t *>(ws + w.hdr) + 4;
   a.status = status;
