@@ -665,11 +665,12 @@ def run_rollout(args):
     short, long_ = 4, 4 + max(args.steps, 256)
     kw = dict(do_sample=True, temperature=0.7, top_p=0.9, seed=7, pad_token_id=0)
 
-    def timed(n, graph):
+    def timed(n, graph, x=ids, share=True):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         e0.record()
-        pkv.paged_kv_decode(model, ids, mask, max_new_tokens=n, use_cuda_graph=graph, **kw)
+        pkv.paged_kv_decode(model, x, torch.ones_like(x), max_new_tokens=n, use_cuda_graph=graph,
+                            share_prompt_pages=share, **kw)
         e1.record()
         torch.cuda.synchronize()
         return e0.elapsed_time(e1)
@@ -680,6 +681,19 @@ def run_rollout(args):
         t_s, t_l = timed(short, graph), timed(long_, graph)
         ms = (t_l - t_s) / (long_ - short)
         res["graph" if graph else "eager"] = {"ms_per_step": round(ms, 3), "seq_steps_per_s": round(batch / ms * 1e3, 1)}
+    # GRPO groups: 16 prompts x 8 responses (the trainer's expanded prompt per group):
+    # one prefill per prompt and shared prompt pages, against every row prefilled
+    # into private pages
+    group = 8
+    gids = torch.randint(0, cfg.vocab_size, (batch // group, prompt), device=device).repeat_interleave(group, 0)
+    grouped = {}
+    for share in (False, True):
+        timed(short, True, gids, share)
+        t_s, t_l = timed(short, True, gids, share), timed(long_, True, gids, share)
+        ms = (t_l - t_s) / (long_ - short)
+        grouped["shared" if share else "private"] = {
+            "setup_prefill_ms": round(t_s - short * ms, 2), "ms_per_step": round(ms, 3),
+            "seq_steps_per_s": round(batch / ms * 1e3, 1)}
     print(json.dumps({
         "metric": "model-level rollout decode step (paged_kv_decode), seq-steps/s",
         "unit": "seq-steps/s",
@@ -690,6 +704,7 @@ def run_rollout(args):
                    "sampling": "temperature 0.7, top-p 0.9", "steps_timed": long_ - short},
         "eager": res["eager"], "graph": res["graph"],
         "speedup": round(res["eager"]["ms_per_step"] / res["graph"]["ms_per_step"], 3),
+        "grpo_groups": {"prompts": batch // group, "group": group, **grouped},
     }), flush=True)
 
 

@@ -57,10 +57,24 @@ def paged_kv_decode(model, input_ids, attention_mask=None, max_new_tokens: int =
     do_sample, temperature, top_p, pad_token_id (0), eos_token_id and seed.
     Raises ImportError when libpkv.so is unavailable, like the reference when
     Triton is missing (the trainer falls back to HF generate on it).
+
+    Like the reference, it returns only the new tokens, [B, max_new_tokens]
+    (paged_kv.py:662-667). The trainer slices ``outputs[j, prompt_len:]``
+    as if it had HF generate's prompt + response rows (trainer.py:444-448);
+    ``return_prompt=True`` returns that layout, [B, prompt + max_new_tokens].
     """
     if not PAGED_KV_AVAILABLE:
         raise ImportError(f"paged KV kernels are not available for paged_kv_decode: {_LOAD_ERROR}")
     input_ids_t = cast(torch.Tensor, input_ids)
+    return_prompt = bool(kwargs.pop("return_prompt", False))
+    out = _route(model, input_ids_t, attention_mask, max_new_tokens, kwargs)
+    if return_prompt:
+        # HF generate's layout: the prompt as passed, then the new tokens
+        return torch.cat([input_ids_t, out.to(input_ids_t.dtype)], dim=1)
+    return out
+
+
+def _route(model, input_ids_t: torch.Tensor, attention_mask, max_new_tokens: int, kwargs: dict):
     mask_t = cast(torch.Tensor, attention_mask) if attention_mask is not None else None
     if all(name in kwargs for name in _LOW_LEVEL_ARGS):
         return _paged_kv_decode_low_level(
@@ -106,6 +120,7 @@ def paged_kv_decode(model, input_ids, attention_mask=None, max_new_tokens: int =
         eos_token_id=kwargs.pop("eos_token_id", None),
         seed=kwargs.pop("seed", None),
         use_cuda_graph=bool(kwargs.pop("use_cuda_graph", True)),
+        share_prompt_pages=bool(kwargs.pop("share_prompt_pages", True)),
     )
 
 

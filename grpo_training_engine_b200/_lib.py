@@ -15,7 +15,9 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libpkv.so"
 
-ABI_VERSION = 5  # PKV_ABI_VERSION in include/pkv.h
+ABI_VERSION = 6  # PKV_ABI_VERSION in include/pkv.h
+
+SAMPLE_FORCE_RADIX = 1  # PKV_SAMPLE_FORCE_RADIX
 
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
@@ -78,7 +80,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pkv_silu_mul": (C.c_int, [_vp, _vp, _vp, _i32, _i32, C.c_int64, C.c_int64, _i32, _vp]),
     "pkv_rope_qk": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, C.c_int64, C.c_int64,
                               C.c_int64, _i32, _vp]),
-    "pkv_sample_top_p": (C.c_int, [_vp, _i32, _i32, _i32, C.c_int64, C.c_float, C.c_float, _vp, _vp, _vp]),
+    "pkv_sample_top_p": (C.c_int, [_vp, _i32, _i32, _i32, C.c_int64, C.c_float, C.c_float, _vp, _vp, _i32, _vp]),
     "pkv_decode": (
         C.c_int,
         [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32,

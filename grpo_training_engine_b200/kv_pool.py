@@ -101,6 +101,17 @@ class KVPagePool:
         self.k[:, dst].copy_(self.k[:, src])
         self.v[:, dst].copy_(self.v[:, src])
 
+    def copy_pages(self, src: Sequence[int], dst: Sequence[int]) -> None:
+        """Copy pages src[i] -> dst[i] (all layers) in one gather/scatter per K and V."""
+        if len(src) != len(dst):
+            raise ValueError("src and dst must have the same length")
+        if not len(src):
+            return
+        si = torch.as_tensor(list(src), dtype=torch.long, device=self.k.device)
+        di = torch.as_tensor(list(dst), dtype=torch.long, device=self.k.device)
+        self.k[:, di] = self.k[:, si]
+        self.v[:, di] = self.v[:, si]
+
     def make_private(self, table: list[int], index: int) -> int:
         """Copy-on-write: give `table[index]` a private copy if it is shared."""
         page = table[index]
@@ -154,3 +165,49 @@ class KVPagePool:
         src = tables[0][idx]
         for t in tables[1:]:
             self.copy_page(src, t[idx])
+
+    def share_prompts(
+        self, groups: Sequence[int], prefix_tokens: int, total_tokens: int
+    ) -> tuple[list[list[int]], list[int]]:
+        """Tables for sequences whose prompts repeat: ``groups[i]`` names the prompt of row i.
+
+        Rows of one group share their full prefix pages (``share_prefix``);
+        rows of different groups share nothing. Returns one page list per row
+        (in row order) and the representative row of each group (its first
+        row, in order of first appearance): the prefix is written once through
+        the representative's table and its partially filled tail page copied
+        into the other rows' tails (``copy_prefix_tails``).
+        """
+        members: dict[int, list[int]] = {}
+        for row, g in enumerate(groups):
+            members.setdefault(int(g), []).append(row)
+        tables: list[list[int]] = [[] for _ in groups]
+        reps = []
+        for rows in members.values():
+            for row, table in zip(rows, self.share_prefix(len(rows), prefix_tokens, total_tokens)):
+                tables[row] = table
+            reps.append(rows[0])
+        return tables, reps
+
+    def copy_prefix_tails(self, tables: Sequence[Sequence[int]], groups: Sequence[int],
+                          prefix_tokens: int) -> None:
+        """Copy each group representative's partially filled prefix page into its other rows."""
+        if prefix_tokens % self.block_size == 0:
+            return
+        idx = prefix_tokens // self.block_size
+        first: dict[int, int] = {}
+        src, dst = [], []
+        for row, g in enumerate(groups):
+            rep = first.setdefault(int(g), row)
+            if rep != row:
+                src.append(tables[rep][idx])
+                dst.append(tables[row][idx])
+        self.copy_pages(src, dst)
+
+    @staticmethod
+    def pages_needed_shared(groups: Sequence[int], prefix_tokens: int, total_tokens: int,
+                            block_size: int) -> int:
+        """Pages ``share_prompts`` takes: full prefix pages once per group, the rest per row."""
+        full = prefix_tokens // block_size
+        need = (total_tokens + block_size - 1) // block_size
+        return len(set(int(g) for g in groups)) * full + len(groups) * max(need - full, 0)

@@ -511,6 +511,7 @@ def sample_top_p(
     temperature: float,
     top_p: float,
     generator: Optional[torch.Generator] = None,
+    force_radix: bool = False,
 ) -> torch.Tensor:
     """One token per row of logits [B, V]: temperature + nucleus (top-p) sampling.
 
@@ -520,7 +521,8 @@ def sample_top_p(
     launch per call (C ABI pkv_sample_top_p) instead of a sort of the whole
     vocabulary. The draw uses one uniform per row from ``generator`` (so a
     seeded generator reproduces the tokens) and the inverse CDF of the kept
-    tokens in index order. Returns int64 [B].
+    tokens in index order. Returns int64 [B]. ``force_radix`` selects the
+    radix-select path for 16-bit logits (the same tokens, slower).
     """
     if logits.ndim != 2:
         raise ValueError(f"logits must be [batch, vocab], got {tuple(logits.shape)}.")
@@ -538,7 +540,8 @@ def sample_top_p(
             "pkv_sample_top_p",
             lib.pkv_sample_top_p(logits.data_ptr(), _dtype_code(logits, "logits"), batch, vocab, logits.stride(0),
                                  float(max(temperature, 1e-6)), float(top_p if top_p < 1.0 else 2.0),
-                                 u.data_ptr(), out.data_ptr(), _stream(dev)),
+                                 u.data_ptr(), out.data_ptr(), _lib.SAMPLE_FORCE_RADIX if force_radix else 0,
+                                 _stream(dev)),
         )
     return out
 

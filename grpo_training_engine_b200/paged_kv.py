@@ -29,6 +29,7 @@ from __future__ import annotations
 import math
 from typing import Callable, Optional, Tuple, cast
 
+import numpy as np
 import torch
 
 from . import ops
@@ -277,6 +278,15 @@ def _prefill_paged_cache(
         ops.paged_kv_append_prompt(k_layer, v_layer, k_cache, v_cache, block_tables)
 
 
+def _prompt_groups(prompt_ids: torch.Tensor, prompt_mask: torch.Tensor) -> list[int]:
+    """Group id of each row: the first row with the same prompt tokens and mask."""
+    if prompt_ids.shape[0] > 1 and prompt_ids.stride(0) == 0 and prompt_mask.stride(0) == 0:
+        return [0] * prompt_ids.shape[0]  # one prompt expanded to the batch
+    key = torch.cat([prompt_ids.long(), prompt_mask.long()], dim=1).cpu().numpy()
+    _, first, inverse = np.unique(key, axis=0, return_index=True, return_inverse=True)
+    return first[inverse.reshape(-1)].tolist()
+
+
 @torch.no_grad()
 def paged_kv_decode_model(
     model: torch.nn.Module,
@@ -291,6 +301,7 @@ def paged_kv_decode_model(
     eos_token_id: Optional[int],
     seed: Optional[int],
     use_cuda_graph: bool = True,
+    share_prompt_pages: bool = True,
 ) -> torch.Tensor:
     """Rollout of an HF Qwen2-style decoder over a paged cache; returns [B, max_new_tokens].
 
@@ -308,6 +319,14 @@ def paged_kv_decode_model(
     (``use_cuda_graph = False``, paged_kv.py:687). A model whose forward
     cannot be captured falls back to eager steps; the tokens are identical
     either way (the same kernels run on the same buffers).
+
+    With share_prompt_pages (the default), rows whose prefilled prompts are
+    identical -- a GRPO group, which the trainer passes as one prompt
+    expanded to the micro-batch (trainer.py:389-392) -- are prefilled once:
+    one HF forward per distinct prompt, its full pages shared by reference
+    count and only the partially filled last prompt page copied per row, the
+    paged form of the trainer's prefix expansion (trainer.py:465-484).
+    Decode then reads a group's prompt pages from L2 after the first row.
     """
     if max_new_tokens <= 0:
         raise ValueError(f"max_new_tokens must be > 0, got {max_new_tokens}.")
@@ -321,13 +340,22 @@ def paged_kv_decode_model(
     max_context_needed = max(prompt_len - 1 + max_new_tokens + 1, 1)
     pages_per_seq = math.ceil(max_context_needed / block_size)
 
-    pool = KVPagePool(batch_size * pages_per_seq, len(layers), num_kv_heads, block_size, head_dim,
-                      dtype=torch.bfloat16, device=device)
-    tables = [pool.alloc(pages_per_seq) for _ in range(batch_size)]
+    prefix = prompt_len - 1
+    groups = _prompt_groups(input_ids[:, :-1], attention_mask[:, :-1]) \
+        if share_prompt_pages and batch_size > 1 and prefix > 0 else list(range(batch_size))
+    pool = KVPagePool(KVPagePool.pages_needed_shared(groups, prefix, max_context_needed, block_size),
+                      len(layers), num_kv_heads, block_size, head_dim, dtype=torch.bfloat16, device=device)
+    tables, reps = pool.share_prompts(groups, prefix, max_context_needed)
     block_tables = pool.block_table(tables, width=pages_per_seq)
-    context_lens = torch.full((batch_size,), prompt_len - 1, device=device, dtype=torch.int32)
-    if prompt_len > 1:
-        _prefill_paged_cache(model, input_ids[:, :-1], attention_mask[:, :-1], pool, block_tables)
+    context_lens = torch.full((batch_size,), prefix, device=device, dtype=torch.int32)
+    if prefix > 0:
+        if len(reps) == batch_size:
+            _prefill_paged_cache(model, input_ids[:, :-1], attention_mask[:, :-1], pool, block_tables)
+        else:
+            rep_idx = torch.as_tensor(reps, device=device)
+            _prefill_paged_cache(model, input_ids[rep_idx, :-1], attention_mask[rep_idx, :-1], pool,
+                                 block_tables[rep_idx])
+            pool.copy_prefix_tails(tables, groups, prefix)
 
     generated = torch.full((batch_size, max_new_tokens), pad_token_id, device=device, dtype=input_ids.dtype)
     generator = _make_generator(device, seed)

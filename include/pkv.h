@@ -37,7 +37,8 @@
 extern "C" {
 #endif
 
-#define PKV_ABI_VERSION 5  /* 2: pkv_append_decode_run, 3: pkv_sample_top_p, 4: rmsnorm, rope, 5: silu_mul */
+#define PKV_ABI_VERSION 6  /* 2: pkv_append_decode_run, 3: pkv_sample_top_p, 4: rmsnorm, rope, 5: silu_mul,
+                              6: pkv_sample_top_p flags */
 
 /* Element types. The reference stores the cache in bfloat16
  * (paged_kv.py:409-410, 629-633); float32 is accepted because the reference
@@ -74,6 +75,12 @@ enum {
                                      weights as a 16-bit head plus 16-bit
                                      remainder (~17 significant bits instead
                                      of 8); slower, closer to fp32           */
+};
+
+/* Sampling flags. */
+enum {
+    PKV_SAMPLE_FORCE_RADIX = 1 /* 16-bit logits: take the radix-select path even
+                                  when the per-pattern counts fit (same tokens) */
 };
 
 int pkv_abi_version(void);
@@ -226,10 +233,11 @@ int pkv_append_decode_run(const void *q, const void *k_new, const void *v_new,
  * index order. uniforms[b] in [0, 1) picks the token by the inverse CDF of the
  * kept tokens in index order. out_tokens is int64 [batch]. temperature and
  * top_p must be > 0; top_p >= 1 keeps every token. One launch, no sort.
+ * flags: PKV_SAMPLE_* (0 for the default).
  */
 int pkv_sample_top_p(const void *logits, int32_t dtype, int32_t batch, int32_t vocab,
                      int64_t row_stride, float temperature, float top_p,
-                     const float *uniforms, int64_t *out_tokens, void *stream);
+                     const float *uniforms, int64_t *out_tokens, int32_t flags, void *stream);
 
 /*
  * Decode-step element-wise steps around the decode launch (one launch each).

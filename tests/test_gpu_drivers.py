@@ -278,3 +278,68 @@ def test_model_level_rows_do_not_share_pages():
             diff = (got != ref[0]).nonzero()
             if len(diff):
                 assert float(gaps[0, int(diff[0])]) < 0.05
+
+
+def _assert_matches_dense(got_row, ref_row, gap_row):
+    diff = (got_row != ref_row).nonzero()
+    if len(diff):  # only a near-tie in the dense logits may flip a greedy token
+        first = int(diff[0])
+        assert float(gap_row[first]) < 0.05, (first, float(gap_row[first]))
+
+
+def test_model_level_group_shares_prompt_pages():
+    """A GRPO group -- one prompt expanded to the micro-batch, as the trainer passes
+    it -- is prefilled once with its full prompt pages shared: greedy rows are
+    identical and match the dense rollout of the prompt alone."""
+    model = _tiny_qwen2(2)
+    torch.manual_seed(9)
+    prompt = torch.randint(0, 96, (1, 37), device=DEV)  # 36 prefilled tokens: 2 shared pages + a tail of 4
+    ids = prompt.expand(6, -1)
+    got = pkg.paged_kv_decode(model, ids, torch.ones_like(prompt).expand(6, -1), max_new_tokens=10,
+                              do_sample=False)
+    assert got.shape == (6, 10) and (got == got[0]).all()
+    ref, gaps = _dense_rollout(model, prompt, 10)
+    _assert_matches_dense(got[0], ref[0], gaps[0])
+
+
+@pytest.mark.parametrize("prompt_len", [33, 40])  # prefix on a page boundary / with a partial page
+def test_model_level_interleaved_groups(prompt_len):
+    model = _tiny_qwen2(3)
+    torch.manual_seed(10)
+    prompts = torch.randint(0, 96, (2, prompt_len), device=DEV)
+    order = [0, 1, 1, 0, 1]
+    ids = prompts[order]
+    got = pkg.paged_kv_decode(model, ids, torch.ones_like(ids), max_new_tokens=8, do_sample=False)
+    for g in range(2):
+        ref, gaps = _dense_rollout(model, prompts[g:g + 1], 8)
+        for row in (r for r, o in enumerate(order) if o == g):
+            _assert_matches_dense(got[row], ref[0], gaps[0])
+    unshared = pkg.paged_kv_decode(model, ids, torch.ones_like(ids), max_new_tokens=8, do_sample=False,
+                                   share_prompt_pages=False)
+    for g in range(2):
+        ref, gaps = _dense_rollout(model, prompts[g:g + 1], 8)
+        for row in (r for r, o in enumerate(order) if o == g):
+            _assert_matches_dense(unshared[row], ref[0], gaps[0])
+
+
+def test_model_level_group_rows_sample_independently():
+    model = _tiny_qwen2(2)
+    torch.manual_seed(12)
+    prompt = torch.randint(0, 96, (1, 25), device=DEV)
+    kw = dict(max_new_tokens=12, do_sample=True, temperature=1.0, top_p=0.95, seed=77, pad_token_id=0)
+    a = pkg.paged_kv_decode(model, prompt.expand(8, -1), torch.ones_like(prompt).expand(8, -1), **kw)
+    b = pkg.paged_kv_decode(model, prompt.expand(8, -1), torch.ones_like(prompt).expand(8, -1), **kw)
+    assert torch.equal(a, b)  # seeded
+    assert len({tuple(r.tolist()) for r in a}) > 1  # shared prompt pages, private draws
+
+
+def test_facade_return_prompt_gives_generate_layout():
+    model = _tiny_qwen2()
+    torch.manual_seed(13)
+    ids = torch.randint(1, 96, (3, 11), device=DEV)
+    mask = torch.ones_like(ids)
+    mask[1, :3] = 0  # left padding
+    new = pkg.paged_kv_decode(model, ids, mask, max_new_tokens=5, do_sample=False)
+    full = pkg.paged_kv_decode(model, ids, mask, max_new_tokens=5, do_sample=False, return_prompt=True)
+    assert full.shape == (3, 16) and torch.equal(full[:, :11], ids)
+    assert torch.equal(full[:, 11:], new.to(ids.dtype))  # the trainer's outputs[j, prompt_len:]

@@ -45,12 +45,17 @@ def test_sample_matches_oracle(dtype, vocab, temperature, top_p):
     _check(logits, temperature, top_p, seed=vocab)
 
 
-def test_ties_at_the_cut_are_kept_in_index_order():
+@pytest.mark.parametrize("low,high", [(-4, 5), (-9, -1)])  # the second: the cut at a negative value
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_ties_at_the_cut_are_kept_in_index_order(low, high, dtype):
     # coarse logits: thousands of exact ties, so the cut falls inside a tie group
     g = torch.Generator().manual_seed(3)
-    logits = torch.randint(-4, 5, (32, 20000), generator=g).to(torch.bfloat16).to(DEV)
-    for seed, top_p in enumerate((0.3, 0.6, 0.9)):
-        _check(logits, 1.0, top_p, seed=seed)
+    logits = torch.randint(low, high, (32, 20000), generator=g).to(dtype).to(DEV)
+    for seed, (temperature, top_p) in enumerate(((1.0, 0.3), (1.0, 0.6), (1.0, 0.9), (1.3, 0.5))):
+        got = _check(logits, temperature, top_p, seed=seed)
+        radix = ops.sample_top_p(logits, temperature, top_p, torch.Generator(device=DEV).manual_seed(seed),
+                                 force_radix=True).cpu()
+        assert torch.equal(got, radix)
 
 
 def test_tiny_top_p_is_argmax_and_strided_rows():
@@ -85,3 +90,64 @@ def test_invalid_arguments():
         ops.sample_top_p(logits, 1.0, 0.0)
     with pytest.raises(ValueError):
         ops.sample_top_p(logits[0], 1.0, 0.9)
+
+
+def _both_paths(logits, temperature, top_p, seed=0):
+    fast = ops.sample_top_p(logits, temperature, top_p, torch.Generator(device=DEV).manual_seed(seed))
+    radix = ops.sample_top_p(logits, temperature, top_p, torch.Generator(device=DEV).manual_seed(seed),
+                             force_radix=True)
+    return fast, radix
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("kind", ["normal", "coarse", "flat", "masked", "peaked"])
+def test_count_path_equals_radix_path(dtype, kind):
+    """16-bit logits: the per-pattern count path and the radix-select path use the
+    same fixed-point masses, cut and target, so every row gives the same token --
+    near-ties included, no margin."""
+    g = torch.Generator().manual_seed(21)
+    vocab = 151936
+    if kind == "normal":
+        x = torch.randn(32, vocab, generator=g) * 4
+    elif kind == "coarse":  # thousands of exact ties: the cut falls inside a tie group
+        x = torch.randint(-4, 5, (32, vocab), generator=g).float()
+    elif kind == "flat":
+        x = torch.zeros(32, vocab)
+    elif kind == "masked":  # a padded vocabulary: -inf tail
+        x = torch.randn(32, vocab, generator=g) * 2
+        x[:, 150000:] = float("-inf")
+    else:  # one dominant token
+        x = torch.randn(32, vocab, generator=g)
+        x[torch.arange(32), torch.randint(0, vocab, (32,), generator=g)] = 30.0
+    logits = x.to(dtype).to(DEV)
+    for seed, (temperature, top_p) in enumerate([(0.7, 0.9), (1.0, 0.5), (1.3, 0.95), (0.8, 1.0), (0.6, 1e-4)]):
+        fast, radix = _both_paths(logits, temperature, top_p, seed)
+        assert torch.equal(fast, radix), (kind, temperature, top_p, (fast != radix).nonzero()[:4])
+
+
+@pytest.mark.parametrize("vocab", [7, 1000, 50257])
+def test_count_path_equals_radix_path_small_vocab(vocab):
+    g = torch.Generator().manual_seed(vocab)
+    for dtype in (torch.bfloat16, torch.float16):
+        logits = (torch.randn(48, vocab, generator=g) * 3).to(dtype).to(DEV)
+        for seed, (temperature, top_p) in enumerate([(0.7, 0.9), (1.0, 1.0), (2.0, 0.3)]):
+            fast, radix = _both_paths(logits, temperature, top_p, seed)
+            assert torch.equal(fast, radix)
+
+
+def test_rows_outside_the_count_window_take_the_radix_path():
+    g = torch.Generator().manual_seed(4)
+    # fp16 at a very high temperature: the massful patterns span more than the window
+    logits = (torch.randn(8, 30000, generator=g) * 4).to(torch.float16).to(DEV)
+    fast, radix = _both_paths(logits, 1000.0, 0.9, 3)
+    assert torch.equal(fast, radix)
+    _check(logits, 1000.0, 0.9, seed=3)
+    # +inf and all -inf rows next to ordinary ones (each CTA picks its own path)
+    x = (torch.randn(4, 5000, generator=g) * 2).to(torch.bfloat16)
+    x[1, 123] = float("inf")
+    x[2] = float("-inf")
+    logits = x.to(DEV)
+    fast, radix = _both_paths(logits, 0.9, 0.9, 5)
+    assert torch.equal(fast, radix)
+    # no finite softmax there (the reference's probabilities are NaN): a valid index, token 0 for all -inf
+    assert 0 <= int(fast[1]) < 5000 and int(fast[2]) == 0

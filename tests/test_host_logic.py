@@ -170,6 +170,63 @@ def test_pool_share_prefix_and_copy_on_write():
     assert bt.dtype == torch.int32 and bt.shape == (3, 5)
 
 
+def test_pool_share_prompts_groups_rows():
+    # rows 0, 2, 3 have one prompt, rows 1, 4 another; bs 4, prefix 10 -> 2 full shared pages per group
+    groups = [0, 1, 0, 0, 1]
+    need = KVPagePool.pages_needed_shared(groups, 10, 17, 4)
+    assert need == 2 * 2 + 5 * (5 - 2)
+    pool = _pool(need)
+    tables, reps = pool.share_prompts(groups, prefix_tokens=10, total_tokens=17)
+    assert reps == [0, 1] and pool.num_free == 0
+    assert tables[0][:2] == tables[2][:2] == tables[3][:2] and tables[1][:2] == tables[4][:2]
+    assert not set(tables[0][:2]) & set(tables[1][:2])
+    assert pool.refcount(tables[0][0]) == 3 and pool.refcount(tables[1][0]) == 2
+    private = [p for t in tables for p in t[2:]]
+    assert len(set(private)) == len(private) == 15 and all(pool.refcount(p) == 1 for p in private)
+    pool.k[:, tables[0][2]] = 3.0
+    pool.v[:, tables[1][2]] = 5.0
+    pool.copy_prefix_tails(tables, groups, 10)
+    assert (pool.k[:, tables[2][2]] == 3.0).all() and (pool.k[:, tables[3][2]] == 3.0).all()
+    assert (pool.v[:, tables[4][2]] == 5.0).all() and (pool.k[:, tables[4][2]] == 0.0).all()
+
+
+def test_pool_share_prompts_without_repeats_is_private():
+    pool = _pool(12)
+    tables, reps = pool.share_prompts([0, 1, 2], prefix_tokens=8, total_tokens=13)
+    assert reps == [0, 1, 2] and sorted(p for t in tables for p in t) == list(range(12))
+    pool.copy_prefix_tails(tables, [0, 1, 2], 8)  # page-aligned prefix: nothing to copy
+
+
+def test_prompt_groups_detects_repeated_prompts():
+    ids = torch.tensor([[1, 2, 3], [4, 5, 6], [1, 2, 3], [1, 2, 3]])
+    mask = torch.ones_like(ids)
+    assert paged_kv._prompt_groups(ids, mask) == [0, 1, 0, 0]
+    mask2 = mask.clone()
+    mask2[2, 0] = 0  # same tokens, different padding: a different prompt
+    assert paged_kv._prompt_groups(ids, mask2) == [0, 1, 2, 0]
+    one = torch.tensor([[7, 8]]).expand(5, -1)
+    assert paged_kv._prompt_groups(one, torch.ones(1, 2, dtype=torch.long).expand(5, -1)) == [0] * 5
+
+
+def test_facade_return_prompt_layout(monkeypatch):
+    seen = {}
+
+    def fake_model(**kw):
+        seen.update(kw)
+        return torch.full((kw["input_ids"].shape[0], kw["max_new_tokens"]), 9, dtype=torch.int32)
+
+    monkeypatch.setattr(pkg, "paged_kv_decode_model", fake_model)
+    monkeypatch.setattr(pkg, "PAGED_KV_AVAILABLE", True)
+    ids = torch.tensor([[0, 0, 5, 6], [0, 7, 8, 9]])
+    mask = torch.tensor([[0, 0, 1, 1], [0, 1, 1, 1]])
+    out = pkg.paged_kv_decode("m", ids, mask, max_new_tokens=3, return_prompt=True, share_prompt_pages=False)
+    assert out.shape == (2, 7) and out.dtype == ids.dtype
+    assert torch.equal(out[:, :4], ids) and (out[:, 4:] == 9).all()  # the trainer's outputs[j, prompt_len:]
+    assert seen["share_prompt_pages"] is False and "return_prompt" not in seen
+    assert pkg.paged_kv_decode("m", ids, mask, max_new_tokens=3).shape == (2, 3)
+    assert seen["share_prompt_pages"] is True
+
+
 # ---------------------------------------------------------------------- sharding
 def test_lpt_assign_partitions_and_balances():
     import random
