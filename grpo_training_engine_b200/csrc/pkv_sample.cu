@@ -4,41 +4,47 @@
 // (src/triton_kernels/paged_kv.py:418-450, the same rule as
 // fused_ops.py:236-248): scaled = logits / max(T, 1e-6) in the logits dtype,
 // sort descending, softmax, running sum, drop every sorted token whose running
-// sum exceeds top_p except the first, renormalise, multinomial draw. At a
-// 151,936-token vocabulary that sort is most of a rollout step's sampling time.
+// sum exceeds top_p except the first, renormalise, then a multinomial draw
+// over the sorted probabilities. At a 151,936-token vocabulary that sort is
+// most of a rollout step's sampling time.
 //
 // Here one CTA handles one row without sorting. A token's mass is the fp32
 // exp of its scaled logit minus the row max, as 40-bit fixed point, so sums
 // are exact and independent of the order of summation (a probability is a
-// mass over the row total; below 2^-40 counts as 0). The cut is the scaled
-// value of the first token, in descending order, whose running mass exceeds
-// top_p x total: tokens above it are kept, and of the tokens tied at it the
-// ones that fit under top_p in index order (the order a stable sort gives
-// equal keys), and always the most likely token. The draw scales the caller's
-// uniform u in [0, 1) by the kept mass and inverts it over the kept tokens in
-// index order. The reference rounds probabilities and their running sum to
-// the logits dtype, so a token whose running probability lies within that
-// rounding of top_p can fall on the other side of the cut.
+// mass over the row total; below 2^-40 counts as 0). Tokens are ordered as
+// the reference's stable sort orders them: by scaled value descending, equal
+// values (a "group") by index. The cut is the group of the first token whose
+// running mass exceeds top_p x total: groups above it are kept, and of the
+// cut group the tokens that fit under top_p, in index order, and always the
+// most likely token. The draw scales the caller's uniform u in [0, 1) by the
+// kept mass and inverts it in the same order: the group where the running
+// mass passes the target, then the r-th token of that group in index order,
+// r = (target - mass above the group) / the group's per-token mass. The
+// reference rounds probabilities and their running sum to the logits dtype,
+// so a token whose running probability lies within that rounding of top_p can
+// fall on the other side of the cut.
 //
 // 16-bit logits (top_p16_kernel): a scaled logit and its mass depend only on
-// the token's 16-bit pattern, and the scaling is monotone in it. So the CTA
+// the token's 16-bit pattern, and the scaling is monotone in it, so a group is
+// a range of patterns. The CTA
 //   1. finds the largest pattern (in value order) of the row;
 //   2. counts the row's tokens per pattern in a window of the 49,152 patterns
 //      below it (every pattern under the window has zero mass; otherwise the
 //      radix path below runs);
-//   3. finds the cut from the counts alone: a scan of count x mass over the
-//      window, then a warp's search for the tie group's pattern range;
-//   4. reads the row once more for the draw, looking each kept token's mass
-//      up by its pattern.
-// Three passes over the row, with a shared-memory increment as the only
-// per-token work besides the loads.
+//   3. scans count x mass over the window, and one warp finds the cut, the
+//      kept mass, the target's group and r from the counts alone;
+//   4. finds the r-th token of that group's pattern range in index order:
+//      per-warp, per-sub-range and per-lane counts of matching keys.
+// Three passes over the row; the only per-token shared-memory work is the
+// count increment.
 //
 // fp32 logits, and rows whose window does not fit (fp16 at high temperature;
 // a +inf or NaN logit; all -inf), take the radix path: the max, then the cut
 // by a radix select over 8-bit digits of the order key of the scaled logit
 // (two passes for bf16, three for fp16, four for fp32), each pass a 256-bin
 // histogram of mass (one per warp, lanes with equal digits summed with warp
-// match / reduce), then the draw with masses computed per token.
+// match / reduce), a count of the cut group, the same radix select at the
+// target, and the same r-th token search.
 #include "pkv_common.cuh"
 
 namespace pkv {
@@ -49,6 +55,7 @@ constexpr int kSampleWarps = kSampleThreads / 32;
 constexpr int kBins = 256;
 constexpr int kTableBytes = 65536 * 2;
 constexpr int kHistBytes = kSampleWarps * kBins * 8;  // per-warp fixed-point mass histograms
+constexpr uint32_t FULL = 0xffffffffu;
 
 __device__ __forceinline__ uint32_t order_key(float x) {
   const uint32_t u = __float_as_uint(x);
@@ -60,8 +67,7 @@ __device__ __forceinline__ float key_value(uint32_t k) {
 }
 
 // Scaled logit as the reference computes it: logits / T rounded to the logits
-// dtype. For 16-bit logits it depends only on the 16-bit pattern, so it is
-// looked up in a 65,536-entry table that each CTA fills once (128 KB of smem).
+// dtype. For 16-bit logits it depends only on the 16-bit pattern.
 template <typename L> struct Scaled;
 template <> struct Scaled<float> {
   static constexpr bool kTable = false;
@@ -102,23 +108,113 @@ struct SampleArgs {
   int32_t flags;
 };
 
-// Masses are exp(x - row max) as 40-bit fixed point: integer sums are exact
-// and independent of the order of summation (below 2^-40 counts as 0).
+// low n bits (n >= 0) of a per-vector match mask
+__device__ __forceinline__ uint32_t low_bits(int n) { return n >= 32 ? FULL : (1u << max(n, 0)) - 1u; }
 
-// The radix path for one row (the CTA's), all threads of the CTA.
+// The index of the r-th (0-based) token of the row, in index order, among the
+// tokens that match, or -1; every thread of the CTA calls it and gets the
+// answer. load(b) gives the 16-byte vector of tokens [b, b + KV) (b a multiple
+// of KV; anything past the row), match(v, b) a bit per token of it. Three
+// levels of counts: contiguous warp ranges of the row, the 32 sub-ranges of
+// the chosen warp's range, the 32 lane slices of the chosen sub-range; the
+// chosen lane walks its slice.
+template <int KV, typename Load, typename Match>
+__device__ __forceinline__ int find_rth(int V, int r, Load load, Match match, int *s_cnt, int *s_res) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int kInFlight = 4;
+  const int sub = ((V + kSampleThreads - 1) / kSampleThreads + KV - 1) / KV * KV;  // per lane
+  const int span = 32 * sub;
+  // matches in [lo, hi), lanes strided by vectors, summed over the warp
+  auto count_range = [&](int lo, int hi) -> int {
+    int c = 0;
+    for (int b0 = lo + lane * KV; b0 < hi; b0 += kInFlight * 32 * KV) {
+      uint4 v[kInFlight];
+#pragma unroll
+      for (int h = 0; h < kInFlight; ++h) {
+        const int b = b0 + h * 32 * KV;
+        v[h] = b < hi ? load(b) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int h = 0; h < kInFlight; ++h) {
+        const int b = b0 + h * 32 * KV;
+        if (b < hi) c += __popc(match(v[h], b) & low_bits(hi - b));
+      }
+    }
+    return __reduce_add_sync(FULL, c);
+  };
+  // the lane whose inclusive count passes rr (counts one per lane), and the count before it
+  auto pick = [&](int c, int rr, int &before) -> int {
+    int inc = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(FULL, inc, o);
+      if (lane >= o) inc += u;
+    }
+    const int l = __ffs(__ballot_sync(FULL, rr < inc && rr >= inc - c)) - 1;
+    before = l >= 0 ? __shfl_sync(FULL, inc - c, l) : 0;
+    return l;
+  };
+  if (tid == 0) *s_res = -1;
+  const int wlo = min(V, warp * span), whi = min(V, wlo + span);
+  const int c1 = count_range(wlo, whi);
+  if (lane == 0) s_cnt[warp] = c1;
+  __syncthreads();
+  int b1 = 0;
+  const int W = pick(s_cnt[lane], r, b1);
+  if (W >= 0) {  // uniform across the CTA
+    const int r2 = r - b1;
+    const int Wlo = min(V, W * span), Whi = min(V, Wlo + span);
+    const int lo2 = min(Whi, Wlo + warp * sub), hi2 = min(Whi, lo2 + sub);
+    const int c2 = count_range(lo2, hi2);
+    __syncthreads();  // every warp has read the level-1 counts
+    if (lane == 0) s_cnt[warp] = c2;
+    __syncthreads();
+    int b2 = 0;
+    const int W2 = pick(s_cnt[lane], r2, b2);
+    if (W2 >= 0 && warp == W2) {
+      const int r3 = r2 - b2;
+      const int sub3 = ((sub + 31) / 32 + KV - 1) / KV * KV;
+      const int lo3 = min(Whi, Wlo + W2 * sub), hi3 = min(Whi, lo3 + sub);
+      const int llo = min(hi3, lo3 + lane * sub3), lhi = min(hi3, llo + sub3);
+      int c3 = 0;
+      for (int b0 = llo; b0 < lhi; b0 += KV) c3 += __popc(match(load(b0), b0) & low_bits(lhi - b0));
+      int b3 = 0;
+      const int L3 = pick(c3, r3, b3);
+      if (L3 >= 0 && lane == L3) {
+        int rr = r3 - b3, res = -1;
+        for (int b0 = llo; b0 < lhi && res < 0; b0 += KV) {
+          uint32_t m = match(load(b0), b0) & low_bits(lhi - b0);
+          const int n = __popc(m);
+          if (rr < n) {
+            for (; rr > 0; --rr) m &= m - 1;  // drop the rr lowest set bits
+            res = b0 + __ffs(m) - 1;
+          } else {
+            rr -= n;
+          }
+        }
+        *s_res = res;
+      }
+    }
+  }
+  __syncthreads();
+  return *s_res;
+}
+
+// ---------------------------------------------------------------------------
+// radix path
+// ---------------------------------------------------------------------------
+// One row (the CTA's), all threads of the CTA.
 template <typename L, int KEY_BITS>
 __device__ __forceinline__ void radix_top_p(const SampleArgs &a, uint8_t *sample_smem) {
   unsigned long long *whist = reinterpret_cast<unsigned long long *>(sample_smem);  // [warps][bins]
   uint16_t *scaled_tbl = reinterpret_cast<uint16_t *>(sample_smem + kHistBytes);    // 16-bit logits
   __shared__ float redm[kSampleWarps];
-  __shared__ unsigned long long s_top;  // top_p x the row's total mass
   __shared__ unsigned long long hmass[kBins];
-  __shared__ unsigned long long wmass[kSampleWarps];
-  __shared__ int wties[kSampleWarps];
+  __shared__ unsigned long long s_tot, s_thr, s_above;
   __shared__ uint32_t s_prefix;
-  __shared__ unsigned long long s_above;
   __shared__ int s_found;
-  __shared__ int s_pick;
+  __shared__ int s_cnt[kSampleWarps];
+  __shared__ int s_res;
   const L *row = reinterpret_cast<const L *>(a.logits) + (int64_t)blockIdx.x * a.row_stride;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int V = a.vocab;
@@ -129,29 +225,30 @@ __device__ __forceinline__ void radix_top_p(const SampleArgs &a, uint8_t *sample
   }
   auto scaled = [&](int i) { return Scaled<L>::get(row, i, t, scaled_tbl); };
   // The row is read as 16-byte vectors of kVec tokens (scalar loads when the
-  // row is not 16-byte aligned), two vectors per thread per step, so each
-  // thread keeps two loads in flight instead of one token.
+  // row is not 16-byte aligned), two vectors per thread per step.
   constexpr int kVec = 16 / (int)sizeof(L);
   constexpr int kStep = kSampleThreads * kVec;
   const bool vec_ok = (reinterpret_cast<uintptr_t>(row) & 15u) == 0;
+  auto load = [&](int base) -> uint4 {
+    if (vec_ok && base + kVec <= V) return __ldg(reinterpret_cast<const uint4 *>(row + base));
+    uint4 v = make_uint4(0, 0, 0, 0);
+    L *e = reinterpret_cast<L *>(&v);
+#pragma unroll
+    for (int j = 0; j < kVec; ++j)
+      if (base + j < V) e[j] = row[base + j];
+    return v;
+  };
   // scaled values of tokens [base, base + kVec); n of them are < V
-  auto fetch = [&](int base, float (&x)[kVec]) -> int {
+  auto fetch = [&](int base, float(&x)[kVec]) -> int {
     const int n = max(0, min(kVec, V - base));
-    if (vec_ok && n == kVec) {
-      const uint4 raw = *reinterpret_cast<const uint4 *>(row + base);
-      const L *e = reinterpret_cast<const L *>(&raw);
+    const uint4 raw = load(base);
+    const L *e = reinterpret_cast<const L *>(&raw);
 #pragma unroll
-      for (int j = 0; j < kVec; ++j) x[j] = Scaled<L>::get(e, j, t, scaled_tbl);
-    } else {
-#pragma unroll
-      for (int j = 0; j < kVec; ++j) x[j] = j < n ? scaled(base + j) : -INFINITY;
-    }
+    for (int j = 0; j < kVec; ++j) x[j] = j < n ? Scaled<L>::get(e, j, t, scaled_tbl) : -INFINITY;
     return n;
   };
 
-  // ---- 1. row max. Masses below are e = exp(x - max) in 40-bit fixed point
-  // (e <= 1); the row sum of e comes out of the first histogram as its total,
-  // and the nucleus bound is top_p times that sum, so no division per token.
+  // ---- row max; masses are e = exp(x - max) in 40-bit fixed point (e <= 1)
   float m = -INFINITY;
   for (int b0 = tid * kVec; b0 < V; b0 += 2 * kStep) {
     float x0[kVec], x1[kVec];
@@ -161,240 +258,161 @@ __device__ __forceinline__ void radix_top_p(const SampleArgs &a, uint8_t *sample
     for (int j = 0; j < kVec; ++j) m = fmaxf(m, fmaxf(x0[j], x1[j]));
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(FULL, m, o));
   if (lane == 0) redm[warp] = m;
   __syncthreads();
   m = lane < kSampleWarps ? redm[lane] : -INFINITY;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(FULL, m, o));
   const float row_max = m;
   auto pfix = [&](float x) -> unsigned long long {
     return __float2ull_rn(expf(x - row_max) * 1099511627776.0f);  // * 2^40
   };
-
-  // ---- 2. radix select of the cut key, 8 bits per pass from the top
-  if (tid == 0) {
-    s_prefix = 0;
-    s_above = 0;
-    s_found = 0;
-  }
-  unsigned long long *myhist = whist + warp * kBins;
-  constexpr int kPasses = KEY_BITS / 8;
   // Keys of 16-bit values converted to fp32 carry their information in the top
   // KEY_BITS bits; the rest are 0 for positive values and 1 for negative ones
   // (the order key complements those). They are cleared, so every token of one
-  // scaled value has the same key and the selected prefix is that key.
+  // scaled value (a group) has the same key.
   constexpr uint32_t kLowMask = KEY_BITS >= 32 ? 0u : (1u << (32 - KEY_BITS)) - 1u;
   auto rkey = [](float x) { return order_key(x) & ~kLowMask; };
+  auto group_value = [](uint32_t k) { return key_value((k & 0x80000000u) ? k : (k | kLowMask)); };
+
+  // ---- radix select, 8 bits per pass from the top: the key of the group
+  // holding the first token, in descending order, whose running mass exceeds
+  // thr (s_prefix; s_found = 0 when none does) and the mass above that group
+  // (s_above). With first set, the threshold is top_p x the row's total,
+  // taken from the first pass (s_tot).
+  unsigned long long *myhist = whist + warp * kBins;
+  constexpr int kPasses = KEY_BITS / 8;
+  auto radix_select = [&](unsigned long long thr, bool first) {
+    if (tid == 0) {
+      s_prefix = 0;
+      s_above = 0;
+      s_found = 0;
+      s_thr = thr;
+    }
 #pragma unroll 1
-  for (int pass = 0; pass < kPasses; ++pass) {
-    const int shift = 32 - 8 * (pass + 1);
-    for (int b = tid; b < kSampleWarps * kBins; b += kSampleThreads) whist[b] = 0;
-    __syncthreads();
-    const uint32_t prefix = s_prefix;
-    // every lane of the warp runs the same number of steps (the sync ops below)
-    for (int s0 = 0; s0 < V; s0 += 2 * kStep) {
-      float xs[2][kVec];
-      const int n0 = fetch(s0 + tid * kVec, xs[0]);
-      const int n1 = fetch(s0 + kStep + tid * kVec, xs[1]);
+    for (int pass = 0; pass < kPasses; ++pass) {
+      const int shift = 32 - 8 * (pass + 1);
+      for (int b = tid; b < kSampleWarps * kBins; b += kSampleThreads) whist[b] = 0;
+      __syncthreads();
+      const uint32_t prefix = s_prefix;
+      // every lane of the warp runs the same number of steps (the sync ops below)
+      for (int s0 = 0; s0 < V; s0 += 2 * kStep) {
+        float xs[2][kVec];
+        const int n0 = fetch(s0 + tid * kVec, xs[0]);
+        const int n1 = fetch(s0 + kStep + tid * kVec, xs[1]);
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
+        for (int h = 0; h < 2; ++h) {
 #pragma unroll
-        for (int j = 0; j < kVec; ++j) {
-          const float x = xs[h][j];
-          const uint32_t k = rkey(x);
-          const bool in = j < (h ? n1 : n0) && (pass == 0 || (k >> (shift + 8)) == (prefix >> (shift + 8)));
-          const uint32_t digit = in ? (k >> shift) & 0xffu : kBins;  // kBins: a group of its own
-          const unsigned long long p = in ? pfix(x) : 0ull;
-          // lanes with the same digit sum their masses (two 20-bit halves,
-          // exact) and the lowest of them adds the sum to the warp's histogram
-          const unsigned grp = __match_any_sync(0xffffffffu, digit);
-          const unsigned hs = __reduce_add_sync(grp, (unsigned)(p >> 20));
-          const unsigned ls = __reduce_add_sync(grp, (unsigned)(p & 0xfffffu));
-          if (in && lane == __ffs(grp) - 1) myhist[digit] += ((unsigned long long)hs << 20) + ls;
+          for (int j = 0; j < kVec; ++j) {
+            const float x = xs[h][j];
+            const uint32_t k = rkey(x);
+            const bool in = j < (h ? n1 : n0) && (pass == 0 || (k >> (shift + 8)) == (prefix >> (shift + 8)));
+            const uint32_t digit = in ? (k >> shift) & 0xffu : kBins;  // kBins: a group of its own
+            const unsigned long long p = in ? pfix(x) : 0ull;
+            // lanes with the same digit sum their masses (two 20-bit halves,
+            // exact) and the lowest of them adds the sum to the warp's histogram
+            const unsigned grp = __match_any_sync(FULL, digit);
+            const unsigned hs = __reduce_add_sync(grp, (unsigned)(p >> 20));
+            const unsigned ls = __reduce_add_sync(grp, (unsigned)(p & 0xfffffu));
+            if (in && lane == __ffs(grp) - 1) myhist[digit] += ((unsigned long long)hs << 20) + ls;
+          }
         }
       }
-    }
-    __syncthreads();
-    for (int b = tid; b < kBins; b += kSampleThreads) {
-      unsigned long long h = 0;
+      __syncthreads();
+      for (int b = tid; b < kBins; b += kSampleThreads) {
+        unsigned long long h = 0;
 #pragma unroll 8
-      for (int w = 0; w < kSampleWarps; ++w) h += whist[w * kBins + b];
-      hmass[b] = h;
+        for (int w = 0; w < kSampleWarps; ++w) h += whist[w * kBins + b];
+        hmass[b] = h;
+      }
+      __syncthreads();
+      if (tid == 0) {
+        if (pass == 0 && first) {  // the row's total mass; the nucleus bound top_p x total
+          unsigned long long tot = 0;
+          for (int b = 0; b < kBins; ++b) tot += hmass[b];
+          s_tot = tot;
+          s_thr = (unsigned long long)fmin((double)a.top_p * (double)tot, 4.0 * (double)tot);
+        }
+        const unsigned long long th = s_thr;
+        // first digit, from the top, at which the running mass exceeds th
+        unsigned long long run = s_above;
+        int d = kBins - 1;
+        for (; d >= 0; --d) {
+          if (hmass[d] == 0) continue;
+          if (run + hmass[d] > th) break;
+          run += hmass[d];
+        }
+        if (d < 0) {  // everything fits under th
+          s_found = 0;
+        } else {
+          s_found = 1;
+          s_above = run;
+          s_prefix = (pass == 0 ? 0u : s_prefix) | ((uint32_t)d << shift);
+        }
+      }
+      __syncthreads();
+      if (!s_found) break;
     }
-    __syncthreads();
-    if (tid == 0) {
-      if (pass == 0) {  // the row's total mass; the nucleus bound top_p x total
-        unsigned long long tot = 0;
-        for (int b = 0; b < kBins; ++b) tot += hmass[b];
-        s_top = (unsigned long long)fmin((double)a.top_p * (double)tot, 4.0 * (double)tot);
-      }
-      const unsigned long long top_p = s_top;
-      // first digit, from the top, at which the running mass exceeds top_p
-      unsigned long long run = s_above;
-      int d = kBins - 1;
-      for (; d >= 0; --d) {
-        if (hmass[d] == 0) continue;
-        if (run + hmass[d] > top_p) break;
-        run += hmass[d];
-      }
-      if (d < 0) {  // everything fits: the cut is below the smallest key
-        s_found = 0;
-      } else {
-        s_found = 1;
-        s_above = run;
-        s_prefix = (pass == 0 ? 0u : s_prefix) | ((uint32_t)d << shift);
-      }
-    }
-    __syncthreads();
-    if (!s_found) break;
-  }
+  };
+  auto match_key = [&](uint32_t key) {
+    return [&, key](const uint4 &v, int b0) -> uint32_t {
+      const L *e = reinterpret_cast<const L *>(&v);
+      uint32_t msk = 0;
+#pragma unroll
+      for (int j = 0; j < kVec; ++j)
+        if (b0 + j < V && rkey(Scaled<L>::get(e, j, t, scaled_tbl)) == key) msk |= 1u << j;
+      return msk;
+    };
+  };
+
+  // ---- the cut
+  radix_select(0ull, true);
   const bool found = s_found != 0;
   const uint32_t cut = s_prefix;
-  const unsigned long long above = s_above;
-  const unsigned long long top_p = s_top;
-  // tokens tied at the cut key that stay: while the running mass is <= top_p,
-  // and at least one token overall (the most likely one); the final pass caps
-  // it by the number of ties there are
-  const unsigned long long pc = found ? pfix(key_value((cut & 0x80000000u) ? cut : (cut | kLowMask))) : 0;
+  const unsigned long long top_p = s_thr, total = s_tot;
+  const unsigned long long above = found ? s_above : total;
+  const unsigned long long pc = found ? pfix(group_value(cut)) : 0;
+  // tokens in the cut group, and how many of them stay: while the running mass
+  // is <= top_p, and at least one token overall (the most likely one)
+  int n_ties = 0;
+  if (found) {
+    const auto mt = match_key(cut);
+    int c = 0;
+    for (int b0 = tid * kVec; b0 < V; b0 += kStep) c += __popc(mt(load(b0), b0));
+    c = __reduce_add_sync(FULL, c);
+    __syncthreads();
+    if (lane == 0) s_cnt[warp] = c;
+    __syncthreads();
+    n_ties = __reduce_add_sync(FULL, s_cnt[lane]);
+  }
   int keep_ties = 0;
   if (found) {
     if (pc > 0 && top_p > above) {
       const unsigned long long n = (top_p - above) / pc;
       keep_ties = n >= (unsigned long long)V ? V : (int)n;
     }
-    if (above == 0 && keep_ties == 0) keep_ties = 1;  // the most likely token always stays
+    if (above == 0 && keep_ties == 0) keep_ties = 1;
   }
-  auto kept_mass = [&](unsigned long long nontie, int ties) {
-    return nontie + (unsigned long long)min(ties, keep_ties) * pc;
-  };
-  // a token's share: its mass if above the cut (or no cut), flags a tie at it
-  auto classify = [&](float x, unsigned long long &p, bool &tie) {
-    const uint32_t k = rkey(x);
-    p = 0;
-    tie = false;
-    if (x == -INFINITY) return;
-    if (!found || k > cut) p = pfix(x);
-    else if (k == cut) tie = true;
-  };
-
-  // ---- 3. inverse CDF over the kept tokens in index order. Warp w owns the
-  // contiguous range [w * span, (w + 1) * span) (span a whole number of
-  // vectors per lane); the warp totals are scanned in warp order, and in the
-  // warp whose range holds the target each lane sums a contiguous 1/32 of the
-  // range, a lane scan finds the lane that holds it, and that lane walks.
-  const int sub = ((V + kSampleThreads - 1) / kSampleThreads + kVec - 1) / kVec * kVec;  // per lane
-  const int span = 32 * sub;
-  const int wlo = min(V, warp * span), whi = min(V, wlo + span);
-  unsigned long long lmass = 0;
-  int lties = 0;
-  for (int b0 = wlo + lane * kVec; b0 < whi; b0 += 32 * kVec) {
-    float x[kVec];
-    const int n = min(fetch(b0, x), whi - b0);
-#pragma unroll
-    for (int j = 0; j < kVec; ++j) {
-      unsigned long long p;
-      bool tie;
-      classify(x[j], p, tie);
-      if (j < n) {
-        lmass += p;
-        lties += tie ? 1 : 0;
-      }
+  const unsigned long long kept = above + (unsigned long long)min(n_ties, keep_ties) * pc;
+  // ---- the draw
+  int token = -1;
+  if (kept > 0) {  // uniform
+    const unsigned long long target = (unsigned long long)((double)a.uniforms[blockIdx.x] * (double)kept);
+    uint32_t gkey;
+    unsigned long long r;
+    if (target < above) {
+      radix_select(target, false);  // found: target < above <= total
+      gkey = s_prefix;
+      r = (target - s_above) / pfix(group_value(gkey));
+    } else {
+      gkey = cut;
+      r = (target - above) / pc;
     }
+    __syncthreads();
+    token = find_rth<kVec>(V, (int)min(r, (unsigned long long)V), load, match_key(gkey), s_cnt, &s_res);
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    lmass += __shfl_xor_sync(0xffffffffu, lmass, o);
-    lties += __shfl_xor_sync(0xffffffffu, lties, o);
-  }
-  if (lane == 0) {
-    wmass[warp] = lmass;
-    wties[warp] = lties;
-  }
-  if (tid == 0) s_pick = -1;
-  __syncthreads();
-  // warp scan of the warp totals: non-tie mass and ties before warp w
-  unsigned long long mi = lane < kSampleWarps ? wmass[lane] : 0;
-  int ti = lane < kSampleWarps ? wties[lane] : 0;
-  const unsigned long long mv = mi;
-  const int tv = ti;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const unsigned long long a2 = __shfl_up_sync(0xffffffffu, mi, o);
-    const int b2 = __shfl_up_sync(0xffffffffu, ti, o);
-    if (lane >= o) {
-      mi += a2;
-      ti += b2;
-    }
-  }
-  const unsigned long long wm_before = __shfl_sync(0xffffffffu, mi - mv, warp);
-  const int wt_before = __shfl_sync(0xffffffffu, ti - tv, warp);
-  const unsigned long long wm_incl = __shfl_sync(0xffffffffu, mi, warp);
-  const int wt_incl = __shfl_sync(0xffffffffu, ti, warp);
-  const unsigned long long total = kept_mass(__shfl_sync(0xffffffffu, mi, 31), __shfl_sync(0xffffffffu, ti, 31));
-  const unsigned long long target =
-      (unsigned long long)((double)a.uniforms[blockIdx.x] * (double)total);  // < total
-  const unsigned long long kb = kept_mass(wm_before, wt_before), ki = kept_mass(wm_incl, wt_incl);
-  if (ki > kb && kb <= target && target < ki) {
-    const int llo = min(whi, wlo + lane * sub), lhi = min(whi, llo + sub);
-    unsigned long long lm = 0;
-    int lt = 0;
-    for (int b0 = llo; b0 < lhi; b0 += kVec) {
-      float x[kVec];
-      const int n = min(fetch(b0, x), lhi - b0);
-#pragma unroll
-      for (int j = 0; j < kVec; ++j) {
-        unsigned long long p;
-        bool tie;
-        classify(x[j], p, tie);
-        if (j < n) {
-          lm += p;
-          lt += tie ? 1 : 0;
-        }
-      }
-    }
-    unsigned long long sm = lm;
-    int st = lt;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const unsigned long long a2 = __shfl_up_sync(0xffffffffu, sm, o);
-      const int b2 = __shfl_up_sync(0xffffffffu, st, o);
-      if (lane >= o) {
-        sm += a2;
-        st += b2;
-      }
-    }
-    const unsigned long long nb = wm_before + sm - lm;
-    const int tb = wt_before + st - lt;
-    const unsigned long long lkb = kept_mass(nb, tb), lki = kept_mass(nb + lm, tb + lt);
-    if (lki > lkb && lkb <= target && target < lki) {
-      unsigned long long run = lkb;
-      int ties = tb, pick = -1, last = -1;
-      for (int b0 = llo; b0 < lhi && pick < 0; b0 += kVec) {
-        float x[kVec];
-        const int n = min(fetch(b0, x), lhi - b0);
-#pragma unroll
-        for (int j = 0; j < kVec; ++j) {
-          unsigned long long p;
-          bool tie;
-          classify(x[j], p, tie);
-          if (j >= n || pick >= 0) continue;
-          if (tie) {
-            if (ties < keep_ties) p = pc;
-            ++ties;
-          }
-          if (p > 0) {
-            last = b0 + j;
-            run += p;
-            if (target < run) pick = b0 + j;
-          }
-        }
-      }
-      s_pick = pick >= 0 ? pick : last;  // exactly one lane of the CTA gets here
-    }
-  }
-  __syncthreads();
-  if (tid == 0) a.out[blockIdx.x] = s_pick >= 0 ? s_pick : 0;
+  if (tid == 0) a.out[blockIdx.x] = token >= 0 ? token : 0;
 }
 
 template <typename L, int KEY_BITS>
@@ -408,7 +426,7 @@ __global__ void __launch_bounds__(kSampleThreads, 1) top_p_kernel(SampleArgs a) 
 // ---------------------------------------------------------------------------
 constexpr int kWindow = 49152;  // patterns counted per row: 192 KB of counts
 static_assert(kWindow * 4 <= kHistBytes + kTableBytes, "both paths share one dynamic smem size");
-static_assert(kWindow % (4 * kSampleThreads) == 0 && kWindow <= 64 * kSampleThreads, "window layout");
+static_assert(kWindow % (4 * kSampleThreads) == 0, "window layout");
 
 // order key of a 16-bit float pattern (larger value, larger key) and back
 __device__ __forceinline__ uint32_t key16(uint32_t u) {
@@ -432,339 +450,350 @@ template <> struct Bits16<__half> {
 template <typename L, int KEY_BITS>
 __global__ void __launch_bounds__(kSampleThreads, 1) top_p16_kernel(SampleArgs a) {
   extern __shared__ __align__(16) uint8_t sample_smem[];
-  uint32_t *cnt = reinterpret_cast<uint32_t *>(sample_smem);  // [kWindow] token count per pattern
-  float *etab = reinterpret_cast<float *>(sample_smem);       // later: exp(scaled - max) per kept pattern
-  __shared__ unsigned long long tex[kSampleThreads];  // exclusive prefix of each thread's window mass
+  uint32_t *cnt = reinterpret_cast<uint32_t *>(sample_smem);  // [kWindow] token count per pattern key - klo
+  // Positions (patterns in descending order from the max) in groups of 128,
+  // one uint4 of counts per lane; group g is summed by warp g % 32, and warp
+  // w's prefix range is groups [w * kWarpGroups, (w + 1) * kWarpGroups).
+  constexpr int kGroup = 128;
+  constexpr int kNumGroups = kWindow / kGroup;
+  constexpr int kWarpGroups = kNumGroups / kSampleWarps;
+  static_assert(kWarpGroups <= 32, "one group per lane in a warp's prefix range");
+  __shared__ unsigned long long gsum[kNumGroups];  // window mass per group
   __shared__ unsigned long long wsum[kSampleWarps];
   __shared__ uint32_t redk[kSampleWarps];
-  __shared__ unsigned long long wmass[kSampleWarps];
-  __shared__ int wties[kSampleWarps];
-  __shared__ int s_owner, s_glo, s_ghi, s_pick;
-  __shared__ unsigned long long s_above, s_pc;
+  __shared__ int s_lo, s_hi, s_r;
+  __shared__ int s_cnt[kSampleWarps];
+  __shared__ int s_res;
 
-  const uint32_t FULL = 0xffffffffu;
   const uint16_t *row = reinterpret_cast<const uint16_t *>(a.logits) + (int64_t)blockIdx.x * a.row_stride;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int V = a.vocab;
   const float t = a.temperature;
   constexpr int kVec = 8;  // tokens per 16-byte vector
   constexpr int kStep = kSampleThreads * kVec;
+  constexpr int kInFlight = 4;  // vectors per thread per step of a pass
   constexpr uint32_t kNoKey = 0x10000u;  // past the end of the row: above every pattern's key
   const bool vec_ok = (reinterpret_cast<uintptr_t>(row) & 15u) == 0;
-  auto fetch = [&](int base, uint32_t(&k)[kVec]) -> int {
-    const int n = max(0, min(kVec, V - base));
-    if (vec_ok && n == kVec) {
-      const uint4 raw = *reinterpret_cast<const uint4 *>(row + base);
-      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  // the row is read twice: start pulling all of it into L2 now
+  if (vec_ok && warp == 0) {
+    const uint32_t bytes = (uint32_t)V * 2u & ~15u;
+    const uint32_t chunk = ((bytes + 31u) / 32u + 15u) & ~15u;
+    const uint32_t off = (uint32_t)lane * chunk;
+    if (off < bytes)
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<const uint8_t *>(row) + off),
+                   "r"(min(chunk, bytes - off))
+                   : "memory");
+  }
+  // 16-byte vector of tokens [base, base + 8); 0 past the row
+  auto load = [&](int base) -> uint4 {
+    if (vec_ok && base + kVec <= V) return __ldg(reinterpret_cast<const uint4 *>(row + base));
+    uint32_t w[4] = {0, 0, 0, 0};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        k[2 * j] = key16(w[j] & 0xffffu);
-        k[2 * j + 1] = key16(w[j] >> 16);
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < kVec; ++j) k[j] = j < n ? key16(row[base + j]) : kNoKey;
-    }
-    return n;
+    for (int j = 0; j < kVec; ++j)
+      if (base + j < V) w[j >> 1] |= (uint32_t)row[base + j] << (16 * (j & 1));
+    return make_uint4(w[0], w[1], w[2], w[3]);
   };
+  auto half_at = [](const uint4 &v, int j) -> uint32_t {
+    const uint32_t w = j < 2 ? v.x : j < 4 ? v.y : j < 6 ? v.z : v.w;
+    return (j & 1) ? w >> 16 : w & 0xffffu;
+  };
+  // key of token j of a loaded vector; kNoKey past the end of the row
+  auto key_at = [&](const uint4 &v, int base, int j) -> uint32_t {
+    return base + j < V ? key16(half_at(v, j)) : kNoKey;
+  };
+  auto sbits = [&](uint32_t k) -> uint32_t { return Scaled<L>::scale_bits((uint16_t)raw16(k), t); };
+  auto pfix = [](float e) -> unsigned long long { return __float2ull_rn(e * 1099511627776.0f); };  // * 2^40
+  auto block_max = [&](uint32_t v) {
+    v = __reduce_max_sync(FULL, v);
+    __syncthreads();  // redk is free
+    if (lane == 0) redk[warp] = v;
+    __syncthreads();
+    return __reduce_max_sync(FULL, redk[lane]);
+  };
+  for (int i = tid * 4; i < kWindow; i += kSampleThreads * 4) *reinterpret_cast<uint4 *>(cnt + i) = make_uint4(0, 0, 0, 0);
 
-  // ---- 1. the row's largest pattern
+  // ---- 1. token counts per pattern key in a window [klo, khi] of kWindow keys,
+  // with the row max found in the same pass. The window's top is the max of
+  // the first step's tokens plus a margin; if the row max lies above it, or a
+  // pattern under the window has mass, the row is counted again below.
+  uint4 v0[kInFlight];
+#pragma unroll
+  for (int h = 0; h < kInFlight; ++h) v0[h] = load(tid * kVec + h * kStep);
   uint32_t km = 0;
-  for (int b0 = tid * kVec; b0 < V; b0 += 2 * kStep) {
-    uint32_t k0[kVec], k1[kVec];
-    fetch(b0, k0);
-    fetch(b0 + kStep, k1);
+#pragma unroll
+  for (int h = 0; h < kInFlight; ++h)
 #pragma unroll
     for (int j = 0; j < kVec; ++j) {
-      if (k0[j] != kNoKey) km = max(km, k0[j]);
-      if (k1[j] != kNoKey) km = max(km, k1[j]);
+      const uint32_t k = key_at(v0[h], tid * kVec + h * kStep, j);
+      if (k != kNoKey) km = max(km, k);
     }
-  }
-  km = __reduce_max_sync(FULL, km);
-  if (lane == 0) redk[warp] = km;
-  __syncthreads();
-  const uint32_t kmax = __reduce_max_sync(FULL, lane < kSampleWarps ? redk[lane] : 0u);
+  const uint32_t kmax0 = block_max(km);  // also orders the zeroing before the counting
+  constexpr uint32_t kMargin = 1024;     // 8 binades of bf16 above the first step's max
+  int khi = (int)min(kmax0 + kMargin, 0xffffu);
+  int klo = max(khi - kWindow + 1, 0);
+  // count the tokens of one vector: a vector of one pattern (flat or padded
+  // rows) takes one increment, any other one increment per token
+  auto count_vec = [&](const uint4 &v, int base) {
+    uint32_t k[kVec];
+    if (base + kVec <= V) {
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) k[j] = key16(half_at(v, j));
+    } else {
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) k[j] = key_at(v, base, j);
+    }
+    bool same = true;
+#pragma unroll
+    for (int j = 1; j < kVec; ++j) same &= k[j] == k[0];
+    if (same) {
+      if (k[0] != kNoKey) {
+        km = max(km, k[0]);
+        if (k[0] - (uint32_t)klo <= (uint32_t)(khi - klo)) atomicAdd(&cnt[k[0] - klo], (uint32_t)kVec);
+      }
+      return;
+    }
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+      if (k[j] == kNoKey) continue;
+      km = max(km, k[j]);
+      if (k[j] - (uint32_t)klo <= (uint32_t)(khi - klo)) atomicAdd(&cnt[k[j] - klo], 1u);
+    }
+  };
+  auto count_rest = [&](int from) {
+    for (int b0 = from + tid * kVec; b0 < V; b0 += kInFlight * kStep) {
+      uint4 v[kInFlight];
+#pragma unroll
+      for (int h = 0; h < kInFlight; ++h) v[h] = load(b0 + h * kStep);
+#pragma unroll
+      for (int h = 0; h < kInFlight; ++h) count_vec(v[h], b0 + h * kStep);
+    }
+  };
+#pragma unroll
+  for (int h = 0; h < kInFlight; ++h) count_vec(v0[h], tid * kVec + h * kStep);
+  count_rest(kInFlight * kStep);
+  const uint32_t kmax = block_max(km);
 
   // scaled value of the pattern with key k, and its mass relative to the max
-  auto sbits = [&](uint32_t k) -> uint32_t { return Scaled<L>::scale_bits((uint16_t)raw16(k), t); };
   const float smax = Bits16<L>::to_float(sbits(kmax));
   auto emass = [&](uint32_t k) { return expf(Bits16<L>::to_float(sbits(k)) - smax); };
-  auto pfix = [](float e) -> unsigned long long { return __float2ull_rn(e * 1099511627776.0f); };  // * 2^40
-
-  // the window: the kWindow patterns up to the max; everything below must be
-  // massless, and the max finite (no +inf or NaN, not all -inf)
-  const int nb = (int)min((uint32_t)kWindow, kmax + 1);
-  const int klo = (int)kmax - nb + 1;
-  const bool window_ok = !(a.flags & PKV_SAMPLE_FORCE_RADIX) && kmax < key16(Bits16<L>::kPosInf) &&
-                         kmax > key16(Bits16<L>::kNegInf) && (klo == 0 || pfix(emass(klo - 1)) == 0);
-  if (!window_ok) {  // uniform across the CTA
+  // rows the window cannot serve: a +inf or NaN max, all -inf, forced radix
+  if ((a.flags & PKV_SAMPLE_FORCE_RADIX) || kmax >= key16(Bits16<L>::kPosInf) || kmax <= key16(Bits16<L>::kNegInf)) {
     radix_top_p<L, KEY_BITS>(a, sample_smem);
     return;
   }
-
-  // ---- 2. token counts per pattern (runs of equal neighbours added at once)
-  for (int i = tid * 4; i < nb; i += kSampleThreads * 4) *reinterpret_cast<uint4 *>(cnt + i) = make_uint4(0, 0, 0, 0);
-  __syncthreads();
-  auto add_run = [&](uint32_t k, uint32_t n) {
-    if (k >= (uint32_t)klo && k <= kmax) atomicAdd(&cnt[k - klo], n);
-  };
-  for (int b0 = tid * kVec; b0 < V; b0 += 2 * kStep) {
-    uint32_t ks[2][kVec];
-    fetch(b0, ks[0]);
-    fetch(b0 + kStep, ks[1]);
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      uint32_t prev = ks[h][0], run = 1;
-#pragma unroll
-      for (int j = 1; j < kVec; ++j) {
-        if (ks[h][j] == prev) {
-          ++run;
-        } else {
-          add_run(prev, run);
-          prev = ks[h][j];
-          run = 1;
-        }
-      }
-      add_run(prev, run);
+  if ((int)kmax > khi || (klo > 0 && pfix(emass((uint32_t)klo - 1)) != 0)) {  // uniform
+    // the window from the row max: [kmax - kWindow + 1, kmax]
+    khi = (int)kmax;
+    klo = max(khi - kWindow + 1, 0);
+    if (klo > 0 && pfix(emass((uint32_t)klo - 1)) != 0) {  // massful patterns beyond any window
+      radix_top_p<L, KEY_BITS>(a, sample_smem);
+      return;
     }
+    for (int i = tid * 4; i < kWindow; i += kSampleThreads * 4) *reinterpret_cast<uint4 *>(cnt + i) = make_uint4(0, 0, 0, 0);
+    __syncthreads();
+    count_rest(0);
+    __syncthreads();
+  }
+
+  // ---- 2. masses over the window. Position j = 0, 1, ... is pattern kmax - j
+  // (bin jmax - j); positions past jmax count nothing.
+  const int jmax = (int)kmax - klo;
+  auto count_at = [&](int j) -> uint32_t { return j <= jmax ? cnt[jmax - j] : 0u; };
+  auto warp_sum = [&](unsigned long long v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+    return v;
+  };
+  // the counts of positions [j, j + 4) (bins jmax - 3 - j .. jmax - j), one 16-byte read when aligned
+  auto counts4 = [&](int j, uint32_t(&c)[4]) {
+    if (j + 3 <= jmax && ((jmax - 3 - j) & 3) == 0) {
+      const uint4 q = *reinterpret_cast<const uint4 *>(cnt + jmax - 3 - j);
+      c[0] = q.w;
+      c[1] = q.z;
+      c[2] = q.y;
+      c[3] = q.x;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) c[e] = count_at(j + e);
+    }
+  };
+  for (int g = warp; g < kNumGroups; g += kSampleWarps) {
+    const int j = g * kGroup + 4 * lane;
+    uint32_t c[4];
+    counts4(j, c);
+    const bool has = (c[0] | c[1] | c[2] | c[3]) != 0u;
+    unsigned long long m = 0;
+    if (__any_sync(FULL, has)) {
+      if (has) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (c[e]) m += (unsigned long long)c[e] * pfix(emass(kmax - (j + e)));
+      }
+      m = warp_sum(m);
+    }
+    if (lane == 0) gsum[g] = m;
+  }
+  __syncthreads();
+  {
+    const unsigned long long v = warp_sum(lane < kWarpGroups ? gsum[warp * kWarpGroups + lane] : 0ull);
+    if (lane == 0) wsum[warp] = v;
   }
   __syncthreads();
 
-  // ---- 3. the cut. Position j = 0, 1, ... is pattern kmax - j (descending);
-  // thread i owns positions [i * cs, (i + 1) * cs).
-  const int cs = (nb + kSampleThreads - 1) / kSampleThreads;  // <= 48
-  auto pos_mass = [&](int j) -> unsigned long long {
-    const uint32_t c = cnt[nb - 1 - j];
-    return c ? (unsigned long long)c * pfix(emass(kmax - j)) : 0ull;
-  };
-  const int j0 = min(nb, tid * cs), j1 = min(nb, j0 + cs);
-  unsigned long long S = 0;
-  for (int j = j0; j < j1; ++j) S += pos_mass(j);
-  unsigned long long inc = S;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const unsigned long long v = __shfl_up_sync(FULL, inc, o);
-    if (lane >= o) inc += v;
-  }
-  if (lane == 31) wsum[warp] = inc;
-  __syncthreads();
+  // ---- 3. one warp: the cut, the kept mass, the target's group and r
   if (warp == 0) {
-    unsigned long long w = wsum[lane];
+    unsigned long long wincl = wsum[lane];  // inclusive prefix of the warp totals
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const unsigned long long v = __shfl_up_sync(FULL, w, o);
-      if (lane >= o) w += v;
+      const unsigned long long v = __shfl_up_sync(FULL, wincl, o);
+      if (lane >= o) wincl += v;
     }
-    wsum[lane] = w;
-  }
-  if (tid == 0) s_owner = -1;
-  __syncthreads();
-  const unsigned long long texcl = (warp ? wsum[warp - 1] : 0ull) + inc - S;
-  tex[tid] = texcl;
-  const unsigned long long total = wsum[kSampleWarps - 1];
-  const unsigned long long top_p = (unsigned long long)fmin((double)a.top_p * (double)total, 4.0 * (double)total);
-  const bool found = total > top_p;
-  if (found && texcl <= top_p && top_p < texcl + S) s_owner = tid;
-  __syncthreads();
-  if (found && warp == (s_owner >> 5)) {
-    // the owner's positions, two per lane, in order: the first whose running mass exceeds top_p
-    const int ow = s_owner, oj0 = min(nb, ow * cs), oj1 = min(nb, oj0 + cs);
-    const int pa = oj0 + lane, pb = oj0 + 32 + lane;
-    const unsigned long long ma = pa < oj1 ? pos_mass(pa) : 0ull, mb = pb < oj1 ? pos_mass(pb) : 0ull;
-    unsigned long long ia = ma, ib = mb;
+    const unsigned long long total = __shfl_sync(FULL, wincl, 31);
+    auto wexcl_of = [&](int w) { return __shfl_sync(FULL, wincl, w) - wsum[w]; };  // warp-uniform w
+    auto excl_scan = [&](unsigned long long v) {
+      unsigned long long i = v;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const unsigned long long va = __shfl_up_sync(FULL, ia, o), vb = __shfl_up_sync(FULL, ib, o);
-      if (lane >= o) {
-        ia += va;
-        ib += vb;
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long u = __shfl_up_sync(FULL, i, o);
+        if (lane >= o) i += u;
       }
-    }
-    const unsigned long long base = tex[ow], ta = __shfl_sync(FULL, ia, 31);
-    const unsigned ba = __ballot_sync(FULL, pa < oj1 && base + ia > top_p);
-    const unsigned bb = __ballot_sync(FULL, pb < oj1 && base + ta + ib > top_p);
-    const int jstar = ba ? oj0 + __ffs(ba) - 1 : oj0 + 32 + __ffs(bb) - 1;  // exists: the owner's range crosses top_p
-    const uint32_t kstar = kmax - (uint32_t)jstar;
-    const uint32_t sstar = key16(sbits(kstar));
-    // the patterns tied with it (same scaled value) form a range [glo, ghi]
-    int lo = (int)kstar, hi = (int)kmax;
-    while (lo < hi) {
-      const int step = (hi - lo + 31) / 32;
-      const int c = lo + (lane + 1) * step;
-      const int n = __popc(__ballot_sync(FULL, c <= hi && key16(sbits((uint32_t)c)) == sstar));
-      lo += n * step;
-      hi = min(hi, lo + step - 1);
-    }
-    const int ghi = lo;
-    lo = klo;
-    hi = (int)kstar;
-    while (lo < hi) {
-      const int step = (hi - lo + 31) / 32;
-      const int c = hi - (lane + 1) * step;
-      const int n = __popc(__ballot_sync(FULL, c >= lo && key16(sbits((uint32_t)c)) == sstar));
-      hi -= n * step;
-      lo = max(lo, hi - step + 1);
-    }
-    const int glo = hi;
-    // mass above the tie group: positions before jhi = kmax - ghi
-    const int jhi = (int)kmax - ghi, th = jhi / cs, hj0 = th * cs;
-    unsigned long long part = (hj0 + lane < jhi ? pos_mass(hj0 + lane) : 0ull) +
-                              (hj0 + 32 + lane < jhi ? pos_mass(hj0 + 32 + lane) : 0ull);
+      return i - v;
+    };
+    // The first position whose running mass exceeds thr (thr < total), the
+    // mass of the positions before it and its per-token mass.
+    auto first_over = [&](unsigned long long thr, unsigned long long &before, unsigned long long &per) -> int {
+      const int ow = __ffs(__ballot_sync(FULL, wincl > thr && wincl - wsum[lane] <= thr)) - 1;
+      const unsigned long long base = wexcl_of(ow);
+      const unsigned long long gv = lane < kWarpGroups ? gsum[ow * kWarpGroups + lane] : 0ull;
+      const unsigned long long gex = excl_scan(gv);
+      const int gl = __ffs(__ballot_sync(FULL, lane < kWarpGroups && base + gex + gv > thr)) - 1;
+      const int jg = (ow * kWarpGroups + gl) * kGroup;
+      const unsigned long long gbase = base + __shfl_sync(FULL, gex, gl);
+      uint32_t c[4];
+      counts4(jg + 4 * lane, c);
+      unsigned long long pf[4], lm = 0;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(FULL, part, o);
+      for (int e = 0; e < 4; ++e) {
+        pf[e] = c[e] ? pfix(emass(kmax - (jg + 4 * lane + e))) : 0ull;
+        lm += c[e] * pf[e];
+      }
+      const unsigned long long lex = excl_scan(lm);
+      const int ll = __ffs(__ballot_sync(FULL, gbase + lex + lm > thr)) - 1;
+      int j = 0;
+      unsigned long long run = 0, p = 0;
+      if (lane == ll) {
+        run = gbase + lex;
+        int e = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (e == q && run + c[q] * pf[q] <= thr) {
+            run += c[q] * pf[q];
+            ++e;
+          }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (q == e) p = pf[q];
+        j = jg + 4 * lane + e;
+      }
+      before = __shfl_sync(FULL, run, ll);
+      per = __shfl_sync(FULL, p, ll);
+      return __shfl_sync(FULL, j, ll);
+    };
+    // the pattern range [glo, ghi] of the group (same scaled value) of
+    // position j, and the mass above the group (before: the mass of the
+    // positions before j)
+    auto group_of = [&](int j, unsigned long long before, int &glo, int &ghi) -> unsigned long long {
+      const uint32_t k = kmax - (uint32_t)j;
+      const uint32_t sk = sbits(k);
+      // neighbours first: a group is usually one pattern
+      const int nbk = lane == 0 ? (int)k + 1 : (int)k - 1;
+      const bool same = lane < 2 && nbk >= klo && nbk <= (int)kmax && sbits((uint32_t)nbk) == sk;
+      const unsigned nbr = __ballot_sync(FULL, same);
+      ghi = (int)k;
+      glo = (int)k;
+      if (nbr & 1u) {
+        int lo = (int)k + 1, hi = (int)kmax;
+        while (lo < hi) {
+          const int step = (hi - lo + 31) / 32;
+          const int c = lo + (lane + 1) * step;
+          const int n = __popc(__ballot_sync(FULL, c <= hi && sbits((uint32_t)c) == sk));
+          lo += n * step;
+          hi = min(hi, lo + step - 1);
+        }
+        ghi = lo;
+      }
+      if (nbr & 2u) {
+        int lo = klo, hi = (int)k - 1;
+        while (lo < hi) {
+          const int step = (hi - lo + 31) / 32;
+          const int c = hi - (lane + 1) * step;
+          const int n = __popc(__ballot_sync(FULL, c >= lo && sbits((uint32_t)c) == sk));
+          hi -= n * step;
+          lo = max(lo, hi - step + 1);
+        }
+        glo = hi;
+      }
+      if (ghi == (int)k) return before;
+      // the mass of positions [kmax - ghi, j): patterns above k in the group
+      unsigned long long part = 0;
+      for (int q = (int)kmax - ghi + lane; q < j; q += 32) part += (unsigned long long)count_at(q) * pfix(emass(kmax - q));
+      return before - warp_sum(part);
+    };
+    // tokens with a pattern in [lo, hi]
+    auto tokens_in = [&](int lo, int hi) {
+      unsigned c = 0;
+      for (int k = lo + lane; k <= hi; k += 32) c += cnt[k - klo];
+      return (int)__reduce_add_sync(FULL, c);
+    };
+    const unsigned long long top_p = (unsigned long long)fmin((double)a.top_p * (double)total, 4.0 * (double)total);
+    const bool found = total > top_p;
+    int glo = 0, ghi = -1, n_ties = 0, keep_ties = 0;
+    unsigned long long above = total, pc = 0;
+    if (found) {
+      unsigned long long before;
+      const int jc = first_over(top_p, before, pc);
+      above = group_of(jc, before, glo, ghi);
+      n_ties = tokens_in(glo, ghi);
+      if (pc > 0 && top_p > above) {
+        const unsigned long long n = (top_p - above) / pc;
+        keep_ties = n >= (unsigned long long)V ? V : (int)n;
+      }
+      if (above == 0 && keep_ties == 0) keep_ties = 1;  // the most likely token always stays
+    }
+    const unsigned long long kept = above + (unsigned long long)min(n_ties, keep_ties) * pc;
+    const unsigned long long target = (unsigned long long)((double)a.uniforms[blockIdx.x] * (double)kept);
+    int lo = glo, hi = ghi;
+    unsigned long long r = 0;
+    if (target < above) {
+      unsigned long long before, per;
+      const int jt = first_over(target, before, per);
+      r = (target - group_of(jt, before, lo, hi)) / per;
+    } else if (pc > 0) {
+      r = (target - above) / pc;
+    }
     if (lane == 0) {
-      s_glo = glo;
-      s_ghi = ghi;
-      s_above = (th < kSampleThreads ? tex[th] : total) + part;
-      s_pc = pfix(emass(kstar));
+      s_lo = lo;
+      s_hi = hi;
+      s_r = (int)min(r, (unsigned long long)V);
     }
-  } else if (!found && tid == 0) {
-    s_glo = klo - 1;
-    s_ghi = klo - 1;
-    s_above = 0;
-    s_pc = 0;
   }
   __syncthreads();
-  const int glo = s_glo, ghi = s_ghi;
-  const unsigned long long above = s_above, pc = s_pc;
-  int keep_ties = 0;
-  if (found) {
-    if (pc > 0 && top_p > above) {
-      const unsigned long long n = (top_p - above) / pc;
-      keep_ties = n >= (unsigned long long)V ? V : (int)n;
-    }
-    if (above == 0 && keep_ties == 0) keep_ties = 1;  // the most likely token always stays
-  }
-  // masses of the kept patterns, in place of their counts
-  for (int j = j0; j < min(j1, (int)kmax - ghi); ++j) {
-    const int b = nb - 1 - j;
-    if (cnt[b]) etab[b] = emass(kmax - j);
-  }
-  __syncthreads();
-  auto kept_mass = [&](unsigned long long nontie, int ties) {
-    return nontie + (unsigned long long)min(ties, keep_ties) * pc;
-  };
-  auto classify = [&](uint32_t k, unsigned long long &p, bool &tie) {
-    p = 0;
-    tie = false;
-    if (k > kmax) return;  // past the end of the row
-    if ((int)k > ghi) p = pfix(etab[k - klo]);
-    else if (found && (int)k >= glo) tie = true;
-  };
 
-  // ---- 4. inverse CDF over the kept tokens in index order: per-warp totals
-  // over contiguous ranges, the warp holding the target splits its range into
-  // lane slices, and the lane holding it walks its slice.
-  const int sub = ((V + kSampleThreads - 1) / kSampleThreads + kVec - 1) / kVec * kVec;  // per lane
-  const int span = 32 * sub;
-  const int wlo = min(V, warp * span), whi = min(V, wlo + span);
-  unsigned long long lmass = 0;
-  int lties = 0;
-  for (int b0 = wlo + lane * kVec; b0 < whi; b0 += 32 * kVec) {
-    uint32_t k[kVec];
-    const int n = min(fetch(b0, k), whi - b0);
+  // ---- 4. the r-th token, in index order, with a pattern key in [lo, hi]. A
+  // group's patterns share a sign, so the key range is one range of raw
+  // patterns (increasing with the key for positive values, decreasing for
+  // negative ones).
+  const uint32_t rk0 = raw16((uint32_t)s_lo), rk1 = raw16((uint32_t)s_hi);
+  const uint32_t rlo = min(rk0, rk1), rspan = max(rk0, rk1) - rlo;
+  const auto match = [&](const uint4 &v, int b0) -> uint32_t {
+    uint32_t msk = 0;
 #pragma unroll
-    for (int j = 0; j < kVec; ++j) {
-      unsigned long long p;
-      bool tie;
-      classify(k[j], p, tie);
-      if (j < n) {
-        lmass += p;
-        lties += tie ? 1 : 0;
-      }
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    lmass += __shfl_xor_sync(FULL, lmass, o);
-    lties += __shfl_xor_sync(FULL, lties, o);
-  }
-  if (lane == 0) {
-    wmass[warp] = lmass;
-    wties[warp] = lties;
-  }
-  if (tid == 0) s_pick = -1;
-  __syncthreads();
-  unsigned long long mi = lane < kSampleWarps ? wmass[lane] : 0;
-  int ti = lane < kSampleWarps ? wties[lane] : 0;
-  const unsigned long long mv = mi;
-  const int tv = ti;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const unsigned long long a2 = __shfl_up_sync(FULL, mi, o);
-    const int b2 = __shfl_up_sync(FULL, ti, o);
-    if (lane >= o) {
-      mi += a2;
-      ti += b2;
-    }
-  }
-  const unsigned long long wm_before = __shfl_sync(FULL, mi - mv, warp);
-  const int wt_before = __shfl_sync(FULL, ti - tv, warp);
-  const unsigned long long wm_incl = __shfl_sync(FULL, mi, warp);
-  const int wt_incl = __shfl_sync(FULL, ti, warp);
-  const unsigned long long kept = kept_mass(__shfl_sync(FULL, mi, 31), __shfl_sync(FULL, ti, 31));
-  const unsigned long long target = (unsigned long long)((double)a.uniforms[blockIdx.x] * (double)kept);
-  const unsigned long long kb = kept_mass(wm_before, wt_before), ki = kept_mass(wm_incl, wt_incl);
-  if (ki > kb && kb <= target && target < ki) {
-    const int llo = min(whi, wlo + lane * sub), lhi = min(whi, llo + sub);
-    unsigned long long lm = 0;
-    int lt = 0;
-    for (int b0 = llo; b0 < lhi; b0 += kVec) {
-      uint32_t k[kVec];
-      const int n = min(fetch(b0, k), lhi - b0);
-#pragma unroll
-      for (int j = 0; j < kVec; ++j) {
-        unsigned long long p;
-        bool tie;
-        classify(k[j], p, tie);
-        if (j < n) {
-          lm += p;
-          lt += tie ? 1 : 0;
-        }
-      }
-    }
-    unsigned long long sm = lm;
-    int st = lt;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const unsigned long long a2 = __shfl_up_sync(FULL, sm, o);
-      const int b2 = __shfl_up_sync(FULL, st, o);
-      if (lane >= o) {
-        sm += a2;
-        st += b2;
-      }
-    }
-    const unsigned long long nb0 = wm_before + sm - lm;
-    const int tb = wt_before + st - lt;
-    const unsigned long long lkb = kept_mass(nb0, tb), lki = kept_mass(nb0 + lm, tb + lt);
-    if (lki > lkb && lkb <= target && target < lki) {
-      unsigned long long run = lkb;
-      int ties = tb, pick = -1, last = -1;
-      for (int b0 = llo; b0 < lhi && pick < 0; b0 += kVec) {
-        uint32_t k[kVec];
-        const int n = min(fetch(b0, k), lhi - b0);
-#pragma unroll
-        for (int j = 0; j < kVec; ++j) {
-          unsigned long long p;
-          bool tie;
-          classify(k[j], p, tie);
-          if (j >= n || pick >= 0) continue;
-          if (tie) {
-            if (ties < keep_ties) p = pc;
-            ++ties;
-          }
-          if (p > 0) {
-            last = b0 + j;
-            run += p;
-            if (target < run) pick = b0 + j;
-          }
-        }
-      }
-      s_pick = pick >= 0 ? pick : last;  // exactly one lane of the CTA gets here
-    }
-  }
-  __syncthreads();
-  if (tid == 0) a.out[blockIdx.x] = s_pick >= 0 ? s_pick : 0;
+    for (int j = 0; j < kVec; ++j)
+      if (((half_at(v, j) - rlo) & 0xffffu) <= rspan) msk |= 1u << j;
+    return msk;  // bits past the row are masked by the caller
+  };
+  const int token = s_hi >= s_lo ? find_rth<kVec>(V, s_r, load, match, s_cnt, &s_res) : -1;
+  if (tid == 0) a.out[blockIdx.x] = token >= 0 ? token : 0;
 }
 
 }  // namespace

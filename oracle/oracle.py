@@ -203,7 +203,8 @@ def sample_top_p(logits, temperature: float, top_p: float, uniforms):
     logits dtype, probabilities softmax(scaled) (here in float64), the sorted
     order descending with ties in index order (a stable sort), tokens kept
     while their running probability is <= top_p, the first always kept. The
-    draw inverts the CDF of the kept tokens in index order at u * kept mass.
+    draw inverts the CDF of the kept tokens in that sorted order at
+    u * kept mass, as a multinomial draw over the sorted probabilities does.
     Returns (tokens int64 [B], cut_margin [B], draw_margin [B]): the distance
     of the running probability from top_p at the cut and of the target from
     the nearest CDF step, so a test can skip rows that float rounding decides.
@@ -225,9 +226,7 @@ def sample_top_p(logits, temperature: float, top_p: float, uniforms):
         keep_sorted[0] = True
         if top_p < 1.0:
             cut_margin[b] = float(np.min(np.abs(run - top_p)))
-        keep = np.zeros(V, dtype=bool)
-        keep[order[keep_sorted]] = True
-        idx = np.nonzero(keep)[0]
+        idx = order[keep_sorted]
         cdf = np.cumsum(p[idx])
         target = u[b] * cdf[-1]
         j = int(np.searchsorted(cdf, target, side="right"))
