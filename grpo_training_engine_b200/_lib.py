@@ -15,7 +15,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libpkv.so"
 
-ABI_VERSION = 6  # PKV_ABI_VERSION in include/pkv.h
+ABI_VERSION = 7  # PKV_ABI_VERSION in include/pkv.h
 
 SAMPLE_FORCE_RADIX = 1  # PKV_SAMPLE_FORCE_RADIX
 
@@ -79,7 +79,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                   C.c_int64, C.c_float, _i32, _vp]),
     "pkv_silu_mul": (C.c_int, [_vp, _vp, _vp, _i32, _i32, C.c_int64, C.c_int64, _i32, _vp]),
     "pkv_rope_qk": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, C.c_int64, C.c_int64,
-                              C.c_int64, _i32, _vp]),
+                              C.c_int64, C.c_int64, C.c_int64, _i32, _vp]),
     "pkv_sample_top_p": (C.c_int, [_vp, _i32, _i32, _i32, C.c_int64, C.c_float, C.c_float, _vp, _vp, _i32, _vp]),
     "pkv_decode": (
         C.c_int,

@@ -125,7 +125,7 @@ __global__ void silu_mul_kernel(const T *gate, const T *up, T *out, int64_t n_ve
 // One CTA per row: threads over (head, d < D/2) pairs of the query and key heads.
 template <typename T>
 __global__ void rope_qk_kernel(const T *q, const T *k, const T *cosv, const T *sinv, T *qo, T *ko, int Hq,
-                               int Hkv, int D, int64_t qs, int64_t ks, int64_t cs) {
+                               int Hkv, int D, int64_t qs, int64_t ks, int64_t cs, int64_t qos, int64_t kos) {
   const int64_t b = blockIdx.x;
   const int half = D / 2;
   const int pairs = (Hq + Hkv) * half;
@@ -134,7 +134,8 @@ __global__ void rope_qk_kernel(const T *q, const T *k, const T *cosv, const T *s
     const bool isq = h < Hq;
     const int hh = isq ? h : h - Hq;
     const T *src = isq ? q + b * qs + (int64_t)hh * D : k + b * ks + (int64_t)hh * D;
-    T *dst = isq ? qo + (b * Hq + hh) * D : ko + (b * Hkv + hh) * D;
+    // one thread reads and writes both elements of its pair: out may alias in
+    T *dst = isq ? qo + b * qos + (int64_t)hh * D : ko + b * kos + (int64_t)hh * D;
     const float x1 = Cvt<T>::f(src[d]), x2 = Cvt<T>::f(src[d + half]);
     const float c1 = Cvt<T>::f(cosv[b * cs + d]), c2 = Cvt<T>::f(cosv[b * cs + d + half]);
     const float s1 = Cvt<T>::f(sinv[b * cs + d]), s2 = Cvt<T>::f(sinv[b * cs + d + half]);
@@ -240,7 +241,7 @@ extern "C" int pkv_silu_mul(const void *gate, const void *up, void *out, int32_t
 extern "C" int pkv_rope_qk(const void *q, const void *k, const void *cos_, const void *sin_, void *q_out,
                            void *k_out, int32_t rows, int32_t num_q_heads, int32_t num_kv_heads,
                            int32_t head_dim, int64_t q_stride, int64_t k_stride, int64_t cs_stride,
-                           int32_t dtype, void *stream) {
+                           int64_t q_out_stride, int64_t k_out_stride, int32_t dtype, void *stream) {
   if (rows < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || head_dim % 2 != 0) {
     set_error_detail("pkv_rope_qk: invalid sizes");
     return PKV_ERR_INVALID_ARG;
@@ -263,18 +264,19 @@ extern "C" int pkv_rope_qk(const void *q, const void *k, const void *cos_, const
       rope_qk_kernel<__nv_bfloat16><<<rows, threads, 0, st>>>(
           (const __nv_bfloat16 *)q, (const __nv_bfloat16 *)k, (const __nv_bfloat16 *)cos_,
           (const __nv_bfloat16 *)sin_, (__nv_bfloat16 *)q_out, (__nv_bfloat16 *)k_out, num_q_heads,
-          num_kv_heads, head_dim, q_stride, k_stride, cs_stride);
+          num_kv_heads, head_dim, q_stride, k_stride, cs_stride, q_out_stride, k_out_stride);
       break;
     case PKV_DTYPE_F16:
       rope_qk_kernel<__half><<<rows, threads, 0, st>>>(
           (const __half *)q, (const __half *)k, (const __half *)cos_, (const __half *)sin_, (__half *)q_out,
-          (__half *)k_out, num_q_heads, num_kv_heads, head_dim, q_stride, k_stride, cs_stride);
+          (__half *)k_out, num_q_heads, num_kv_heads, head_dim, q_stride, k_stride, cs_stride, q_out_stride,
+          k_out_stride);
       break;
     default:
       rope_qk_kernel<float><<<rows, threads, 0, st>>>((const float *)q, (const float *)k, (const float *)cos_,
                                                       (const float *)sin_, (float *)q_out, (float *)k_out,
                                                       num_q_heads, num_kv_heads, head_dim, q_stride,
-                                                      k_stride, cs_stride);
+                                                      k_stride, cs_stride, q_out_stride, k_out_stride);
       break;
   }
   return check_launch("pkv_rope_qk");

@@ -475,12 +475,15 @@ def rope_qk(
     num_q_heads: int,
     num_kv_heads: int,
     head_dim: int,
+    k_out: Optional[torch.Tensor] = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """RoPE of one new query / key row per sequence, one launch.
 
     q [rows, Hq * D], k [rows, Hkv * D] (the projections' outputs), cos / sin
-    [rows, D]; returns contiguous q [rows, Hq, D] and k [rows, Hkv, D] equal to
-    HF's apply_rotary_pos_emb of the same rows (C ABI pkv_rope_qk).
+    [rows, D]; returns q [rows, Hq, D] (contiguous) and k [rows, Hkv, D] equal to
+    HF's apply_rotary_pos_emb of the same rows (C ABI pkv_rope_qk). With k_out
+    ([rows, Hkv * D], contiguous rows; k itself rotates k in place) the keys are
+    written there and the returned k is its [rows, Hkv, D] view.
     """
     rows = q.shape[0]
     if (q.shape != (rows, num_q_heads * head_dim) or k.shape != (rows, num_kv_heads * head_dim)
@@ -492,13 +495,21 @@ def rope_qk(
         raise ValueError("q, k, cos and sin must share one dtype.")
     dev = _require_cuda(q, k, cos, sin)
     qo = torch.empty(rows, num_q_heads, head_dim, dtype=q.dtype, device=dev)
-    ko = torch.empty(rows, num_kv_heads, head_dim, dtype=k.dtype, device=dev)
+    if k_out is None:
+        ko = torch.empty(rows, num_kv_heads, head_dim, dtype=k.dtype, device=dev)
+        k_rows = num_kv_heads * head_dim
+    else:
+        if k_out.shape != k.shape or k_out.dtype != k.dtype or k_out.stride(1) != 1:
+            raise ValueError("k_out must match k: [rows, heads * head_dim] with contiguous rows.")
+        _require_cuda(k_out)
+        ko, k_rows = k_out.view(rows, num_kv_heads, head_dim), k_out.stride(0)
     with torch.cuda.device(dev):
         _lib.check(
             "pkv_rope_qk",
             _lib.load().pkv_rope_qk(q.data_ptr(), k.data_ptr(), cos.data_ptr(), sin.data_ptr(), qo.data_ptr(),
                                     ko.data_ptr(), rows, num_q_heads, num_kv_heads, head_dim, q.stride(0),
-                                    k.stride(0), cos.stride(0), _dtype_code(q, "q"), _stream(dev)),
+                                    k.stride(0), cos.stride(0), num_q_heads * head_dim, k_rows,
+                                    _dtype_code(q, "q"), _stream(dev)),
         )
     return qo, ko
 

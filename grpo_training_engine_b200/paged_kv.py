@@ -387,11 +387,43 @@ def paged_kv_decode_model(
                    and all(hasattr(layer.mlp, n) for n in ("gate_proj", "up_proj", "down_proj"))
                    and layer.mlp.gate_proj.out_features % 8 == 0 for layer in layers)
 
-    def _mlp(layer, h):
+    # Projections that read the same input run as one GEMM on stacked weights:
+    # q / k / v (with their biases) and the MLP's gate / up. The stacks are
+    # copied from the modules' current weights for this call (the trainer
+    # updates them between rollouts); modules that are not plain nn.Linear
+    # (e.g. LoRA-wrapped) are called as they are.
+    def _stack(mods):
+        if not all(type(m) is torch.nn.Linear for m in mods):
+            return None
+        w = torch.cat([m.weight.detach() for m in mods], 0)
+        if all(m.bias is None for m in mods):
+            return w, None
+        return w, torch.cat([m.bias.detach() if m.bias is not None else
+                             torch.zeros(m.out_features, dtype=w.dtype, device=w.device) for m in mods])
+
+    qkv_stack = [_stack((layer.self_attn.q_proj, layer.self_attn.k_proj, layer.self_attn.v_proj))
+                 if fused_glue else None for layer in layers]
+    gate_up_stack = [_stack((layer.mlp.gate_proj, layer.mlp.up_proj)) if fused_glue and silu_mlp else None
+                     for layer in layers]
+    q_cols, kv_cols = num_heads * head_dim, num_kv_heads * head_dim
+
+    def _qkv(layer_idx, attn, h):
+        st = qkv_stack[layer_idx]
+        if st is None:
+            return attn.q_proj(h), attn.k_proj(h), attn.v_proj(h)
+        qkv = torch.nn.functional.linear(h, st[0], st[1])
+        return qkv[:, :q_cols], qkv[:, q_cols:q_cols + kv_cols], qkv[:, q_cols + kv_cols:]
+
+    def _mlp(layer_idx, layer, h):
         mlp = layer.mlp
-        if silu_mlp:
+        if not silu_mlp:
+            return mlp(h)
+        st = gate_up_stack[layer_idx]
+        if st is None:
             return mlp.down_proj(ops.silu_mul(mlp.gate_proj(h), mlp.up_proj(h)))
-        return mlp(h)
+        inter = mlp.gate_proj.out_features
+        gu = torch.nn.functional.linear(h, st[0], st[1])
+        return mlp.down_proj(ops.silu_mul(gu[:, :inter], gu[:, inter:]))
 
     def _forward_modules() -> tuple[torch.Tensor, torch.Tensor]:
         hidden = cast(torch.Tensor, embeddings(tokens_buf))
@@ -438,8 +470,11 @@ def paged_kv_decode_model(
                                        residual=None if pending is None else hidden)
             if total is not None:
                 hidden = total
-            q1, k1 = ops.rope_qk(attn.q_proj(h), attn.k_proj(h), cos, sin, num_heads, num_kv_heads, head_dim)
-            v1 = attn.v_proj(h).view(batch_size, num_kv_heads, head_dim)
+            q_lin, k_lin, v_lin = _qkv(layer_idx, attn, h)
+            # stacked: the keys rotate in place, so k and v are views of one buffer with equal strides
+            q1, k1 = ops.rope_qk(q_lin, k_lin, cos, sin, num_heads, num_kv_heads, head_dim,
+                                 k_out=k_lin if qkv_stack[layer_idx] is not None else None)
+            v1 = v_lin.view(batch_size, num_kv_heads, head_dim)
             k_cache, v_cache = pool.layer(layer_idx)
             # append at context_lens and attend over new_context_lens: one fused call
             attn_out = ops.paged_attention_decode(q1, k_cache, v_cache, block_tables, new_context_lens,
@@ -447,7 +482,7 @@ def paged_kv_decode_model(
             o = attn.o_proj(attn_out.to(hidden.dtype).reshape(batch_size, num_heads * head_dim))
             ln = layer.post_attention_layernorm
             h2, hidden = ops.add_rmsnorm(o, ln.weight, ln.variance_epsilon, residual=hidden)
-            pending = _mlp(layer, h2)
+            pending = _mlp(layer_idx, layer, h2)
         h, _ = ops.add_rmsnorm(pending, norm.weight, norm.variance_epsilon, residual=hidden)
         return lm_head(h), new_context_lens
 

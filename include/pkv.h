@@ -37,8 +37,8 @@
 extern "C" {
 #endif
 
-#define PKV_ABI_VERSION 6  /* 2: pkv_append_decode_run, 3: pkv_sample_top_p, 4: rmsnorm, rope, 5: silu_mul,
-                              6: pkv_sample_top_p flags */
+#define PKV_ABI_VERSION 7  /* 2: pkv_append_decode_run, 3: pkv_sample_top_p, 4: rmsnorm, rope, 5: silu_mul,
+                              6: pkv_sample_top_p flags, 7: pkv_rope_qk output strides */
 
 /* Element types. The reference stores the cache in bfloat16
  * (paged_kv.py:409-410, 629-633); float32 is accepted because the reference
@@ -251,9 +251,10 @@ int pkv_sample_top_p(const void *logits, int32_t dtype, int32_t batch, int32_t v
  *
  * pkv_rope_qk: RoPE of one new query row [num_q_heads * head_dim] and key row
  * [num_kv_heads * head_dim] per sequence with cos/sin [rows, head_dim] (row
- * stride cs_stride), written as contiguous q_out [rows, Hq, D] and
- * k_out [rows, Hkv, D] (the layout pkv_append_decode_run reads), with the
- * element-wise rounding of HF's apply_rotary_pos_emb.
+ * stride cs_stride), written as q_out [rows, Hq, D] and k_out [rows, Hkv, D]
+ * (row strides q_out_stride / k_out_stride, heads contiguous: the layout
+ * pkv_append_decode_run reads), with the element-wise rounding of HF's
+ * apply_rotary_pos_emb. k_out may be k itself (rotation in place).
  */
 int pkv_add_rmsnorm(const void *x, const void *residual, const void *weight, void *sum_out, void *out,
                     int32_t rows, int32_t hidden, int64_t x_stride, int64_t residual_stride,
@@ -267,7 +268,7 @@ int pkv_silu_mul(const void *gate, const void *up, void *out, int32_t rows, int3
 int pkv_rope_qk(const void *q, const void *k, const void *cos_, const void *sin_, void *q_out,
                 void *k_out, int32_t rows, int32_t num_q_heads, int32_t num_kv_heads,
                 int32_t head_dim, int64_t q_stride, int64_t k_stride, int64_t cs_stride,
-                int32_t dtype, void *stream);
+                int64_t q_out_stride, int64_t k_out_stride, int32_t dtype, void *stream);
 
 int pkv_decode(const void *q, const void *k_cache, const void *v_cache,
                const int32_t *block_tables, const int32_t *context_lens,

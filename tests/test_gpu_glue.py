@@ -56,6 +56,13 @@ def test_rope_qk_matches_apply_rotary_pos_emb(hq, hkv, d):
     qo, ko = ops.rope_qk(q, k, cos.reshape(b, d), sin.reshape(b, d), hq, hkv, d)
     assert torch.equal(qo, q_ref[:, :, 0, :])
     assert torch.equal(ko, k_ref[:, :, 0, :])
+    # q / k / v as column slices of one stacked projection, keys rotated in place
+    qkv = torch.cat([q, k, k.flip(0)], dim=1)
+    qs, ks = qkv[:, :hq * d], qkv[:, hq * d:(hq + hkv) * d]
+    qo2, ko2 = ops.rope_qk(qs, ks, cos.reshape(b, d), sin.reshape(b, d), hq, hkv, d, k_out=ks)
+    assert torch.equal(qo2, qo) and torch.equal(ko2, ko)
+    assert ko2.data_ptr() == ks.data_ptr() and ko2.stride() == (qkv.stride(0), d, 1)
+    assert torch.equal(qkv[:, :hq * d], q) and torch.equal(qkv[:, (hq + hkv) * d:], k.flip(0))
 
 
 def test_silu_mul_matches_qwen2_mlp_gate():
