@@ -708,9 +708,7 @@ decode_tc_kernel(DecodeArgs a) {
     int4 d2 = w2 < total ? r1 : none;
     load_next(w1, d1);
 
-    int32_t kcount[NW];
-#pragma unroll
-    for (int i = 0; i < NW; ++i) kcount[i] = 0;
+    int32_t kcount = 0;  // lane cw < NW: elements published to consumer warp cw
     bool ok = true;
     int32_t nunit = 0;  // units issued by this CTA (query slot = nunit % QS)
     while (w1 < total && ok) {
@@ -763,7 +761,47 @@ decode_tc_kernel(DecodeArgs a) {
                                             (int64_t)app_row * a.c2) * 2 + 16 * cc) = nkv;
         }
       }
-      // (2) prefetch: the next unit's block-table entries and query rows, the
+      // (2) publish the unit's pages to the consumer warps (page p -> warp p % NW),
+      //     lane cw filling warp cw's ring; each consumer loads its pages itself
+      //     with cp.async
+      if (lane < NW && ok) {
+        const int32_t rounds = npages > 0 ? (npages + NW - 1) / NW : 1;
+        for (int32_t j = 0; j < rounds; ++j) {
+          const int32_t pi = j * NW + lane;
+          const bool has = pi < npages;
+          const bool last = (j == rounds - 1);
+          if (!has && !last) continue;
+          const int32_t k = kcount++;
+          const int slot = lane * MD + (k % MD);
+          const int32_t use = k / MD;
+          if (use > 0 && !mbar_wait_backoff(&empty[slot], (use - 1) & 1)) {
+            flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
+            ok = false;
+            break;
+          }
+          const int32_t page = has ? btbuf[pi] : -1;
+          SlotMeta md;
+          md.kind = page >= 0 ? kElemPage : kElemEmpty;
+          md.valid = has ? min(kBoxRows, u.ctx - (u.p_begin + pi) * kBoxRows) : 0;
+          md.last = last ? 1 : 0;
+          md.work = w1;
+          md.qslot = qs;
+          md.b = u.b;
+          md.s = u.s;
+          md.nsplit = u.nsplit;
+          md.kvh = u.kvh;
+          md.hg = u.hg;
+          md.gcount = u.gcount;
+          md.qh0 = u.qh0;
+          md.page = page;
+          md.newrow = (pi == app_pi) ? app_row : -1;
+          md.split_row = split_row;
+          md.pad = 0;
+          meta[slot] = md;
+          mbar_arrive(&full[slot]);
+        }
+      }
+      // (3) prefetch: the next unit's block-table entries and query rows, the
       //     descriptor of the one after
       load_next(w2, d2);
       int32_t w3;
@@ -775,49 +813,7 @@ decode_tc_kernel(DecodeArgs a) {
       // the claim for round r + 3 is consumed at the next iteration
       if (lane == 0 && round + 3 >= R && w3 < total) fetched = atomicAdd(&a.sched[0], 1);
       const int4 d3 = w3 < total ? a.items[w3 / a.upi] : none;
-      // (3) publish the unit's pages to the consumer warps (page p -> warp p % NW);
-      //     each consumer loads its pages itself with cp.async
-      if (lane == 0 && ok) {
-        const int32_t rounds = npages > 0 ? (npages + NW - 1) / NW : 1;
-        for (int32_t j = 0; j < rounds && ok; ++j) {
-#pragma unroll
-          for (int cw = 0; cw < NW; ++cw) {
-            const int32_t pi = j * NW + cw;
-            const bool has = pi < npages;
-            const bool last = (j == rounds - 1);
-            if (!has && !last) continue;
-            const int32_t k = kcount[cw]++;
-            const int slot = cw * MD + (k % MD);
-            const int32_t use = k / MD;
-            if (use > 0 && !mbar_wait_backoff(&empty[slot], (use - 1) & 1)) {
-              flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
-              ok = false;
-              break;
-            }
-            const int32_t page = has ? btbuf[pi] : -1;
-            SlotMeta md;
-            md.kind = page >= 0 ? kElemPage : kElemEmpty;
-            md.valid = has ? min(kBoxRows, u.ctx - (u.p_begin + pi) * kBoxRows) : 0;
-            md.last = last ? 1 : 0;
-            md.work = w1;
-            md.qslot = qs;
-            md.b = u.b;
-            md.s = u.s;
-            md.nsplit = u.nsplit;
-            md.kvh = u.kvh;
-            md.hg = u.hg;
-            md.gcount = u.gcount;
-            md.qh0 = u.qh0;
-            md.page = page;
-            md.newrow = (pi == app_pi) ? app_row : -1;
-            md.split_row = split_row;
-            md.pad = 0;
-            meta[slot] = md;
-            mbar_arrive(&full[slot]);
-          }
-        }
-      }
-      ok = __shfl_sync(FULL, ok ? 1 : 0, 0) != 0;
+      ok = __all_sync(FULL, ok);
       __syncwarp();  // btbuf / qbuf are rewritten for the next unit
       ++nunit;
       ++round;
@@ -836,16 +832,13 @@ decode_tc_kernel(DecodeArgs a) {
         atomicExch(&a.sched[1], 0);
       }
     }
-    if (lane == 0 && ok) {
-#pragma unroll
-      for (int cw = 0; cw < NW; ++cw) {
-        const int32_t k = kcount[cw]++;
-        const int slot = cw * MD + (k % MD);
-        const int32_t use = k / MD;
-        if (use > 0 && !mbar_wait_backoff(&empty[slot], (use - 1) & 1)) {
-          flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
-          break;
-        }
+    if (lane < NW && ok) {  // a stop element to each consumer warp
+      const int32_t k = kcount++;
+      const int slot = lane * MD + (k % MD);
+      const int32_t use = k / MD;
+      if (use > 0 && !mbar_wait_backoff(&empty[slot], (use - 1) & 1)) {
+        flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
+      } else {
         SlotMeta md{};
         md.kind = kElemStop;
         md.last = 1;
