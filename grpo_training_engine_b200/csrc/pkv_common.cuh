@@ -111,14 +111,33 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that gives up after about ns nanoseconds (the suspend-time hint)
+// instead of the hardware-defined interval
+__device__ __forceinline__ bool mbar_try_wait_ns(uint64_t *bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait on an mbarrier phase. Each try_wait suspends the thread for a
 // hardware-defined interval, so kMaxTries bounds the wait to well under a
 // minute. Returns false if the phase never completed.
 constexpr uint32_t kMaxWaitTries = 1u << 22;
 
+// Bounded wait for a thread on the critical path (a consumer waiting for its
+// next element or for the group): polls every ~100 ns, so it resumes soon
+// after the phase completes; 2^24 polls bound the wait to a few seconds.
+constexpr uint32_t kPollNs = 100;
+constexpr uint32_t kMaxPolls = 1u << 24;
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kMaxWaitTries; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+  for (uint32_t i = 0; i < kMaxPolls; ++i) {
+    if (mbar_try_wait_ns(bar, parity, kPollNs)) return true;
   }
   return false;
 }

@@ -108,7 +108,8 @@ struct DecodeArgs {
   int32_t B, Hq, Hkv, G, GR, HG, D, bs, num_blocks, max_blocks, P, upi, part_o, part_floats;
   int32_t q_dtype, kv_dtype;
   int32_t q_vec;    // q rows are 16-byte aligned and contiguous in head_dim
-  int32_t out_vec;  // out rows are 16-byte aligned and contiguous in head_dim
+  int32_t out_vec;  // out rows are aligned for 4-element stores and contiguous in head_dim
+  int32_t out16;    // out element type: 0 fp32, 1 bf16, 2 fp16 (rounded to nearest)
   int64_t q0, q1, q2;
   int64_t c0, c1, c2, c3;
   int64_t bt0, bt1;
@@ -132,6 +133,32 @@ struct DecodeArgs {
 struct Unit {
   int32_t b, s, kvh, hg, nsplit, ctx, p_begin, p_end, gcount, qh0;
 };
+
+// One output element, in the output's type.
+__device__ __forceinline__ void store_out(const DecodeArgs &a, int64_t idx, float v) {
+  if (a.out16 == 1)
+    reinterpret_cast<__nv_bfloat16 *>(a.out)[idx] = __float2bfloat16_rn(v);
+  else if (a.out16 == 2)
+    reinterpret_cast<__half *>(a.out)[idx] = __float2half_rn(v);
+  else
+    a.out[idx] = v;
+}
+
+// Four consecutive output elements starting at element idx (a multiple of 4
+// on a row of 4-element-aligned stores).
+__device__ __forceinline__ void store_out4(const DecodeArgs &a, int64_t idx, float4 r) {
+  if (a.out16 == 1) {
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(r.x, r.y), hi = __floats2bfloat162_rn(r.z, r.w);
+    *reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(a.out) + idx) =
+        make_uint2(*reinterpret_cast<const uint32_t *>(&lo), *reinterpret_cast<const uint32_t *>(&hi));
+  } else if (a.out16 == 2) {
+    const __half2 lo = __floats2half2_rn(r.x, r.y), hi = __floats2half2_rn(r.z, r.w);
+    *reinterpret_cast<uint2 *>(reinterpret_cast<__half *>(a.out) + idx) =
+        make_uint2(*reinterpret_cast<const uint32_t *>(&lo), *reinterpret_cast<const uint32_t *>(&hi));
+  } else {
+    *reinterpret_cast<float4 *>(a.out + idx) = r;
+  }
+}
 
 // Work unit w = (item, kv head, head group); the item descriptor comes from the plan.
 __device__ __forceinline__ Unit unit_from(const DecodeArgs &a, int32_t w, int4 it) {
@@ -318,7 +345,7 @@ __device__ bool unit_epilogue(const DecodeArgs &a, const Unit &u, int32_t split_
       }
     }
     if (u.nsplit == 1) {
-      a.out[u.b * a.o0 + (int64_t)(u.qh0 + g) * a.o1 + d * a.o2] = O / fmaxf(L, 1e-6f);
+      store_out(a, u.b * a.o0 + (int64_t)(u.qh0 + g) * a.o1 + d * a.o2, O / fmaxf(L, 1e-6f));
     } else {  // merged by merge_kernel after the launch
       part[a.part_o + g * D + d] = O;
       if (d == 0) {
@@ -361,7 +388,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(DecodeArgs a) {
         O += f * p[a.part_o + g * D + d];
       }
     }
-    a.out[b * a.o0 + (int64_t)(qh0 + g) * a.o1 + d * a.o2] = O / fmaxf(L, 1e-6f);
+    store_out(a, b * a.o0 + (int64_t)(qh0 + g) * a.o1 + d * a.o2, O / fmaxf(L, 1e-6f));
   }
 }
 
@@ -1170,14 +1197,14 @@ decode_tc_kernel(DecodeArgs a) {
           if (u.nsplit == 1) {
             const float inv = 1.f / fmaxf(Ls, 1e-6f);
             const float4 r = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
-            float *op = a.out + u.b * a.o0 + (int64_t)(u.qh0 + g) * a.o1;
+            const int64_t op = u.b * a.o0 + (int64_t)(u.qh0 + g) * a.o1;
             if (a.out_vec) {
-              *reinterpret_cast<float4 *>(op + 4 * c4) = r;
+              store_out4(a, op + 4 * c4, r);
             } else {
-              op[(4 * c4 + 0) * a.o2] = r.x;
-              op[(4 * c4 + 1) * a.o2] = r.y;
-              op[(4 * c4 + 2) * a.o2] = r.z;
-              op[(4 * c4 + 3) * a.o2] = r.w;
+              store_out(a, op + (4 * c4 + 0) * a.o2, r.x);
+              store_out(a, op + (4 * c4 + 1) * a.o2, r.y);
+              store_out(a, op + (4 * c4 + 2) * a.o2, r.z);
+              store_out(a, op + (4 * c4 + 3) * a.o2, r.w);
             }
           } else {  // merged by merge_kernel after the launch
             float *part = a.partials +
@@ -1525,7 +1552,8 @@ int decode_run_impl(const void *q, const void *kn, const void *vn, const void *k
   a.c0 = cache_strides[0]; a.c1 = cache_strides[1]; a.c2 = cache_strides[2]; a.c3 = cache_strides[3];
   a.bt0 = bt_strides[0]; a.bt1 = bt_strides[1];
   a.o0 = out_strides[0]; a.o1 = out_strides[1]; a.o2 = out_strides[2];
-  a.out_vec = (a.o2 == 1 && a.o0 % 4 == 0 && a.o1 % 4 == 0 && aligned_to(out, 16)) ? 1 : 0;
+  a.out16 = (flags & PKV_DECODE_OUT_Q_DTYPE) ? (q_dtype == PKV_DTYPE_BF16 ? 1 : q_dtype == PKV_DTYPE_F16 ? 2 : 0) : 0;
+  a.out_vec = (a.o2 == 1 && a.o0 % 4 == 0 && a.o1 % 4 == 0 && aligned_to(out, a.out16 ? 8 : 16)) ? 1 : 0;
   a.scale = scale;
   a.scale_log2 = scale * kLog2e;
   a.hdr = reinterpret_cast<const int32_t *>(ws + w.hdr);

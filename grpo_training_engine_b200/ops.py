@@ -327,6 +327,7 @@ def paged_attention_decode(
     status: Optional[torch.Tensor] = None,
     k_new: Optional[torch.Tensor] = None,
     v_new: Optional[torch.Tensor] = None,
+    out_dtype: Optional[torch.dtype] = None,
 ) -> torch.Tensor:
     """Single-query attention over the paged cache; returns fp32 [B, Hq, D].
 
@@ -347,6 +348,10 @@ def paged_attention_decode(
     context_lens[b] - 1 (context_lens stay POST-append) and attended to, in
     a single launch on the tensor-core kernel (C ABI pkv_append_decode_run).
     It writes the cache bytes paged_kv_append(..., context_lens - 1) writes.
+
+    out_dtype=q.dtype (bf16 / fp16 q) returns the output in q's dtype, each
+    fp32 result rounded to nearest: the values of ``.to(q.dtype)`` of the fp32
+    output, without a separate conversion launch.
     """
     _check_cache_pair(k_cache, v_cache)
     if q.ndim != 3:
@@ -359,10 +364,14 @@ def paged_attention_decode(
         raise ValueError(f"num_heads ({hq}) must be divisible by num_kv_heads ({hkv}).")
     _check_tables(block_tables, context_lens, batch)
     dev = _require_cuda(q, k_cache, v_cache, block_tables, context_lens, out, status)
+    if out_dtype is None:
+        out_dtype = out.dtype if out is not None else torch.float32
+    if out_dtype not in (torch.float32, q.dtype):
+        raise ValueError(f"out_dtype must be float32 or q's dtype ({q.dtype}), got {out_dtype}.")
     if out is None:
-        out = torch.empty((batch, hq, head_dim), dtype=torch.float32, device=dev)
-    elif out.dtype != torch.float32 or tuple(out.shape) != (batch, hq, head_dim):
-        raise ValueError("out must be a float32 [batch, heads, head_dim] tensor.")
+        out = torch.empty((batch, hq, head_dim), dtype=out_dtype, device=dev)
+    elif out.dtype != out_dtype or tuple(out.shape) != (batch, hq, head_dim):
+        raise ValueError(f"out must be a {out_dtype} [batch, heads, head_dim] tensor.")
     if scale is None:
         scale = 1.0 / math.sqrt(head_dim)
     bt = _as_i32(block_tables)
@@ -375,6 +384,8 @@ def paged_attention_decode(
     lib = _lib.load()
     ws = plan.workspace
     flags = (_lib.DECODE_FORCE_GENERIC if force_generic else 0) | (_lib.DECODE_EXACT_P if exact else 0)
+    if out.dtype != torch.float32:
+        flags |= _lib.DECODE_OUT_Q_DTYPE
     if k_new is not None or v_new is not None:
         if k_new is None or v_new is None:
             raise ValueError("k_new and v_new must be given together.")

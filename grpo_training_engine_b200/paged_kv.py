@@ -478,8 +478,9 @@ def paged_kv_decode_model(
             k_cache, v_cache = pool.layer(layer_idx)
             # append at context_lens and attend over new_context_lens: one fused call
             attn_out = ops.paged_attention_decode(q1, k_cache, v_cache, block_tables, new_context_lens,
-                                                  scale=scale, plan=plan, k_new=k1, v_new=v1)
-            o = attn.o_proj(attn_out.to(hidden.dtype).reshape(batch_size, num_heads * head_dim))
+                                                  scale=scale, plan=plan, k_new=k1, v_new=v1,
+                                                  out_dtype=hidden.dtype)
+            o = attn.o_proj(attn_out.reshape(batch_size, num_heads * head_dim))
             ln = layer.post_attention_layernorm
             h2, hidden = ops.add_rmsnorm(o, ln.weight, ln.variance_epsilon, residual=hidden)
             pending = _mlp(layer_idx, layer, h2)

@@ -71,10 +71,13 @@ enum {
 enum {
     PKV_DECODE_FORCE_GENERIC = 1, /* use the CUDA-core kernel even when the
                                      tensor-core kernel could run            */
-    PKV_DECODE_EXACT_P = 2        /* tensor-core kernel: multiply the softmax
+    PKV_DECODE_EXACT_P = 2,       /* tensor-core kernel: multiply the softmax
                                      weights as a 16-bit head plus 16-bit
                                      remainder (~17 significant bits instead
                                      of 8); slower, closer to fp32           */
+    PKV_DECODE_OUT_Q_DTYPE = 4    /* out holds q's dtype (bf16 or fp16; fp32 q:
+                                     no change): each fp32 result rounded to
+                                     nearest, as a cast of the fp32 output   */
 };
 
 /* Sampling flags. */

@@ -393,3 +393,29 @@ def test_config2_append_gather_round_trip():
     full_v = torch.cat([prompt_v[layer], new_v[:, layer].permute(1, 2, 0, 3)], dim=2).cpu()
     oracle.append_prompt(full_k, full_v, kc, vc, perm.cpu())
     assert _sha(k_pool[layer], v_pool[layer]) == _sha(kc, vc)
+
+
+@pytest.mark.parametrize("shape", [s for s in DECODE_SHAPES if s[5] != torch.float32],
+                         ids=lambda s: f"b{s[0]}q{s[1]}kv{s[2]}d{s[3]}bs{s[4]}")
+@pytest.mark.parametrize("splits", [0, 3])
+def test_out_in_q_dtype_equals_cast_of_fp32_out(shape, splits):
+    """out_dtype=q.dtype writes what .to(q.dtype) of the fp32 output holds, on every
+    kernel (tensor-core, CUDA-core, split-K merge) and with the fused append."""
+    batch, hq, hkv, d, bs, dtype, ctxs = shape
+    q, kc, vc, bt, ctx = (t.to(DEV) for t in _random_case(31, batch, hq, hkv, d, bs, ctxs, dtype))
+    for force_generic in (False, True):
+        ref = paged_attention_decode(q, kc, vc, bt, ctx, num_splits=splits, force_generic=force_generic)
+        got = paged_attention_decode(q, kc, vc, bt, ctx, num_splits=splits, force_generic=force_generic,
+                                     out_dtype=dtype)
+        assert got.dtype == dtype and torch.equal(got, ref.to(dtype)), force_generic
+    # strided 16-bit out (no vector stores) and the fused append
+    g = torch.Generator().manual_seed(6)
+    kn, vn = (torch.randn(batch, hkv, d, generator=g).to(dtype).to(DEV) for _ in range(2))
+    kc2, vc2 = kc.clone(), vc.clone()
+    ref = paged_attention_decode(q, kc, vc, bt, ctx, num_splits=splits, k_new=kn, v_new=vn)
+    wide = torch.zeros(batch, hq, d + 4, dtype=dtype, device=DEV)  # rows 4-byte but not 8-byte aligned
+    got = paged_attention_decode(q, kc2, vc2, bt, ctx, num_splits=splits, k_new=kn, v_new=vn,
+                                 out=wide[:, :, 2:d + 2], out_dtype=dtype)
+    assert torch.equal(got, ref.to(dtype)) and not wide[:, :, :2].any() and not wide[:, :, d + 2:].any()
+    with pytest.raises(ValueError, match="out_dtype"):
+        paged_attention_decode(q, kc, vc, bt, ctx, out_dtype=torch.float64)
