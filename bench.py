@@ -643,6 +643,39 @@ def _cpu_name() -> str:
 
 
 # ----------------------------------------------------------------------------- model-level rollout
+def _profile_rollout_kernels(pkv, model, ids, kw, short=4, long_=24):
+    """Kernel time per rollout step by kernel name: CUDA activity of rollouts of
+    `short` and `long_` tokens under the torch profiler, difference / (long_ - short)."""
+    import collections
+
+    from torch.profiler import ProfilerActivity, profile
+
+    mask = torch.ones_like(ids)
+    pkv.paged_kv_decode(model, ids, mask, max_new_tokens=short, **kw)
+    torch.cuda.synchronize()
+
+    def kernel_times(n):
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            pkv.paged_kv_decode(model, ids, mask, max_new_tokens=n, **kw)
+            torch.cuda.synchronize()
+        tot, cnt = collections.Counter(), collections.Counter()
+        for e in prof.events():
+            if e.device_type == torch.autograd.DeviceType.CUDA:
+                tot[e.name[:90]] += e.device_time_total
+                cnt[e.name[:90]] += 1
+        return tot, cnt
+
+    t_s, c_s = kernel_times(short)
+    t_l, c_l = kernel_times(long_)
+    steps = long_ - short
+    per = {k: (t_l[k] - t_s.get(k, 0)) / steps for k in t_l}
+    total = sum(v for v in per.values() if v > 0)
+    top = sorted(per.items(), key=lambda kv: -kv[1])[:16]
+    return {"per_step_us": round(total, 1),
+            "top": [{"kernel": k, "calls_per_step": (c_l[k] - c_s.get(k, 0)) / steps, "us_per_step": round(v, 1),
+                     "share": round(v / total, 4)} for k, v in top]}
+
+
 def run_rollout(args):
     """Model-level decode steps of paged_kv_decode (the trainer's rollout call) on the
     DeepSeek-R1-Distill-Qwen-1.5B geometry with random bf16 weights: eager steps vs
@@ -686,6 +719,9 @@ def run_rollout(args):
         return {"ms_per_step": round(ms, 3), "seq_steps_per_s": round(batch / ms * 1e3, 1),
                 "setup_prefill_ms": round(setup, 2)}
 
+    if args.profile_kernels:
+        print(json.dumps(_profile_rollout_kernels(pkv, model, ids, kw)), flush=True)
+        return
     res = {"graph" if graph else "eager": per_step(graph) for graph in (False, True)}
     # GRPO groups: 16 prompts x 8 responses (the trainer's expanded prompt per group):
     # one prefill per prompt and shared prompt pages, against every row prefilled
@@ -818,6 +854,8 @@ def main():
                     help="launch every kernel from Python instead of replaying a CUDA graph of the timed steps")
     ap.add_argument("--separate-append", action="store_true",
                     help="append with its own launch (pkv_append) instead of inside the decode launch")
+    ap.add_argument("--profile-kernels", action="store_true",
+                    help="with --rollout: per-kernel time of one graph-replayed step (torch profiler)")
     ap.add_argument("--rollout", action="store_true",
                     help="time the model-level rollout step (eager vs CUDA graph) instead of the decode path")
     ap.add_argument("--no-e2e", action="store_true")
