@@ -253,6 +253,9 @@ plan_kernel(const int32_t *__restrict__ ctx, int32_t B, int32_t bs, int32_t max_
   __shared__ int32_t warp_tot[kPlanThreads / 32];
   __shared__ int32_t bucket[kMaxPagesPerSplit + 1];  // partial splits per length, then cursors
   __shared__ int32_t carry_all, carry_full;
+  // the decode launch that follows may start its CTAs' setup now (it waits
+  // for this grid before reading the plan)
+  asm volatile("griddepcontrol.launch_dependents;");
   const int tid = threadIdx.x;
   for (int i = tid; i <= P; i += kPlanThreads) bucket[i] = 0;
   if (tid == 0) carry_all = carry_full = 0;
@@ -633,6 +636,10 @@ decode_tc_kernel(DecodeArgs a) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int MD = L::MD, QS = L::QS;
   static_assert(NW * MD <= (NW + 1) * 32 && QS <= (NW + 1) * 32, "one thread per mbarrier");
+  // Programmatic dependent launch: the next launch in the stream may place its
+  // CTAs on SMs this grid frees; each of its threads waits (griddepcontrol.wait
+  // below) for this grid to complete before it reads global memory.
+  asm volatile("griddepcontrol.launch_dependents;");
   if (tid < NW * MD) {
     mbar_init(&full[tid], 1);
     mbar_init(&empty[tid], 1);
@@ -641,6 +648,10 @@ decode_tc_kernel(DecodeArgs a) {
   if (tid == 0) mbar_init(group, NW);
   fence_mbar_init();
   __syncthreads();
+  // Only shared memory was touched so far. From here on the previous kernel in
+  // the stream (which may have written q, the new rows, the caches or the
+  // plan) is complete and its writes are visible.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   const int32_t total = a.hdr[0];
 
@@ -1402,7 +1413,19 @@ int launch_tc_x(const DecodeArgs &a, cudaStream_t st, int64_t max_units) {
   int64_t grid = (int64_t)device_sms() * per_sm;
   if (grid > max_units) grid = max_units;
   if (grid < 1) grid = 1;
-  kern<<<(unsigned)grid, (kTcWarps + 1) * 32, smem, st>>>(a);
+  // launched with programmatic stream serialization: its CTAs may become
+  // resident while the previous kernel finishes (the kernel waits for it)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3((kTcWarps + 1) * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, a) != cudaSuccess) return check_launch("decode_tc_kernel");
   return check_launch("decode_tc_kernel");
 }
 

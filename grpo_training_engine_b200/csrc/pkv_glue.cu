@@ -126,6 +126,9 @@ __global__ void silu_mul_kernel(const T *gate, const T *up, T *out, int64_t n_ve
 template <typename T>
 __global__ void rope_qk_kernel(const T *q, const T *k, const T *cosv, const T *sinv, T *qo, T *ko, int Hq,
                                int Hkv, int D, int64_t qs, int64_t ks, int64_t cs, int64_t qos, int64_t kos) {
+  // the decode launch that follows may start its CTAs' setup now (it waits
+  // for this grid before reading the rows written here)
+  asm volatile("griddepcontrol.launch_dependents;");
   const int64_t b = blockIdx.x;
   const int half = D / 2;
   const int pairs = (Hq + Hkv) * half;
