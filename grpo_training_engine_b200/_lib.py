@@ -15,7 +15,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libpkv.so"
 
-ABI_VERSION = 7  # PKV_ABI_VERSION in include/pkv.h
+ABI_VERSION = 8  # PKV_ABI_VERSION in include/pkv.h
 
 SAMPLE_FORCE_RADIX = 1  # PKV_SAMPLE_FORCE_RADIX
 
@@ -74,6 +74,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pkv_append_decode_run": (
         C.c_int,
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
+         _i64p, _i64p, _i64p, _i64p, _i64p, _i32, _i32, C.c_float, _i32, _i32, _vp, _sz, _vp, _vp],
+    ),
+    "pkv_rope_append_decode_run": (
+        C.c_int,
+        [_vp, _vp, _vp, _vp, _vp, C.c_int64, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
          _i64p, _i64p, _i64p, _i64p, _i64p, _i32, _i32, C.c_float, _i32, _i32, _vp, _sz, _vp, _vp],
     ),
     "pkv_add_rmsnorm": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, C.c_int64, C.c_int64, C.c_int64,

@@ -128,6 +128,11 @@ struct DecodeArgs {
   const void *kn;
   const void *vn;
   int64_t n0, n1;  // k_new / v_new strides [B, Hkv, D] (elements; D contiguous)
+  // RoPE of q and k_new in the producer (nullptr: q and k_new are final):
+  // cos / sin [B, D] in q's dtype, row stride rcs elements
+  const void *rcos;
+  const void *rsin;
+  int64_t rcs;
 };
 
 struct Unit {
@@ -612,6 +617,32 @@ __device__ __forceinline__ void split_pair(float x, float y, uint32_t &hi, uint3
 }
 
 
+// RoPE of one 16-byte chunk x (8 elements of one head) with the chunk p at the
+// same place in the other half of the head, and the cos / sin chunks of those
+// 8 positions; second: x lies in the second half. The rounding points of HF's
+// apply_rotary_pos_emb: x * cos and rotate_half(x) * sin rounded to T, then
+// their sum.
+template <typename T>
+__device__ __forceinline__ uint4 rope_chunk(uint4 x, uint4 p, uint4 cs, uint4 sn, bool second) {
+  const T *xe = reinterpret_cast<const T *>(&x), *pe = reinterpret_cast<const T *>(&p);
+  const T *ce = reinterpret_cast<const T *>(&cs), *se = reinterpret_cast<const T *>(&sn);
+  uint4 out;
+  T *oe = reinterpret_cast<T *>(&out);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float a = Elem<T>::to_f32(T(Elem<T>::to_f32(xe[j]) * Elem<T>::to_f32(ce[j])));
+    const float pv = Elem<T>::to_f32(pe[j]);
+    const float b = Elem<T>::to_f32(T((second ? pv : -pv) * Elem<T>::to_f32(se[j])));
+    oe[j] = T(a + b);
+  }
+  return out;
+}
+
+__device__ __forceinline__ uint4 shfl_xor_u4(uint4 v, int m) {
+  return make_uint4(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m),
+                    __shfl_xor_sync(0xffffffffu, v.z, m), __shfl_xor_sync(0xffffffffu, v.w, m));
+}
+
 template <typename T, int D, int NW, int S, bool kExactP, int NT>
 __global__ void __launch_bounds__((NW + 1) * 32, 1)
 decode_tc_kernel(DecodeArgs a) {
@@ -679,6 +710,9 @@ decode_tc_kernel(DecodeArgs a) {
     uint4 qr[(kTcRows * D * 2 / 16 + 31) / 32];
     int32_t srow = 0;
     uint4 nkv = make_uint4(0, 0, 0, 0);  // appended token: lane < D/8 a K chunk, then V chunks
+    // RoPE: the cos / sin chunk (lane % (D/8)) of the next unit's sequence; a
+    // lane's query chunks and its K chunk all sit at that chunk index
+    uint4 rc = make_uint4(0, 0, 0, 0), rs = make_uint4(0, 0, 0, 0);
     constexpr int kRowChunks = D / 8;    // 16-byte chunks of one K or V row
     constexpr int kQVec = kTcRows * D * 2 / 16;  // 16-byte vectors of a query block
     constexpr int kQPerLane = (kQVec + 31) / 32;
@@ -695,6 +729,11 @@ decode_tc_kernel(DecodeArgs a) {
       for (int i = 0; i < kBtRegs; ++i) {
         const int32_t pi = lane + 32 * i;
         btr[i] = (w < total && pi < np) ? a.bt[u.b * a.bt0 + (int64_t)(u.p_begin + pi) * a.bt1] : -1;
+      }
+      if (a.rcos != nullptr && w < total) {
+        const int64_t off = (u.b * a.rcs + 8 * (lane % kRowChunks)) * 2;
+        rc = *reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(a.rcos) + off);
+        rs = *reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(a.rsin) + off);
       }
       const uint8_t *qb = reinterpret_cast<const uint8_t *>(a.q);
 #pragma unroll
@@ -772,6 +811,14 @@ decode_tc_kernel(DecodeArgs a) {
           }
           btbuf[pi] = page;
         }
+      }
+      if (a.rcos != nullptr) {  // RoPE: the partner chunk (other half of the head) is in lane ^ D/16
+        const bool second = (lane % kRowChunks) >= kRowChunks / 2;
+#pragma unroll
+        for (int i = 0; i < kQPerLane; ++i)
+          qr[i] = rope_chunk<T>(qr[i], shfl_xor_u4(qr[i], kRowChunks / 2), rc, rs, second);
+        const uint4 pk = shfl_xor_u4(nkv, kRowChunks / 2);
+        if (lane < kRowChunks) nkv = rope_chunk<T>(nkv, pk, rc, rs, second);
       }
 #pragma unroll
       for (int i = 0; i < kQPerLane; ++i) {
@@ -1519,7 +1566,9 @@ int decode_run_impl(const void *q, const void *kn, const void *vn, const void *k
                     const int64_t *cache_strides, const int64_t *bt_strides,
                     const int64_t *out_strides, int32_t q_dtype, int32_t kv_dtype, float scale,
                     int32_t pages_per_split, int32_t flags, void *workspace,
-                    size_t workspace_bytes, int32_t *status, void *stream) {
+                    size_t workspace_bytes, int32_t *status, void *stream,
+                    const void *rope_cos = nullptr, const void *rope_sin = nullptr,
+                    int64_t rope_stride = 0) {
   int rc = validate_decode(q, k_cache, v_cache, block_tables, context_lens, out, batch,
                            num_q_heads, num_kv_heads, head_dim, block_size, num_blocks,
                            max_blocks, q_strides, cache_strides, bt_strides, out_strides, q_dtype,
@@ -1591,6 +1640,22 @@ int decode_run_impl(const void *q, const void *kn, const void *vn, const void *k
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const bool tc = tc_eligible(k_cache, v_cache, num_q_heads, num_kv_heads, head_dim, block_size,
                               cache_strides, q_dtype, kv_dtype, flags);
+  if (rope_cos != nullptr) {
+    // RoPE in the producer: the tensor-core kernel with 16-byte query and new
+    // rows and 16-byte cos / sin rows, nothing else
+    const bool rope_ok = kn != nullptr && rope_sin != nullptr && tc && q_dtype == kv_dtype && a.q_vec &&
+                         new_strides[2] == 1 && new_strides[0] % 8 == 0 && new_strides[1] % 8 == 0 &&
+                         aligned_to(kn, 16) && aligned_to(vn, 16) && rope_stride >= head_dim &&
+                         rope_stride % 8 == 0 && aligned_to(rope_cos, 16) && aligned_to(rope_sin, 16);
+    if (!rope_ok) {
+      set_error_detail("RoPE in the decode needs the tensor-core kernel (16-bit q and cache of one dtype), "
+                       "16-byte aligned contiguous q and new rows, and 16-byte aligned cos / sin rows");
+      return PKV_ERR_UNSUPPORTED;
+    }
+    a.rcos = rope_cos;
+    a.rsin = rope_sin;
+    a.rcs = rope_stride;
+  }
   if (kn != nullptr) {
     // the tensor-core kernel takes the new token rows as 16-byte vectors;
     // anything else appends with the append kernel first (slot = length - 1)
@@ -1675,6 +1740,27 @@ extern "C" int pkv_append_decode_run(const void *q, const void *k_new, const voi
                          max_blocks, q_strides, new_strides, cache_strides, bt_strides,
                          out_strides, q_dtype, kv_dtype, scale, pages_per_split, flags,
                          workspace, workspace_bytes, status, stream);
+}
+
+extern "C" int pkv_rope_append_decode_run(
+    const void *q, const void *k_new, const void *v_new, const void *rope_cos, const void *rope_sin,
+    int64_t rope_stride, void *k_cache, void *v_cache, const int32_t *block_tables,
+    const int32_t *context_lens, float *out, int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+    int32_t head_dim, int32_t block_size, int32_t num_blocks, int32_t max_blocks,
+    const int64_t *q_strides, const int64_t *new_strides, const int64_t *cache_strides,
+    const int64_t *bt_strides, const int64_t *out_strides, int32_t q_dtype, int32_t kv_dtype, float scale,
+    int32_t pages_per_split, int32_t flags, void *workspace, size_t workspace_bytes, int32_t *status,
+    void *stream) {
+  if (batch > 0 && (k_new == nullptr || v_new == nullptr || rope_cos == nullptr || rope_sin == nullptr)) {
+    set_error_detail("pkv_rope_append_decode_run: k_new, v_new, cos and sin must not be NULL");
+    return PKV_ERR_INVALID_ARG;
+  }
+  if (batch == 0) return PKV_OK;
+  return decode_run_impl(q, k_new, v_new, k_cache, v_cache, block_tables, context_lens, out, batch,
+                         num_q_heads, num_kv_heads, head_dim, block_size, num_blocks, max_blocks,
+                         q_strides, new_strides, cache_strides, bt_strides, out_strides, q_dtype,
+                         kv_dtype, scale, pages_per_split, flags, workspace, workspace_bytes, status,
+                         stream, rope_cos, rope_sin, rope_stride);
 }
 
 extern "C" int pkv_decode(const void *q, const void *k_cache, const void *v_cache,

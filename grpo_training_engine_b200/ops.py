@@ -328,6 +328,7 @@ def paged_attention_decode(
     k_new: Optional[torch.Tensor] = None,
     v_new: Optional[torch.Tensor] = None,
     out_dtype: Optional[torch.dtype] = None,
+    rope: Optional[tuple[torch.Tensor, torch.Tensor]] = None,
 ) -> torch.Tensor:
     """Single-query attention over the paged cache; returns fp32 [B, Hq, D].
 
@@ -348,6 +349,10 @@ def paged_attention_decode(
     context_lens[b] - 1 (context_lens stay POST-append) and attended to, in
     a single launch on the tensor-core kernel (C ABI pkv_append_decode_run).
     It writes the cache bytes paged_kv_append(..., context_lens - 1) writes.
+
+    With rope=(cos, sin) ([B, D], q's dtype) and k_new / v_new, q and k_new
+    are the rows before RoPE and the launch rotates them as rope_qk does (C ABI
+    pkv_rope_append_decode_run; tensor-core kernel only, PkvError otherwise).
 
     out_dtype=q.dtype (bf16 / fp16 q) returns the output in q's dtype, each
     fp32 result rounded to nearest: the values of ``.to(q.dtype)`` of the fp32
@@ -383,6 +388,8 @@ def paged_attention_decode(
         raise ValueError("decode plan was made for a different geometry.")
     lib = _lib.load()
     ws = plan.workspace
+    if rope is not None and k_new is None:
+        raise ValueError("rope needs k_new / v_new (RoPE runs with the fused append).")
     flags = (_lib.DECODE_FORCE_GENERIC if force_generic else 0) | (_lib.DECODE_EXACT_P if exact else 0)
     if out.dtype != torch.float32:
         flags |= _lib.DECODE_OUT_Q_DTYPE
@@ -397,6 +404,27 @@ def paged_attention_decode(
         if k_new.dtype != k_cache.dtype or v_new.dtype != k_cache.dtype:
             raise ValueError("k_new/v_new must have the cache dtype.")
         _require_cuda(k_new, v_new, k_cache)
+        if rope is not None:
+            cos, sin = rope
+            if cos.shape != (batch, head_dim) or sin.shape != cos.shape or cos.stride() != sin.stride() \
+                    or cos.stride(1) != 1 or cos.dtype != q.dtype or sin.dtype != q.dtype:
+                raise ValueError("rope cos / sin must be matching [batch, head_dim] tensors of q's dtype "
+                                 "with contiguous rows.")
+            _require_cuda(cos, sin)
+            with torch.cuda.device(dev):
+                _lib.check(
+                    "pkv_rope_append_decode_run",
+                    lib.pkv_rope_append_decode_run(
+                        q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+                        cos.stride(0), k_cache.data_ptr(), v_cache.data_ptr(), bt.data_ptr(),
+                        plan.context_lens.data_ptr(), out.data_ptr(), batch, hq, hkv, head_dim, block_size,
+                        num_blocks, max_blocks, _lib.i64_array(q.stride()), _lib.i64_array(k_new.stride()),
+                        _lib.i64_array(k_cache.stride()), _lib.i64_array(bt.stride()), _lib.i64_array(out.stride()),
+                        _dtype_code(q, "q"), _dtype_code(k_cache, "k_cache"), float(scale), plan.pages_per_split,
+                        flags, ws.data_ptr(), ws.numel() * ws.element_size(), _status_ptr(status), _stream(dev),
+                    ),
+                )
+            return out
         with torch.cuda.device(dev):
             _lib.check(
                 "pkv_append_decode_run",

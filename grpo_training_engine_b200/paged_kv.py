@@ -417,6 +417,12 @@ def paged_kv_decode_model(
     down_stack = [_stack((layer.mlp.down_proj,)) if fused_glue and silu_mlp else None for layer in layers]
     head_stack = _stack((lm_head,)) if fused_glue else None
     q_cols, kv_cols = num_heads * head_dim, num_kv_heads * head_dim
+    # With stacked q / k / v on the tensor-core decode, RoPE runs inside the
+    # decode launch (ops.paged_attention_decode(rope=...)): q and k are passed
+    # as the projection wrote them, and the separate RoPE launch disappears.
+    rope_in_decode = fused_glue and all(st is not None for st in qkv_stack) and ops.decode_kernel_kind(
+        torch.empty(batch_size, num_heads, head_dim, dtype=pool.k.dtype, device=device),
+        pool.layer(0)[0]) == "tensor_core" and head_dim % 16 == 0
 
     def _qkv(layer_idx, attn, h):
         st = qkv_stack[layer_idx]
@@ -482,15 +488,22 @@ def paged_kv_decode_model(
             if total is not None:
                 hidden = total
             q_lin, k_lin, v_lin = _qkv(layer_idx, attn, h)
-            # stacked: the keys rotate in place, so k and v are views of one buffer with equal strides
-            q1, k1 = ops.rope_qk(q_lin, k_lin, cos, sin, num_heads, num_kv_heads, head_dim,
-                                 k_out=k_lin if qkv_stack[layer_idx] is not None else None)
-            v1 = v_lin.view(batch_size, num_kv_heads, head_dim)
             k_cache, v_cache = pool.layer(layer_idx)
-            # append at context_lens and attend over new_context_lens: one fused call
-            attn_out = ops.paged_attention_decode(q1, k_cache, v_cache, block_tables, new_context_lens,
-                                                  scale=scale, plan=plan, k_new=k1, v_new=v1,
-                                                  out_dtype=hidden.dtype)
+            v1 = v_lin.view(batch_size, num_kv_heads, head_dim)
+            if rope_in_decode:
+                # RoPE, append at context_lens and attention over new_context_lens: one launch
+                attn_out = ops.paged_attention_decode(
+                    q_lin.view(batch_size, num_heads, head_dim), k_cache, v_cache, block_tables,
+                    new_context_lens, scale=scale, plan=plan, k_new=k_lin.view(batch_size, num_kv_heads, head_dim),
+                    v_new=v1, rope=(cos, sin), out_dtype=hidden.dtype)
+            else:
+                # stacked: the keys rotate in place, so k and v are views of one buffer with equal strides
+                q1, k1 = ops.rope_qk(q_lin, k_lin, cos, sin, num_heads, num_kv_heads, head_dim,
+                                     k_out=k_lin if qkv_stack[layer_idx] is not None else None)
+                # append at context_lens and attend over new_context_lens: one fused call
+                attn_out = ops.paged_attention_decode(q1, k_cache, v_cache, block_tables, new_context_lens,
+                                                      scale=scale, plan=plan, k_new=k1, v_new=v1,
+                                                      out_dtype=hidden.dtype)
             o = _linear(o_stack[layer_idx], attn.o_proj, attn_out.reshape(batch_size, num_heads * head_dim))
             ln = layer.post_attention_layernorm
             h2, hidden = ops.add_rmsnorm(o, ln.weight, ln.variance_epsilon, residual=hidden)

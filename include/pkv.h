@@ -37,8 +37,9 @@
 extern "C" {
 #endif
 
-#define PKV_ABI_VERSION 7  /* 2: pkv_append_decode_run, 3: pkv_sample_top_p, 4: rmsnorm, rope, 5: silu_mul,
-                              6: pkv_sample_top_p flags, 7: pkv_rope_qk output strides */
+#define PKV_ABI_VERSION 8  /* 2: pkv_append_decode_run, 3: pkv_sample_top_p, 4: rmsnorm, rope, 5: silu_mul,
+                              6: pkv_sample_top_p flags, 7: pkv_rope_qk output strides,
+                              8: pkv_rope_append_decode_run */
 
 /* Element types. The reference stores the cache in bfloat16
  * (paged_kv.py:409-410, 629-633); float32 is accepted because the reference
@@ -283,6 +284,28 @@ int pkv_decode(const void *q, const void *k_cache, const void *v_cache,
                int32_t q_dtype, int32_t kv_dtype, float scale,
                int32_t pages_per_split, int32_t flags, void *workspace,
                size_t workspace_bytes, int32_t *status, void *stream);
+
+/*
+ * pkv_rope_append_decode_run: pkv_append_decode_run for q and k_new rows taken
+ * before RoPE (the projections' outputs), rotated inside the launch with
+ * cos / sin [batch, head_dim] (q's dtype, row stride rope_stride) exactly as
+ * pkv_rope_qk rotates them (HF apply_rotary_pos_emb's rounding): one launch
+ * for the per-layer RoPE, page append and decode of the reference's model loop
+ * (paged_kv.py:720-783). Only on the tensor-core kernel: 16-bit q and cache of
+ * one dtype, 16-byte aligned rows with contiguous head_dim for q, k_new, v_new,
+ * cos and sin; anything else returns PKV_ERR_UNSUPPORTED without launching.
+ */
+int pkv_rope_append_decode_run(const void *q, const void *k_new, const void *v_new,
+                               const void *rope_cos, const void *rope_sin, int64_t rope_stride,
+                               void *k_cache, void *v_cache, const int32_t *block_tables,
+                               const int32_t *context_lens, float *out, int32_t batch,
+                               int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                               int32_t block_size, int32_t num_blocks, int32_t max_blocks,
+                               const int64_t *q_strides, const int64_t *new_strides,
+                               const int64_t *cache_strides, const int64_t *bt_strides,
+                               const int64_t *out_strides, int32_t q_dtype, int32_t kv_dtype,
+                               float scale, int32_t pages_per_split, int32_t flags, void *workspace,
+                               size_t workspace_bytes, int32_t *status, void *stream);
 
 /*
  * pkv_decode_noalloc — pkv_decode without a caller workspace. No counterpart

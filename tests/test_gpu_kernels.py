@@ -419,3 +419,60 @@ def test_out_in_q_dtype_equals_cast_of_fp32_out(shape, splits):
     assert torch.equal(got, ref.to(dtype)) and not wide[:, :, :2].any() and not wide[:, :, d + 2:].any()
     with pytest.raises(ValueError, match="out_dtype"):
         paged_attention_decode(q, kc, vc, bt, ctx, out_dtype=torch.float64)
+
+
+ROPE_SHAPES = [
+    (4, 12, 2, 128, 16, torch.bfloat16, [1, 16, 17, 777]),    # 1.5B geometry
+    (3, 28, 4, 128, 16, torch.bfloat16, [5000, 33, 2048]),     # 7B geometry (split-K)
+    (2, 40, 2, 64, 16, torch.float16, [500, 1]),               # two head groups
+    (2, 16, 2, 64, 16, torch.bfloat16, [0, 95]),               # empty context
+]
+
+
+@pytest.mark.parametrize("shape", ROPE_SHAPES, ids=lambda s: f"b{s[0]}q{s[1]}kv{s[2]}d{s[3]}")
+@pytest.mark.parametrize("splits", [0, 3])
+def test_rope_in_decode_equals_rope_then_fused_decode(shape, splits):
+    """RoPE inside the decode launch gives the bits of rope_qk followed by the fused
+    append + decode: the same output and the same cache bytes, also when q / k / v
+    are column views of one stacked projection output."""
+    from grpo_training_engine_b200 import ops
+
+    batch, hq, hkv, d, bs, dtype, ctxs = shape
+    q, kc, vc, bt, ctx = _random_case(41, batch, hq, hkv, d, bs, ctxs, dtype)
+    g = torch.Generator().manual_seed(7)
+    qkv = (torch.randn(batch, (hq + 2 * hkv) * d, generator=g) * 2).to(dtype).to(DEV)
+    ang = torch.rand(batch, d // 2, generator=g) * 50
+    cos = torch.cat([ang.cos(), ang.cos()], 1).to(dtype).to(DEV)
+    sin = torch.cat([ang.sin(), ang.sin()], 1).to(dtype).to(DEV)
+    bt, ctx = bt.to(DEV), ctx.to(DEV)
+    q_lin, k_lin, v_lin = qkv[:, :hq * d], qkv[:, hq * d:(hq + hkv) * d], qkv[:, (hq + hkv) * d:]
+    kc1, vc1 = kc.to(DEV), vc.to(DEV)
+    kc2, vc2 = kc1.clone(), vc1.clone()
+    q1, k1 = ops.rope_qk(q_lin, k_lin, cos, sin, hq, hkv, d)
+    v1 = v_lin.contiguous().view(batch, hkv, d)
+    ref = paged_attention_decode(q1, kc1, vc1, bt, ctx, num_splits=splits, k_new=k1, v_new=v1)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    got = paged_attention_decode(q_lin.view(batch, hq, d), kc2, vc2, bt, ctx, num_splits=splits,
+                                 k_new=k_lin.view(batch, hkv, d), v_new=v_lin.view(batch, hkv, d),
+                                 rope=(cos, sin), status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert torch.equal(got, ref)
+    assert _sha(kc1, vc1) == _sha(kc2, vc2)
+    # contiguous inputs, 16-bit output
+    got16 = paged_attention_decode(q_lin.contiguous().view(batch, hq, d), kc2.clone(), vc2.clone(), bt, ctx,
+                                   num_splits=splits, k_new=k_lin.contiguous().view(batch, hkv, d), v_new=v1,
+                                   rope=(cos, sin), out_dtype=dtype)
+    assert torch.equal(got16, ref.to(dtype))
+
+
+def test_rope_in_decode_refuses_what_it_cannot_serve():
+    from grpo_training_engine_b200 import _lib
+
+    q, kc, vc, bt, ctx = (t.to(DEV) for t in _random_case(3, 2, 4, 2, 8, 4, [5, 9], torch.float32))
+    kn = torch.zeros(2, 2, 8, device=DEV)
+    cs = torch.ones(2, 8, device=DEV)
+    with pytest.raises(_lib.PkvError, match="RoPE in the decode"):  # fp32: CUDA-core kernel
+        paged_attention_decode(q, kc, vc, bt, ctx, k_new=kn, v_new=kn.clone(), rope=(cs, cs))
+    with pytest.raises(ValueError, match="rope needs k_new"):
+        paged_attention_decode(q, kc, vc, bt, ctx, rope=(cs, cs))
