@@ -32,6 +32,9 @@
 //                         page, issued S - 1 pages ahead) and computes
 //                         K.q^T and V^T.P^T with m16n8k16 tensor-core MMAs
 //                         (tokens, resp. head_dim, on M; query heads on N).
+//                         Optionally it also appends the step's new K/V row
+//                         (and rotates q and that K row by RoPE first), and it
+//                         is launched as a programmatic dependent launch.
 //   decode_generic_kernel any dtype (fp32/bf16/fp16), any block size,
 //                         head_dim <= 256: CUDA-core FMAs, plain coalesced
 //                         loads, per-warp online softmax.

@@ -339,7 +339,7 @@ int pkv_decode_noalloc(const void *q, const void *k_cache, const void *v_cache,
 
 /*
  * Which decode kernel pkv_decode_run would launch for these arguments:
- * 1 = TMA + tensor-core kernel, 0 = CUDA-core kernel, <0 = error code.
+ * 1 = tensor-core kernel (cp.async page staging, mma.sync), 0 = CUDA-core kernel, <0 = error code.
  */
 int pkv_decode_kernel_kind(const void *k_cache, int32_t num_q_heads,
                            int32_t num_kv_heads, int32_t head_dim,
