@@ -343,3 +343,29 @@ def test_facade_return_prompt_gives_generate_layout():
     full = pkg.paged_kv_decode(model, ids, mask, max_new_tokens=5, do_sample=False, return_prompt=True)
     assert full.shape == (3, 16) and torch.equal(full[:, :11], ids)
     assert torch.equal(full[:, 11:], new.to(ids.dtype))  # the trainer's outputs[j, prompt_len:]
+
+
+def test_model_level_wrapped_projections_take_the_module_path():
+    """Projections that are not plain nn.Linear (a LoRA-wrapped layer in the trainer)
+    are called as modules: no weight stacks, RoPE as its own launch. Same weights,
+    same greedy tokens as the dense rollout."""
+
+    class Wrapped(torch.nn.Linear):  # stands in for an adapter-wrapped projection
+        pass
+
+    model = _tiny_qwen2(4)
+    for layer in model.model.layers:
+        for owner, names in ((layer.self_attn, ("q_proj", "k_proj", "v_proj", "o_proj")),
+                             (layer.mlp, ("gate_proj", "up_proj", "down_proj"))):
+            for n in names:
+                old = getattr(owner, n)
+                new = Wrapped(old.in_features, old.out_features, bias=old.bias is not None,
+                              device=old.weight.device, dtype=old.weight.dtype)
+                new.load_state_dict(old.state_dict())
+                setattr(owner, n, new)
+    torch.manual_seed(14)
+    ids = torch.randint(0, 96, (3, 19), device=DEV)
+    got = pkg.paged_kv_decode(model, ids, torch.ones_like(ids), max_new_tokens=8, do_sample=False)
+    for row in range(3):
+        ref, gaps = _dense_rollout(model, ids[row:row + 1], 8)
+        _assert_matches_dense(got[row], ref[0], gaps[0])
