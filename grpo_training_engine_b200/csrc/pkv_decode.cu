@@ -585,7 +585,8 @@ struct TcSmem {
   static constexpr size_t kFull = align_up(kMeta + sizeof(SlotMeta) * NW * MD, 16);
   static constexpr size_t kEmpty = kFull + 8 * NW * MD;
   static constexpr size_t kQEmpty = kEmpty + 8 * NW * MD;
-  static constexpr size_t kGroup = kQEmpty + 8 * QS;
+  static constexpr size_t kQFull = kQEmpty + 8 * QS;
+  static constexpr size_t kGroup = kQFull + 8 * QS;
   static constexpr size_t kXSlot = kGroup + 8;  // [NW] slot holding each warp's exchange rows
   static constexpr size_t kXm = align_up(kXSlot + 4 * NW, 16);
   static constexpr size_t kXl = kXm + sizeof(float) * NW * kTcRows;
@@ -661,6 +662,7 @@ decode_tc_kernel(DecodeArgs a) {
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::kFull);
   uint64_t *empty = reinterpret_cast<uint64_t *>(smem + L::kEmpty);
   uint64_t *qempty = reinterpret_cast<uint64_t *>(smem + L::kQEmpty);
+  uint64_t *qfull = reinterpret_cast<uint64_t *>(smem + L::kQFull);  // query slot staged
   uint64_t *group = reinterpret_cast<uint64_t *>(smem + L::kGroup);
   int32_t *xslot = reinterpret_cast<int32_t *>(smem + L::kXSlot);
   float *xm = reinterpret_cast<float *>(smem + L::kXm);
@@ -678,7 +680,10 @@ decode_tc_kernel(DecodeArgs a) {
     mbar_init(&full[tid], 1);
     mbar_init(&empty[tid], 1);
   }
-  if (tid < QS) mbar_init(&qempty[tid], 1);
+  if (tid < QS) {
+    mbar_init(&qempty[tid], 1);
+    mbar_init(&qfull[tid], 1);
+  }
   if (tid == 0) mbar_init(group, NW);
   fence_mbar_init();
   __syncthreads();
@@ -815,46 +820,20 @@ decode_tc_kernel(DecodeArgs a) {
           btbuf[pi] = page;
         }
       }
-      if (a.rcos != nullptr) {  // RoPE: the partner chunk (other half of the head) is in lane ^ D/16
-        const bool second = (lane % kRowChunks) >= kRowChunks / 2;
-#pragma unroll
-        for (int i = 0; i < kQPerLane; ++i)
-          qr[i] = rope_chunk<T>(qr[i], shfl_xor_u4(qr[i], kRowChunks / 2), rc, rs, second);
-        const uint4 pk = shfl_xor_u4(nkv, kRowChunks / 2);
-        if (lane < kRowChunks) nkv = rope_chunk<T>(nkv, pk, rc, rs, second);
-      }
-#pragma unroll
-      for (int i = 0; i < kQPerLane; ++i) {
-        const int v = lane + 32 * i;
-        if (v < kQVec) {
-          const int r = v / (D / 8), c = v % (D / 8);
-          *reinterpret_cast<uint4 *>(qbuf + qs * Sh::kQSlot + r * Sh::kQRow + 16 * c) = qr[i];
-        }
-      }
       // fused append: this unit holds the sequence's last page (its last split)
       const bool app = a.kn != nullptr && u.s == u.nsplit - 1 && u.ctx > 0;
       const int32_t app_pi = app ? (u.ctx - 1) / kBoxRows - u.p_begin : -1;  // page within the unit
       const int32_t app_row = (u.ctx - 1) % kBoxRows;
-      if (app && lane < 2 * kRowChunks)
-        *reinterpret_cast<uint4 *>(qbuf + qs * Sh::kQSlot + Sh::kQNew + 16 * lane) = nkv;
-      __syncwarp();
-      if (app && u.hg == 0 && lane < 2 * kRowChunks) {
-        // one unit per (sequence, kv head) writes the token into the cache for
-        // later steps; every unit reading the page patches its own smem copy
-        const int32_t page = btbuf[app_pi];
-        if (page >= 0) {
-          const int which = lane / kRowChunks, cc = lane % kRowChunks;
-          uint8_t *dst = reinterpret_cast<uint8_t *>(const_cast<void *>(which ? a.vc : a.kc));
-          *reinterpret_cast<uint4 *>(dst + ((int64_t)page * a.c0 + (int64_t)u.kvh * a.c1 +
-                                            (int64_t)app_row * a.c2) * 2 + 16 * cc) = nkv;
-        }
-      }
+      __syncwarp();  // btbuf written
       // (2) publish the unit's pages to the consumer warps (page p -> warp p % NW),
       //     lane cw filling warp cw's ring; each consumer loads its pages itself
-      //     with cp.async
-      if (lane < NW && ok) {
-        const int32_t rounds = npages > 0 ? (npages + NW - 1) / NW : 1;
-        for (int32_t j = 0; j < rounds; ++j) {
+      //     with cp.async. The first page of every warp goes out before the
+      //     query rows are staged, so the first loads overlap the staging; a
+      //     consumer waits for qfull[qs] before it reads the rows.
+      const int32_t rounds = npages > 0 ? (npages + NW - 1) / NW : 1;
+      auto publish = [&](int32_t j0, int32_t j1) {
+        if (lane >= NW || !ok) return;
+        for (int32_t j = j0; j < j1; ++j) {
           const int32_t pi = j * NW + lane;
           const bool has = pi < npages;
           const bool last = (j == rounds - 1);
@@ -865,7 +844,7 @@ decode_tc_kernel(DecodeArgs a) {
           if (use > 0 && !mbar_wait_backoff(&empty[slot], (use - 1) & 1)) {
             flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
             ok = false;
-            break;
+            return;
           }
           const int32_t page = has ? btbuf[pi] : -1;
           SlotMeta md;
@@ -884,11 +863,46 @@ decode_tc_kernel(DecodeArgs a) {
           md.page = page;
           md.newrow = (pi == app_pi) ? app_row : -1;
           md.split_row = split_row;
-          md.pad = 0;
+          md.pad = (nunit / QS) & 1;  // phase of qfull[qs] that stages this unit's rows
           meta[slot] = md;
           mbar_arrive(&full[slot]);
         }
+      };
+      publish(0, 1);
+      __syncwarp();
+      // query rows (and the appended K/V row) -> the unit's query slot
+      if (a.rcos != nullptr) {  // RoPE: the partner chunk (other half of the head) is in lane ^ D/16
+        const bool second = (lane % kRowChunks) >= kRowChunks / 2;
+#pragma unroll
+        for (int i = 0; i < kQPerLane; ++i)
+          qr[i] = rope_chunk<T>(qr[i], shfl_xor_u4(qr[i], kRowChunks / 2), rc, rs, second);
+        const uint4 pk = shfl_xor_u4(nkv, kRowChunks / 2);
+        if (lane < kRowChunks) nkv = rope_chunk<T>(nkv, pk, rc, rs, second);
       }
+#pragma unroll
+      for (int i = 0; i < kQPerLane; ++i) {
+        const int v = lane + 32 * i;
+        if (v < kQVec) {
+          const int r = v / (D / 8), c = v % (D / 8);
+          *reinterpret_cast<uint4 *>(qbuf + qs * Sh::kQSlot + r * Sh::kQRow + 16 * c) = qr[i];
+        }
+      }
+      if (app && lane < 2 * kRowChunks)
+        *reinterpret_cast<uint4 *>(qbuf + qs * Sh::kQSlot + Sh::kQNew + 16 * lane) = nkv;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&qfull[qs]);
+      if (app && u.hg == 0 && lane < 2 * kRowChunks) {
+        // one unit per (sequence, kv head) writes the token into the cache for
+        // later steps; every unit reading the page patches its own smem copy
+        const int32_t page = btbuf[app_pi];
+        if (page >= 0) {
+          const int which = lane / kRowChunks, cc = lane % kRowChunks;
+          uint8_t *dst = reinterpret_cast<uint8_t *>(const_cast<void *>(which ? a.vc : a.kc));
+          *reinterpret_cast<uint4 *>(dst + ((int64_t)page * a.c0 + (int64_t)u.kvh * a.c1 +
+                                            (int64_t)app_row * a.c2) * 2 + 16 * cc) = nkv;
+        }
+      }
+      publish(1, rounds);
       // (3) prefetch: the next unit's block-table entries and query rows, the
       //     descriptor of the one after
       load_next(w2, d2);
@@ -1043,6 +1057,7 @@ decode_tc_kernel(DecodeArgs a) {
     const int4 tailv = *reinterpret_cast<const int4 *>(&meta[ms].page);  // bytes 48..63
     md.newrow = tailv.y;
     md.split_row = tailv.z;
+    md.pad = tailv.w;
     if (md.last || md.work != cur_work) {
       // 16-byte aligned blocks of SlotMeta: bytes 16..31 and 32..47
       const int4 m1v = *reinterpret_cast<const int4 *>(&meta[ms].qslot);
@@ -1063,6 +1078,11 @@ decode_tc_kernel(DecodeArgs a) {
     if (md.work != cur_work) {
       cur_work = md.work;
       cur_qslot = md.qslot;
+      if (!mbar_wait_bounded(&qfull[md.qslot], (uint32_t)md.pad)) {  // the unit's rows are staged
+        flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
+        cp_async_wait_all();
+        return;
+      }
       const uint32_t qs0 = smem_u32(qbuf + md.qslot * Sh::kQSlot) + q_off;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
