@@ -409,13 +409,24 @@ def paged_kv_decode_model(
             return mod(h)
         return h @ st[0] if st[1] is None else torch.addmm(st[1], h, st[0])
 
+    # the copies need as much memory as those weights; without twice that free
+    # (the trainer may hold most of the GPU) the modules are called as they are
+    proj_bytes = sum(m.weight.numel() * m.weight.element_size() for layer in layers
+                     for owner, names in ((layer.self_attn, ("q_proj", "k_proj", "v_proj", "o_proj")),
+                                          (layer.mlp, ("gate_proj", "up_proj", "down_proj")))
+                     for m in (getattr(owner, n, None) for n in names)
+                     if isinstance(getattr(m, "weight", None), torch.Tensor)) if fused_glue else 0
+    if fused_glue and device.type == "cuda" and torch.cuda.mem_get_info(device)[0] < 2 * proj_bytes:
+        fused_glue_copies = False
+    else:
+        fused_glue_copies = fused_glue
     qkv_stack = [_stack((layer.self_attn.q_proj, layer.self_attn.k_proj, layer.self_attn.v_proj))
-                 if fused_glue else None for layer in layers]
-    o_stack = [_stack((layer.self_attn.o_proj,)) if fused_glue else None for layer in layers]
-    gate_up_stack = [_stack((layer.mlp.gate_proj, layer.mlp.up_proj)) if fused_glue and silu_mlp else None
+                 if fused_glue_copies else None for layer in layers]
+    o_stack = [_stack((layer.self_attn.o_proj,)) if fused_glue_copies else None for layer in layers]
+    gate_up_stack = [_stack((layer.mlp.gate_proj, layer.mlp.up_proj)) if fused_glue_copies and silu_mlp else None
                      for layer in layers]
-    down_stack = [_stack((layer.mlp.down_proj,)) if fused_glue and silu_mlp else None for layer in layers]
-    head_stack = _stack((lm_head,)) if fused_glue else None
+    down_stack = [_stack((layer.mlp.down_proj,)) if fused_glue_copies and silu_mlp else None for layer in layers]
+    head_stack = _stack((lm_head,)) if fused_glue_copies else None
     q_cols, kv_cols = num_heads * head_dim, num_kv_heads * head_dim
     # With stacked q / k / v on the tensor-core decode, RoPE runs inside the
     # decode launch (ops.paged_attention_decode(rope=...)): q and k are passed
