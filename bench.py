@@ -301,7 +301,7 @@ def run_ours(args, rank, world, local):
             # per-launch events around layer 0 only: an event node between two
             # launches would also keep the second one from starting early
             if ev_pairs is not None and layer == 0:
-                ev_pairs[layer][0].record()
+                ev_pairs[0][0].record()
             if args.separate_append:
                 pkv.paged_attention_decode(wl.q[layer], kc, vc, wl.block_tables, wl.ctx, out=wl.out[layer],
                                            plan=plan, exact=args.exact)
@@ -310,7 +310,7 @@ def run_ours(args, rank, world, local):
                                            plan=plan, exact=args.exact, k_new=wl.k_new[layer],
                                            v_new=wl.v_new[layer])
             if ev_pairs is not None and layer == 0:
-                ev_pairs[layer][1].record()
+                ev_pairs[0][1].record()
         return plan
 
     step()
@@ -320,8 +320,8 @@ def run_ours(args, rank, world, local):
     torch.cuda.synchronize()
 
     # external events: inside a CUDA graph they become event-record nodes
-    ev_all = [[[torch.cuda.Event(enable_timing=True, external=args.graph) for _ in range(2)] for _ in range(L)]
-              for _ in range(args.steps)]
+    ev_all = [[[torch.cuda.Event(enable_timing=True, external=args.graph) for _ in range(2)]]
+              for _ in range(args.steps)]  # one pair per step, around layer 0
     graph = None
     if args.graph:
         graph = capture_steps(lambda: [step(ev_all[s]) for s in range(args.steps)])
