@@ -607,6 +607,10 @@ __device__ __forceinline__ uint32_t slab_chunk_offset(int c) {
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
+// 16-byte copy of which only the first src_bytes are read; the rest are zero
+__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
@@ -1023,11 +1027,16 @@ decode_tc_kernel(DecodeArgs a) {
           const uint8_t *ks = kbase + off;
           const uint8_t *vs = vbase + off;
           const uint32_t dst = smem_u32(tiles + (size_t)(cw * S + (e % S)) * Sh::kSlot);
+          // rows past the context are zero-filled, not read: their weights are
+          // 0, but 0 x (a NaN or Inf left in an unused cache slot) is not, and
+          // the reference's masked loads read 0 there
+          const int32_t valid = meta[ms].valid;
 #pragma unroll
           for (int i = 0; i < D / 16; ++i) {
             const uint32_t o = dst + dst_off[i & 3] + 1024 * (i >> 2);
-            cp_async16(o, ks + 512 * i);
-            cp_async16(o + Sh::kTile, vs + 512 * i);
+            const uint32_t n = (32 * i + lane) / (D / 8) < valid ? 16u : 0u;  // token row of this chunk
+            cp_async16_zfill(o, ks + 512 * i, n);
+            cp_async16_zfill(o + Sh::kTile, vs + 512 * i, n);
           }
         }
       }

@@ -476,3 +476,32 @@ def test_rope_in_decode_refuses_what_it_cannot_serve():
         paged_attention_decode(q, kc, vc, bt, ctx, k_new=kn, v_new=kn.clone(), rope=(cs, cs))
     with pytest.raises(ValueError, match="rope needs k_new"):
         paged_attention_decode(q, kc, vc, bt, ctx, rope=(cs, cs))
+
+
+@pytest.mark.parametrize("dtype,d", [(torch.bfloat16, 128), (torch.float16, 64)])
+def test_nan_in_unused_page_slots_does_not_leak(dtype, d):
+    """Slots past a sequence's context in its last page may hold anything (a cache
+    from torch.empty); the reference's masked loads never read them. NaN / Inf there
+    must not reach the output: same bits as with zeros there, fused append included."""
+    batch, hq, hkv, bs = 3, 12, 2, 16
+    ctxs = [5, 40, 17]
+    q, kc, vc, bt, ctx = _random_case(51, batch, hq, hkv, d, bs, ctxs, dtype)
+    q, kc, vc, bt, ctx = (t.to(DEV) for t in (q, kc, vc, bt, ctx))
+    dirty_k, dirty_v = kc.clone(), vc.clone()
+    for b, c in enumerate(ctxs):
+        page = int(bt[b, c // bs])
+        dirty_k[page, :, c % bs:] = float("nan")
+        dirty_v[page, :, c % bs:] = float("inf")
+        kc[page, :, c % bs:] = 0
+        vc[page, :, c % bs:] = 0
+    for splits in (0, 2):
+        clean = paged_attention_decode(q, kc, vc, bt, ctx, num_splits=splits)
+        got = paged_attention_decode(q, dirty_k, dirty_v, bt, ctx, num_splits=splits)
+        assert torch.isfinite(got).all() and torch.equal(got, clean)
+    # fused append: the new token lands at ctx - 1 of the post-append length
+    g = torch.Generator().manual_seed(2)
+    kn, vn = (torch.randn(batch, hkv, d, generator=g).to(dtype).to(DEV) for _ in range(2))
+    post = ctx + 1
+    clean = paged_attention_decode(q, kc.clone(), vc.clone(), bt, post, k_new=kn, v_new=vn)
+    got = paged_attention_decode(q, dirty_k.clone(), dirty_v.clone(), bt, post, k_new=kn, v_new=vn)
+    assert torch.isfinite(got).all() and torch.equal(got, clean)
