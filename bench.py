@@ -46,7 +46,7 @@ METRIC = "paged KV decode: KV-read HBM GB/s and seq-steps/s at 1/2/4/8 B200"
 # ncu capture of decode_tc_kernel on the config-4 geometry (512 sequences, one
 # layer; profiles/decode_tc_512seq_1layer_ncu.md). Traffic grows with the
 # pages read, so roofline.traffic scales it to the full launch.
-DECODE_DRAM_TRAFFIC_RATIO = 1.0032
+DECODE_DRAM_TRAFFIC_RATIO = 1.0017
 UNIT = "seq-steps/s"
 
 
