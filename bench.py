@@ -718,12 +718,15 @@ def run_rollout(args):
 
     def per_step(graph, x=ids, share=True):
         # both lengths once untimed (allocator pools of both sizes, kernels loaded), then
-        # the median of three (short, long) pairs: setup time varies from call to call
+        # five calls of each. The HF prefill of distinct prompts varies by up to ~0.3 s from
+        # call to call, always upward (as much as 128 steps take), so each length's fastest
+        # call is the one without that delay: the difference of the minima
         timed(short, graph, x, share)
         timed(long_, graph, x, share)
-        pairs = [(timed(short, graph, x, share), timed(long_, graph, x, share)) for _ in range(3)]
-        ms = sorted((t_l - t_s) / (long_ - short) for t_s, t_l in pairs)[1]
-        setup = sorted(t_s for t_s, _ in pairs)[1] - short * ms
+        pairs = [(timed(short, graph, x, share), timed(long_, graph, x, share)) for _ in range(5)]
+        t_s = min(t for t, _ in pairs)
+        ms = (min(t for _, t in pairs) - t_s) / (long_ - short)
+        setup = t_s - short * ms
         return {"ms_per_step": round(ms, 3), "seq_steps_per_s": round(batch / ms * 1e3, 1),
                 "setup_prefill_ms": round(setup, 2)}
 
