@@ -478,12 +478,23 @@ def test_rope_in_decode_refuses_what_it_cannot_serve():
         paged_attention_decode(q, kc, vc, bt, ctx, rope=(cs, cs))
 
 
-@pytest.mark.parametrize("dtype,d", [(torch.bfloat16, 128), (torch.float16, 64)])
-def test_nan_in_unused_page_slots_does_not_leak(dtype, d):
+@pytest.mark.parametrize(
+    "dtype,d,hq,hkv,kw",
+    [
+        (torch.bfloat16, 128, 12, 2, {}),
+        (torch.float16, 64, 12, 2, {}),
+        (torch.bfloat16, 128, 16, 1, {}),  # 16 query heads per KV head: two head tiles
+        (torch.bfloat16, 128, 12, 2, {"exact": True}),
+        (torch.bfloat16, 128, 12, 2, {"force_generic": True}),
+        (torch.float32, 128, 12, 2, {}),  # fp32 cache: the generic kernel
+    ],
+)
+def test_nan_in_unused_page_slots_does_not_leak(dtype, d, hq, hkv, kw):
     """Slots past a sequence's context in its last page may hold anything (a cache
     from torch.empty); the reference's masked loads never read them. NaN / Inf there
-    must not reach the output: same bits as with zeros there, fused append included."""
-    batch, hq, hkv, bs = 3, 12, 2, 16
+    must not reach the output: same bits as with zeros there, fused append included,
+    in every kernel variant."""
+    batch, bs = 3, 16
     ctxs = [5, 40, 17]
     q, kc, vc, bt, ctx = _random_case(51, batch, hq, hkv, d, bs, ctxs, dtype)
     q, kc, vc, bt, ctx = (t.to(DEV) for t in (q, kc, vc, bt, ctx))
@@ -495,13 +506,13 @@ def test_nan_in_unused_page_slots_does_not_leak(dtype, d):
         kc[page, :, c % bs:] = 0
         vc[page, :, c % bs:] = 0
     for splits in (0, 2):
-        clean = paged_attention_decode(q, kc, vc, bt, ctx, num_splits=splits)
-        got = paged_attention_decode(q, dirty_k, dirty_v, bt, ctx, num_splits=splits)
+        clean = paged_attention_decode(q, kc, vc, bt, ctx, num_splits=splits, **kw)
+        got = paged_attention_decode(q, dirty_k, dirty_v, bt, ctx, num_splits=splits, **kw)
         assert torch.isfinite(got).all() and torch.equal(got, clean)
     # fused append: the new token lands at ctx - 1 of the post-append length
     g = torch.Generator().manual_seed(2)
     kn, vn = (torch.randn(batch, hkv, d, generator=g).to(dtype).to(DEV) for _ in range(2))
     post = ctx + 1
-    clean = paged_attention_decode(q, kc.clone(), vc.clone(), bt, post, k_new=kn, v_new=vn)
-    got = paged_attention_decode(q, dirty_k.clone(), dirty_v.clone(), bt, post, k_new=kn, v_new=vn)
+    clean = paged_attention_decode(q, kc.clone(), vc.clone(), bt, post, k_new=kn, v_new=vn, **kw)
+    got = paged_attention_decode(q, dirty_k.clone(), dirty_v.clone(), bt, post, k_new=kn, v_new=vn, **kw)
     assert torch.isfinite(got).all() and torch.equal(got, clean)
