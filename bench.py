@@ -13,8 +13,10 @@ Multi-GPU: one process per GPU (torchrun). Sequences are independent, so the
 job is partitioned — each rank owns a seeded shard of whole sequences
 (LPT-balanced by context length), its own page pool and block tables — and no
 collective runs inside the timed region; only the start barrier and the
-max-over-ranks time reduction cross ranks. Per-GPU work is fixed as N grows
-("scaling": "weak").
+max-over-ranks time reduction cross ranks. `--scaling strong` (the default)
+shards the config's own sequence count over the N GPUs, as BASELINE states the
+configs (config 4: 1024 sequences over 1/2/4/8 GPUs); `--scaling weak` gives
+every GPU the full count.
 
 Rank 0 prints ONE JSON line. `--impl reference` times the CPU restatement of
 the reference algorithm (oracle/, the reference itself is Python/Triton and
@@ -42,11 +44,12 @@ sys.path.insert(0, str(REPO))
 
 METRIC = "paged KV decode: KV-read HBM GB/s and seq-steps/s at 1/2/4/8 B200"
 
-# DRAM bytes (read + write) per algorithmic byte of one decode launch, from an
-# ncu capture of decode_tc_kernel on the config-4 geometry (512 sequences, one
-# layer; profiles/decode_tc_512seq_1layer_ncu.md). Traffic grows with the
-# pages read, so roofline.traffic scales it to the full launch.
-DECODE_DRAM_TRAFFIC_RATIO = 1.0017
+# DRAM bytes (read + write) per algorithmic byte of one decode launch, per
+# config, from one-launch ncu captures of decode_tc_kernel on a reduced case of
+# that config's geometry (dram__bytes_read.sum + dram__bytes_write.sum over the
+# launch's algorithmic bytes). Traffic grows with the pages read, so
+# roofline.traffic scales the ratio to the full launch.
+DECODE_DRAM_TRAFFIC_RATIO = {4: 1.0017}
 UNIT = "seq-steps/s"
 
 
@@ -73,29 +76,66 @@ def global_lengths(config: int, n_total: int, seed: int = 1234) -> np.ndarray:
     raise ValueError(config)
 
 
+def shard_indices(config: int, lens: np.ndarray, rank: int, world: int) -> list[int]:
+    """Sequences of `rank`: LPT by context length (config 3: whole GRPO groups of 8,
+    so a group's shared prompt pages stay on one GPU)."""
+    if config == 3:
+        group = 8
+        n_groups = len(lens) // group
+        costs = [lens[g * group:(g + 1) * group].sum() for g in range(n_groups)]
+        groups = lpt_assign(costs, world)[rank]
+        return [g * group + j for g in groups for j in range(group)]
+    return lpt_assign(lens.tolist(), world)[rank]
+
+
+def workload_config(args, world: int) -> dict:
+    """The `config` object of the JSON line: the workload only (both arms print the same one)."""
+    c = dict(CONFIGS[args.config])
+    strong = args.scaling == "strong"
+    if args.seqs:
+        c["seqs"] = args.seqs
+        c["name"] += f" [reduced to {args.seqs} seqs" + (" in all]" if strong else "/GPU]")
+    n_total = c["seqs"] if strong else c["seqs"] * world
+    lens = global_lengths(args.config, n_total)
+    mine = shard_indices(args.config, lens, 0, world)
+    layers = args.layers or c["layers"]
+    pages = sum((int(lens[i]) + c["bs"] - 1) // c["bs"] for i in mine)
+    if args.config == 3:  # each group's 32 prompt pages are stored once
+        pages -= (len(mine) // 8) * 7 * (512 // c["bs"])
+    pool_gb = 2 * layers * pages * c["hkv"] * c["bs"] * c["d"] * 2 / 1e9
+    return {
+        "workload": c["name"],
+        "seqs_total": n_total,
+        "seqs_per_gpu": len(mine),
+        "layers": layers,
+        "q_heads": c["hq"],
+        "kv_heads": c["hkv"],
+        "head_dim": c["d"],
+        "block_size": c["bs"],
+        "step": "per layer: append 1 token per sequence and kv head, then paged decode attention over ctx",
+        "l2": "no flush: KV pool of rank 0 %.1f GB >> 126 MB L2" % pool_gb,
+        "parallelism": f"dp{world} (sequence shards, LPT by context length, no collective)",
+        "sharding": (f"strong: the config's {n_total} sequences split over {world} GPU(s)" if strong else
+                     f"weak: {c['seqs']} sequences per GPU ({n_total} in all)"),
+    }
+
+
 class Workload:
     """One rank's shard: page pool, block tables, per-layer q/k_new/v_new, context lengths."""
 
-    def __init__(self, config: int, rank: int, world: int, layers: int | None, device, seqs: int | None = None):
-        from grpo_training_engine_b200.sharding import lpt_assign
-
+    def __init__(self, config: int, rank: int, world: int, layers: int | None, device, seqs: int | None = None,
+                 strong: bool = True):
         c = dict(CONFIGS[config])
         if seqs:
             c["seqs"] = seqs
-            c["name"] += f" [reduced to {seqs} seqs/GPU]"
+            c["name"] += f" [reduced to {seqs} seqs" + (" in all]" if strong else "/GPU]")
         self.config, self.cfg = config, c
         self.layers = layers or c["layers"]
         hq, hkv, d, bs = c["hq"], c["hkv"], c["d"], c["bs"]
-        n_total = c["seqs"] * world
+        n_total = c["seqs"] if strong else c["seqs"] * world
+        self.n_total = n_total
         lens = global_lengths(config, n_total)
-        if config == 3:
-            group = 8
-            n_groups = n_total // group
-            costs = [lens[g * group:(g + 1) * group].sum() for g in range(n_groups)]
-            groups = lpt_assign(costs, world)[rank]
-            mine = [g * group + j for g in groups for j in range(group)]
-        else:
-            mine = lpt_assign(lens.tolist(), world)[rank]
+        mine = shard_indices(config, lens, rank, world)
         self.ctx_post = torch.tensor([int(lens[i]) for i in mine], dtype=torch.int32)
         B = len(mine)
         self.B, self.hq, self.hkv, self.d, self.bs = B, hq, hkv, d, bs
@@ -157,6 +197,17 @@ class Workload:
 
     def append_bytes_layer(self) -> int:
         return self.B * self.hkv * self.d * 2 * 2 * 2  # read new K,V + write into pages
+
+
+def lpt_assign(costs, world):
+    """sharding.lpt_assign, loaded from its file: importing the package would
+    load libpkv.so, which the reference arm must not map."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("_pkv_sharding", REPO / "grpo_training_engine_b200" / "sharding.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod.lpt_assign(costs, world)
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -284,7 +335,7 @@ def run_ours(args, rank, world, local):
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    wl = Workload(args.config, rank, world, args.layers, device, args.seqs)
+    wl = Workload(args.config, rank, world, args.layers, device, args.seqs, strong=args.scaling == "strong")
     L, B = wl.layers, wl.B
     stream = torch.cuda.current_stream(device)
 
@@ -296,12 +347,14 @@ def run_ours(args, rank, world, local):
         ws["buf"] = plan.workspace
         for layer in range(L):
             kc, vc = wl.k_pool[layer], wl.v_pool[layer]
-            if args.separate_append:
-                pkv.paged_kv_append(wl.k_new[layer], wl.v_new[layer], kc, vc, wl.block_tables, wl.ctx_pre)
-            # per-launch events around layer 0 only: an event node between two
-            # launches would also keep the second one from starting early
+            # one event pair per step, around all L layers after the plan: an
+            # event node between two layers would keep the second launch from
+            # starting early (programmatic dependent launch), so the per-layer
+            # time is the bracket / L
             if ev_pairs is not None and layer == 0:
                 ev_pairs[0][0].record()
+            if args.separate_append:
+                pkv.paged_kv_append(wl.k_new[layer], wl.v_new[layer], kc, vc, wl.block_tables, wl.ctx_pre)
             if args.separate_append:
                 pkv.paged_attention_decode(wl.q[layer], kc, vc, wl.block_tables, wl.ctx, out=wl.out[layer],
                                            plan=plan, exact=args.exact)
@@ -309,7 +362,7 @@ def run_ours(args, rank, world, local):
                 pkv.paged_attention_decode(wl.q[layer], kc, vc, wl.block_tables, wl.ctx, out=wl.out[layer],
                                            plan=plan, exact=args.exact, k_new=wl.k_new[layer],
                                            v_new=wl.v_new[layer])
-            if ev_pairs is not None and layer == 0:
+            if ev_pairs is not None and layer == L - 1:
                 ev_pairs[0][1].record()
         return plan
 
@@ -321,7 +374,7 @@ def run_ours(args, rank, world, local):
 
     # external events: inside a CUDA graph they become event-record nodes
     ev_all = [[[torch.cuda.Event(enable_timing=True, external=args.graph) for _ in range(2)]]
-              for _ in range(args.steps)]  # one pair per step, around layer 0
+              for _ in range(args.steps)]  # one pair per step, around the L layers
     graph = None
     if args.graph:
         graph = capture_steps(lambda: [step(ev_all[s]) for s in range(args.steps)])
@@ -347,8 +400,16 @@ def run_ours(args, rank, world, local):
     clk = clocks.stop()
     ms_local = t0.elapsed_time(t1)
     ms = max_over_ranks(ms_local, world)
-    decode_ms = [pairs[0][0].elapsed_time(pairs[0][1]) for pairs in ev_all]
-    decode_avg_ms = sum(decode_ms) / len(decode_ms)
+    layers_ms = [pairs[0][0].elapsed_time(pairs[0][1]) for pairs in ev_all]
+    decode_avg_ms = sum(layers_ms) / len(layers_ms) / L  # mean launch (one layer) of the step
+    rank_avg = [decode_avg_ms]
+    if world > 1:  # per-rank step-time spread: every rank's mean layer time
+        import torch.distributed as dist
+
+        t = torch.zeros(world, dtype=torch.float64, device=device)
+        t[rank] = ms_local / args.steps
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        rank_avg = [round(float(x), 4) for x in t.tolist()]
 
     if world > 1:
         import torch.distributed as dist
@@ -366,6 +427,7 @@ def run_ours(args, rank, world, local):
     dec_bytes = wl.decode_bytes_layer() + (0 if args.separate_append else wl.append_bytes_layer())
     achieved = dec_bytes / (decode_avg_ms / 1e3) / 1e9
     merges = 1 if wl.max_blocks > plan_pps(wl, args) else 0  # split-K merge launch per layer
+    traffic_ratio = DECODE_DRAM_TRAFFIC_RATIO.get(wl.config)
     launches = args.steps * (1 + ((2 if args.separate_append else 1) + merges) * L)
 
     # ---- end-to-end through the public ops with pinned host buffers
@@ -388,28 +450,21 @@ def run_ours(args, rank, world, local):
             "warmup": args.warmup,
             "ms_per_step": round(ms_per_step, 4),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": args.scaling,
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic: seeded N(0,1) q/K/V/new tokens, seeded context lengths and random page permutations",
-            "config": {
-                "workload": wl.cfg["name"],
-                "seqs_per_gpu": B,
-                "layers": L,
-                "q_heads": wl.hq,
-                "kv_heads": wl.hkv,
-                "head_dim": wl.d,
-                "block_size": wl.bs,
+            "config": workload_config(args, world),
+            "run": {
                 "pages_per_split": plan_pps(wl, args),
-                "step": ("per layer: append 1 token/seq/kv-head + paged decode attention; 1 plan per step"
-                         + ("" if args.separate_append else " (append fused into the decode launch)")),
+                "step": ("1 plan per step, then per layer one launch that appends the token and decodes"
+                         if not args.separate_append else "1 plan per step, then per layer append + decode launches"),
                 "launch": (f"the {args.steps} timed steps captured as one CUDA graph, replayed once (after "
                            f"{args.warmup} eager warm-up steps and one untimed replay)" if args.graph else
                            "eager launches from Python"),
                 "softmax_weights": "16-bit hi+lo (exact)" if args.exact else "bf16",
-                "l2": "no flush: KV pool per GPU %.1f GB >> 126 MB L2" % (2 * wl.k_pool.numel() * 2 / 1e9),
-                "parallelism": f"dp{world} (sequence shards, LPT by context length, no collective)",
             },
+            "step_ms_per_rank": rank_avg if world > 1 else None,
             "kv_read_GBps": round(kv_gbs, 1),
             "kv_read_GBps_per_gpu": round(kv_gbs / world, 1),
             "roofline": {
@@ -422,18 +477,20 @@ def run_ours(args, rank, world, local):
                 "unit": "GB/s",
                 "frac": round(achieved / peak, 4),
                 "traffic": (args.traffic_bytes if args.traffic_bytes is not None else
-                            (int(DECODE_DRAM_TRAFFIC_RATIO * dec_bytes) if wl.config == 4 else None)),
-                "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of a reduced "
-                                   "capture (512 seqs, 1 layer), scaled by pages read"
-                                   if wl.config == 4 else None),
+                            (int(traffic_ratio * dec_bytes) if traffic_ratio else None)),
+                "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of a one-launch "
+                                   "capture of a reduced case of this config, scaled by pages read"
+                                   if traffic_ratio else None),
                 "algorithmic_bytes_per_launch": dec_bytes,
                 "avg_launch_ms": round(decode_avg_ms, 4),
+                "timing": (f"CUDA events around the {L} layers of every timed step (after its plan), "
+                           f"divided by {L}" + (", split-K merge launches included" if merges else "")),
             },
             "gpu_launches": launches,
             "clocks": clk,
         }
         if wl.config == 3:
-            line["config"]["unique_kv_GBps"] = round(kv_gbs * wl.unique_tokens / float(wl.ctx_post.sum()), 1)
+            line["unique_kv_GBps"] = round(kv_gbs * wl.unique_tokens / float(wl.ctx_post.sum()), 1)
         if e2e is not None:
             line["e2e"] = e2e
         if cpu is not None:
@@ -571,7 +628,7 @@ def run_e2e(args, wl, world, device):
     barrier(world)
     ms = max_over_ranks(t0.elapsed_time(t1), world) / args.steps
     ok = torch.allclose(out_h[0], wl.out[0].cpu())
-    total = wl.B * world
+    total = wl.n_total
     h2d_bytes = in_h.numel() + ctx_h.numel() * 4
     return {
         "value": round(total / (ms / 1e3), 2),
@@ -765,12 +822,13 @@ def run_reference(args, rank, world):
 
     oracle.build()
     threads = oracle.max_threads()
-    c = CONFIGS[args.config]
-    # build the same rank-0 workload lengths on the CPU without a GPU pool
-    lens = global_lengths(args.config, c["seqs"] * max(world, 1))
-    from grpo_training_engine_b200.sharding import lpt_assign
-
-    mine = lpt_assign(lens.tolist(), max(world, 1))[0]
+    c = dict(CONFIGS[args.config])
+    if args.seqs:
+        c["seqs"] = args.seqs
+    # the rank-0 shard's lengths of the same workload, on the CPU without a GPU pool
+    world = max(world, 1)
+    lens = global_lengths(args.config, c["seqs"] if args.scaling == "strong" else c["seqs"] * world)
+    mine = shard_indices(args.config, lens, 0, world)
     layers = args.layers or c["layers"]
     hq, hkv, d, bs = c["hq"], c["hkv"], c["d"], c["bs"]
     rs = np.random.RandomState(5)
@@ -829,12 +887,11 @@ def run_reference(args, rank, world):
         "warmup": args.warmup,
         "ms_per_step": round(1e3 * total / args.steps, 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": args.scaling,
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic: seeded N(0,1) q/K/V, seeded context lengths and page permutations",
-        "config": {"workload": c["name"], "layers": layers, "q_heads": hq, "kv_heads": hkv, "head_dim": d,
-                   "block_size": bs},
+        "data": "synthetic: seeded N(0,1) q/K/V/new tokens, seeded context lengths and random page permutations",
+        "config": workload_config(args, world),
         "cpu_baseline": {
             "value": round(value, 4),
             "unit": UNIT,
@@ -857,7 +914,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", type=int, default=4, choices=sorted(CONFIGS))
     ap.add_argument("--layers", type=int, default=None, help="override the layer count (diagnostics only)")
-    ap.add_argument("--seqs", type=int, default=None, help="override sequences per GPU (diagnostics only)")
+    ap.add_argument("--seqs", type=int, default=None,
+                    help="override the sequence count (in all with strong scaling, per GPU with weak; diagnostics)")
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                    help="strong: the config's sequences split over the GPUs (BASELINE's statement of the configs); "
+                         "weak: every GPU gets the config's full sequence count")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--pages-per-split", type=int, default=0)
     ap.add_argument("--exact", action="store_true", help="decode with PKV_DECODE_EXACT_P")

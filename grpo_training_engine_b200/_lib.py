@@ -38,6 +38,7 @@ DEV_WAIT_TIMEOUT = 4
 DECODE_FORCE_GENERIC = 1
 DECODE_EXACT_P = 2
 DECODE_OUT_Q_DTYPE = 4  # PKV_DECODE_OUT_Q_DTYPE
+DECODE_TEST_WAIT_TIMEOUT = 1 << 30  # PKV_DECODE_TEST_WAIT_TIMEOUT (tests of the bounded waits only)
 NOALLOC_SCRATCH_BYTES = 32 << 20  # PKV_NOALLOC_SCRATCH_BYTES in include/pkv.h
 
 _i32 = C.c_int32

@@ -135,8 +135,9 @@ constexpr uint32_t kMaxWaitTries = 1u << 22;
 // after the phase completes; 2^24 polls bound the wait to a few seconds.
 constexpr uint32_t kPollNs = 100;
 constexpr uint32_t kMaxPolls = 1u << 24;
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kMaxPolls; ++i) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
+                                                  uint32_t max_polls = kMaxPolls) {
+  for (uint32_t i = 0; i < max_polls; ++i) {
     if (mbar_try_wait_ns(bar, parity, kPollNs)) return true;
   }
   return false;
@@ -145,9 +146,10 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
 // Bounded wait for a thread that is usually AHEAD of the threads it waits for
 // (a producer whose ring is full): after a few polls it sleeps with growing
 // back-off, so it does not take issue slots from the warps it is waiting on.
-__device__ __forceinline__ bool mbar_wait_backoff(uint64_t *bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t *bar, uint32_t parity,
+                                                  uint32_t max_tries = kMaxWaitTries) {
   uint32_t sleep_ns = 32;
-  for (uint32_t i = 0; i < kMaxWaitTries; ++i) {
+  for (uint32_t i = 0; i < max_tries; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if (i >= 4) {
       __nanosleep(sleep_ns);

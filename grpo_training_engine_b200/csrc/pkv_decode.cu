@@ -55,6 +55,8 @@ constexpr int kGenWarps = kGenThreads / 32;
 // lane-strided: kBtRegs per lane, so a split has at most kMaxPagesPerSplit pages.
 constexpr int kBtRegs = 16;
 constexpr int32_t kMaxPagesPerSplit = kBtRegs * 32;
+// wait bound of every device wait under PKV_DECODE_TEST_WAIT_TIMEOUT
+constexpr uint32_t kTestWaitPolls = 4096;
 
 // ---------------------------------------------------------------------------
 // workspace layout
@@ -136,6 +138,11 @@ struct DecodeArgs {
   const void *rcos;
   const void *rsin;
   int64_t rcs;
+  // bounds of the tensor-core kernel's device waits (polls of a consumer wait,
+  // tries of a producer wait); withhold != 0 (PKV_DECODE_TEST_WAIT_TIMEOUT
+  // only): CTA 0's producer never publishes consumer warp 0's first element
+  uint32_t max_polls, max_tries;
+  int32_t withhold;
 };
 
 struct Unit {
@@ -416,10 +423,11 @@ struct GroupSync {
   uint64_t *bar;
   uint32_t phase;
   int32_t *status;
+  uint32_t max_polls;
   __device__ bool operator()() {
     __syncwarp();
     if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
-    const bool ok = mbar_wait_bounded(bar, phase & 1u);
+    const bool ok = mbar_wait_bounded(bar, phase & 1u, max_polls);
     ++phase;
     if (!ok) flag_status(status, PKV_DEV_WAIT_TIMEOUT);
     return ok;
@@ -807,7 +815,7 @@ decode_tc_kernel(DecodeArgs a) {
       const int32_t split_row = srow;
       // (1) the unit's block-table entries and query rows -> smem
       if (nunit >= QS) {
-        if (!mbar_wait_backoff(&qempty[qs], ((nunit / QS) - 1) & 1)) {
+        if (!mbar_wait_backoff(&qempty[qs], ((nunit / QS) - 1) & 1, a.max_tries)) {
           flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
           ok = false;
         }
@@ -843,9 +851,11 @@ decode_tc_kernel(DecodeArgs a) {
           const bool last = (j == rounds - 1);
           if (!has && !last) continue;
           const int32_t k = kcount++;
+          // test of the bounded waits: an element that is never published
+          if (a.withhold && k == 0 && lane == 0 && blockIdx.x == 0) continue;
           const int slot = lane * MD + (k % MD);
           const int32_t use = k / MD;
-          if (use > 0 && !mbar_wait_backoff(&empty[slot], (use - 1) & 1)) {
+          if (use > 0 && !mbar_wait_backoff(&empty[slot], (use - 1) & 1, a.max_tries)) {
             flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
             ok = false;
             return;
@@ -942,7 +952,7 @@ decode_tc_kernel(DecodeArgs a) {
       const int32_t k = kcount++;
       const int slot = lane * MD + (k % MD);
       const int32_t use = k / MD;
-      if (use > 0 && !mbar_wait_backoff(&empty[slot], (use - 1) & 1)) {
+      if (use > 0 && !mbar_wait_backoff(&empty[slot], (use - 1) & 1, a.max_tries)) {
         flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
       } else {
         SlotMeta md{};
@@ -961,7 +971,7 @@ decode_tc_kernel(DecodeArgs a) {
   const int cw = warp;
   // m16n8k16 fragment coordinates: lane = 4 * fr + fq
   const int fr = lane >> 2, fq = lane & 3;
-  GroupSync sync{group, 0u, a.status};
+  GroupSync sync{group, 0u, a.status, a.max_polls};
 
   // A page is processed transposed: S^T = K Q^T (the 16 tokens on M, up to 8
   // query heads per head tile on N) and O^T = V^T P^T (head_dim on M), so one
@@ -1014,7 +1024,7 @@ decode_tc_kernel(DecodeArgs a) {
   auto issue = [&](int32_t e) {
     if (e <= stop_at && alive) {
       const int ms = cw * MD + (e % MD);
-      if (!mbar_wait_bounded(&full[ms], (e / MD) & 1)) {
+      if (!mbar_wait_bounded(&full[ms], (e / MD) & 1, a.max_polls)) {
         flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
         alive = false;
       } else {
@@ -1087,7 +1097,7 @@ decode_tc_kernel(DecodeArgs a) {
     if (md.work != cur_work) {
       cur_work = md.work;
       cur_qslot = md.qslot;
-      if (!mbar_wait_bounded(&qfull[md.qslot], (uint32_t)md.pad)) {  // the unit's rows are staged
+      if (!mbar_wait_bounded(&qfull[md.qslot], (uint32_t)md.pad, a.max_polls)) {  // the unit's rows are staged
         flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
         cp_async_wait_all();
         return;
@@ -1668,6 +1678,15 @@ int decode_run_impl(const void *q, const void *kn, const void *vn, const void *k
   a.partials = reinterpret_cast<float *>(ws + w.partials);
   a.sched = reinterpret_cast<int32_t *>(ws + w.hdr) + 4;
   a.status = status;
+  a.max_polls = kMaxPolls;
+  a.max_tries = kMaxWaitTries;
+  if (flags & PKV_DECODE_TEST_WAIT_TIMEOUT) {
+    // a few thousand polls (well under a millisecond) instead of seconds, and
+    // one element withheld, so the launch ends by its wait limits
+    a.max_polls = kTestWaitPolls;
+    a.max_tries = kTestWaitPolls;
+    a.withhold = 1;
+  }
   const int64_t max_units = w.max_items * w.units_per_item;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const bool tc = tc_eligible(k_cache, v_cache, num_q_heads, num_kv_heads, head_dim, block_size,

@@ -76,9 +76,18 @@ enum {
                                      weights as a 16-bit head plus 16-bit
                                      remainder (~17 significant bits instead
                                      of 8); slower, closer to fp32           */
-    PKV_DECODE_OUT_Q_DTYPE = 4    /* out holds q's dtype (bf16 or fp16; fp32 q:
+    PKV_DECODE_OUT_Q_DTYPE = 4,   /* out holds q's dtype (bf16 or fp16; fp32 q:
                                      no change): each fp32 result rounded to
                                      nearest, as a cast of the fp32 output   */
+    PKV_DECODE_TEST_WAIT_TIMEOUT = 1 << 30 /* TEST ONLY (tensor-core kernel):
+                                     every device wait gives up after 4096
+                                     polls instead of seconds' worth, and the
+                                     first CTA's producer never publishes one
+                                     pipeline element, so waits run out: the
+                                     launch returns, ORs PKV_DEV_WAIT_TIMEOUT
+                                     into *status, and its output is
+                                     undefined. Exercises the timeout path;
+                                     never set it otherwise. */
 };
 
 /* Sampling flags. */
@@ -318,9 +327,12 @@ int pkv_rope_append_decode_run(const void *q, const void *k_new, const void *v_n
  * PKV_NOALLOC_SCRATCH_BYTES inside the library; every GPU that loads the
  * library's device code keeps that much memory for it until the process
  * exits. Decodes whose workspace (pkv_decode_workspace_size) exceeds it are
- * rejected with PKV_ERR_WORKSPACE. The first call on a device looks up the
- * array's device address (once per device, with that device current); make
- * that first call before any stream capture. All calls share the array:
+ * rejected with PKV_ERR_WORKSPACE. The first call in a CUDA context looks up
+ * the array's device address in that context (cudaGetSymbolAddress, with the
+ * caller's device and context current) and caches it under the context's
+ * unique id, so a context made with the driver API, or a primary context
+ * re-created after cudaDeviceReset, gets its own lookup. Make that first call
+ * before any stream capture. All calls share the array:
  * calls that run concurrently on the GPU race on it and must be serialised by
  * the caller. Arguments and results are those of pkv_decode.
  */

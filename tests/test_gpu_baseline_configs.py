@@ -1,0 +1,121 @@
+"""Kernel-level parity at the BASELINE configurations' own sizes.
+
+One decode step of one layer of configs 3, 4 and 5, through
+the public fused op ``paged_attention_decode(..., k_new=, v_new=)`` (C ABI
+pkv_append_decode_run) with the library's default split length, against the
+CPU oracle: the append restated from the reference's _paged_kv_update_kernel
+(src/triton_kernels/paged_kv.py:253-319) and the 3-pass decode of
+_paged_attention_decode_kernel (paged_kv.py:63-251).
+
+  config 3: 16 prompts x group 8 = 128 sequences; each group's 512-token prompt
+            lives in 32 pages shared by its 8 block tables (the refcounted
+            prompt pages of GRPO groups) followed by U{1..512} private tokens;
+  config 4: 1024 sequences, ctx U[1024, 8192], random page permutation;
+  config 5: Qwen2.5-7B heads (28 q / 4 kv), 64 sequences, ctx log-U[4096,
+            32768]; the default split length is shorter than the longest
+            sequences, so the split-K partials and the merge kernel run.
+
+Bars: cache bytes after the append bit-exact, decode
+output within max-abs 2e-2 (bf16, fp32 accumulate).
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import ATOL
+from grpo_training_engine_b200 import decode_kernel_kind, paged_attention_decode, plan_decode
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda")
+BS, D = 16, 128
+
+
+def _pool(seed: int, tables: list[list[int]], num_blocks: int, lens, hq: int, hkv: int):
+    """Device tensors of one layer: block tables (ids permuted by seed), caches,
+    q and the new K / V rows, all N(0,1) bf16."""
+    g = torch.Generator().manual_seed(seed)
+    perm = torch.randperm(num_blocks, generator=g)
+    B = len(tables)
+    max_blocks = max(len(t) for t in tables)
+    bt = torch.zeros(B, max_blocks, dtype=torch.int32)
+    for i, t in enumerate(tables):
+        bt[i, : len(t)] = perm[torch.tensor(t, dtype=torch.long)].int()
+    gd = torch.Generator(device=DEV).manual_seed(seed)
+    kc = torch.randn(num_blocks, hkv, BS, D, device=DEV, generator=gd).to(torch.bfloat16)
+    vc = torch.randn(num_blocks, hkv, BS, D, device=DEV, generator=gd).to(torch.bfloat16)
+    q = torch.randn(B, hq, D, device=DEV, generator=gd).to(torch.bfloat16)
+    kn = torch.randn(B, hkv, D, device=DEV, generator=gd).to(torch.bfloat16)
+    vn = torch.randn(B, hkv, D, device=DEV, generator=gd).to(torch.bfloat16)
+    ctx = torch.tensor([int(x) for x in lens], dtype=torch.int32)
+    return q, kc, vc, bt.to(DEV), ctx.to(DEV), kn, vn
+
+
+def _private_tables(lens) -> tuple[list[list[int]], int]:
+    tables, nxt = [], 0
+    for n in lens:
+        p = math.ceil(int(n) / BS)
+        tables.append(list(range(nxt, nxt + p)))
+        nxt += p
+    return tables, nxt
+
+
+def _step_vs_oracle(q, kc, vc, bt, ctx, kn, vn, expect_merge: bool | None = None):
+    """One fused append + decode step on the GPU and by the oracle on copies of
+    the same inputs; returns the max-abs decode error and the plan."""
+    assert decode_kernel_kind(q, kc) == "tensor_core"
+    kc_h, vc_h = kc.cpu(), vc.cpu()
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    plan = plan_decode(ctx, q.shape[1], kc.shape[1], D, BS, bt.shape[1], status=status)
+    if expect_merge is not None:
+        assert (bt.shape[1] > plan.pages_per_split) == expect_merge
+    out = paged_attention_decode(q, kc, vc, bt, ctx, plan=plan, k_new=kn, v_new=vn, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    bt_h, ctx_h = bt.cpu(), ctx.cpu()
+    oracle.append(kn.cpu(), vn.cpu(), kc_h, vc_h, bt_h, ctx_h - 1)
+    assert torch.equal(kc.cpu(), kc_h) and torch.equal(vc.cpu(), vc_h), "appended cache bytes differ"
+    ref = oracle.decode(q.cpu(), kc_h, vc_h, bt_h, ctx_h)
+    err = float((out.cpu() - ref).abs().max())
+    return err, plan
+
+
+def test_config3_grpo_groups_with_shared_prompt_pages_at_size():
+    rs = np.random.RandomState(31)
+    groups, group, prompt_pages = 16, 8, 512 // BS
+    lens = 512 + rs.randint(1, 513, size=groups * group)  # post-append lengths
+    tables, nxt = [], 0
+    for gi in range(groups):
+        shared = list(range(nxt, nxt + prompt_pages))
+        nxt += prompt_pages
+        for j in range(group):
+            own = math.ceil(int(lens[gi * group + j]) / BS) - prompt_pages
+            tables.append(shared + list(range(nxt, nxt + own)))
+            nxt += own
+    args = _pool(3, tables, nxt, lens, 12, 2)
+    bt = args[3].cpu()
+    # the 8 rows of a group really share their prompt pages
+    assert all(torch.equal(bt[g * group, :prompt_pages], bt[g * group + j, :prompt_pages])
+               for g in range(groups) for j in range(group))
+    err, _ = _step_vs_oracle(*args)
+    assert err <= ATOL["bfloat16"], err
+
+
+def test_config4_full_batch_one_layer_at_size():
+    lens = np.random.RandomState(41).randint(1024, 8193, size=1024)
+    tables, nb = _private_tables(lens)
+    err, _ = _step_vs_oracle(*_pool(4, tables, nb, lens, 12, 2), expect_merge=False)
+    assert err <= ATOL["bfloat16"], err
+
+
+def test_config5_qwen7b_long_context_split_k_at_size():
+    rs = np.random.RandomState(51)
+    lens = np.exp(rs.uniform(np.log(4096), np.log(32768), size=64)).astype(np.int64)
+    tables, nb = _private_tables(lens)
+    err, plan = _step_vs_oracle(*_pool(5, tables, nb, lens, 28, 4), expect_merge=True)
+    assert err <= ATOL["bfloat16"], (err, plan.pages_per_split)
