@@ -49,7 +49,10 @@ METRIC = "paged KV decode: KV-read HBM GB/s and seq-steps/s at 1/2/4/8 B200"
 # that config's geometry (dram__bytes_read.sum + dram__bytes_write.sum over the
 # launch's algorithmic bytes). Traffic grows with the pages read, so
 # roofline.traffic scales the ratio to the full launch.
-DECODE_DRAM_TRAFFIC_RATIO = {4: 1.0017}
+# config 3 counts every sequence's reads of its group's shared prompt pages in
+# its algorithmic bytes, but those pages come from L2 after the first reader:
+# its traffic is 1.012x the unique K/V bytes.
+DECODE_DRAM_TRAFFIC_RATIO = {3: 0.4254, 4: 1.0017, 5: 1.0023}
 UNIT = "seq-steps/s"
 
 

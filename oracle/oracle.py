@@ -14,7 +14,14 @@ What it restates (reference = src/triton_kernels/paged_kv.py):
   sample_top_p  -> _sample_tokens / _apply_top_p (:418-450): scaled logits in the
                    logits dtype, stable descending sort, running probability,
                    nucleus cut, then the draw for a given uniform by the inverse
-                   CDF of the kept tokens in index order (the CUDA op's draw).
+                   CDF of the kept tokens in index order (the CUDA op's draw);
+  nucleus       -> the kept-token mask of that rule alone, with the exact
+                   probabilities (pinned to the reference's own _apply_top_p
+                   by tests/golden/sampling_*.npz);
+  rmsnorm       -> the arithmetic of the reference's _rmsnorm_kernel
+                   (src/triton_kernels/fused_ops.py:34-77): fp32 sum of squares,
+                   x * rsqrt(mean + eps) rounded to bf16, times the weight,
+                   rounded to bf16 (pinned by tests/golden/rmsnorm_*.npz).
 The byte-moving functions work on raw-bit numpy views, so they are exact for
 every dtype. Parity of this oracle with the reference itself is pinned by
 tests/golden/ (fixtures produced by running the reference's own kernels).
@@ -194,6 +201,51 @@ def gather(k_cache, v_cache, block_tables, context_lens, max_tokens=None):
 
 if __name__ == "__main__":  # pragma: no cover
     print(build(force=True), max_threads(), os.cpu_count())
+
+
+def nucleus(logits, temperature: float, top_p: float):
+    """Exact-rule nucleus of each row: (kept bool [B, V], scaled float64 [B, V],
+    p float64 [B, V]). scaled = logits / max(T, 1e-6) rounded to the logits dtype
+    (paged_kv.py:446); p = softmax(scaled) in float64; in descending order with
+    ties in index order, a token is kept while the running probability including
+    it is <= top_p (paged_kv.py:426-429), the first always (:428); top_p >= 1
+    keeps every token."""
+    lg = _cpu(logits)
+    scaled = (lg.float() / max(float(temperature), 1e-6)).to(lg.dtype).double().numpy()
+    B, V = scaled.shape
+    kept = np.ones((B, V), dtype=bool)
+    p = np.exp(scaled - scaled.max(axis=1, keepdims=True))
+    p /= p.sum(axis=1, keepdims=True)
+    if top_p < 1.0:
+        for b in range(B):
+            order = np.argsort(-scaled[b], kind="stable")
+            keep_sorted = np.cumsum(p[b, order]) <= top_p
+            keep_sorted[0] = True
+            kept[b] = False
+            kept[b, order[keep_sorted]] = True
+    return kept, scaled, p
+
+
+def rmsnorm(x, weight, eps: float, cast_rounding: str = "rne") -> torch.Tensor:
+    """bf16 [rows, hidden]: the reference _rmsnorm_kernel's arithmetic in numpy
+    (fused_ops.py:48-77): s = sum of fp32 squares, inv = 1 / sqrt(s / n + eps) in
+    fp32, normed = bf16(x * inv), y = bf16(normed * w). cast_rounding is the
+    rounding of the kernel's fp32 -> bf16 cast of `normed` (:73): "rne" (to
+    nearest even, compiled Triton's default on the GPU) or "rtz" (toward zero,
+    what Triton's CPU interpreter does)."""
+    xf = _cpu(x).float().numpy()
+    wf = _cpu(weight).float().numpy()
+    n = np.float32(xf.shape[1])
+    s = (xf * xf).sum(axis=1, dtype=np.float32)
+    inv = (np.float32(1.0) / np.sqrt(s / n + np.float32(eps))).astype(np.float32)
+    prod = (xf * inv[:, None]).astype(np.float32)
+    if cast_rounding == "rtz":
+        normed = torch.from_numpy((prod.view(np.int32) & np.int32(~0xFFFF)).view(np.float32))
+    elif cast_rounding == "rne":
+        normed = torch.from_numpy(prod).to(torch.bfloat16).float()
+    else:
+        raise ValueError(f"cast_rounding must be 'rne' or 'rtz', got {cast_rounding!r}")
+    return (normed * torch.from_numpy(wf)).to(torch.bfloat16)
 
 
 def sample_top_p(logits, temperature: float, top_p: float, uniforms):

@@ -82,3 +82,53 @@ def to_torch(inp: dict[str, np.ndarray], dtype: str, device="cpu") -> dict:
             t = t.to(dt)
         res[key] = t.to(device)
     return res
+
+
+# ---------------------------------------------------------------- sampling nucleus
+# Rows of logits for the reference's _apply_top_p (src/triton_kernels/paged_kv.py:418-434),
+# applied as _sample_tokens applies it (paged_kv.py:437-450): scaled = logits / max(T, 1e-6)
+# in the logits dtype. kind: "normal" N(0,1) * scale; "coarse": rounded to multiples of
+# `step` (many equal values, ties at the cut); "peaked": one dominant token.
+SAMPLING_CASES = [
+    dict(name="f32_v1000", seed=21, rows=6, vocab=1000, dtype="float32", kind="normal", scale=3.0),
+    dict(name="bf16_v1000", seed=22, rows=6, vocab=1000, dtype="bfloat16", kind="normal", scale=3.0),
+    dict(name="f16_v1000", seed=23, rows=4, vocab=1000, dtype="float16", kind="normal", scale=3.0),
+    dict(name="bf16_coarse_v5000", seed=24, rows=4, vocab=5000, dtype="bfloat16", kind="coarse", scale=2.0,
+         step=0.5),
+    dict(name="bf16_peaked_v3000", seed=25, rows=3, vocab=3000, dtype="bfloat16", kind="peaked", scale=1.0),
+    dict(name="bf16_v151936", seed=26, rows=2, vocab=151936, dtype="bfloat16", kind="normal", scale=3.0),
+]
+# (temperature, top_p) pairs applied to every row
+SAMPLING_PARAMS = [(0.7, 0.9), (1.0, 0.5), (0.5, 0.95), (1.3, 0.3)]
+
+
+def make_sampling_logits(case: dict) -> np.ndarray:
+    """fp32 [rows, vocab]; the tests and the generator cast it to case["dtype"]."""
+    rs = np.random.RandomState(case["seed"])
+    x = rs.standard_normal((case["rows"], case["vocab"])).astype(np.float32) * np.float32(case["scale"])
+    if case["kind"] == "coarse":
+        x = (np.round(x / case["step"]) * case["step"]).astype(np.float32)
+    elif case["kind"] == "peaked":
+        hot = rs.randint(0, case["vocab"], size=case["rows"])
+        x[np.arange(case["rows"]), hot] += np.float32(12.0)
+    return x
+
+
+# ---------------------------------------------------------------- RMSNorm
+# Rows for the reference's fused_rmsnorm (src/triton_kernels/fused_ops.py:118-148, kernel
+# :34-77), bf16 x [rows, hidden] and weight [hidden], eps 1e-6: the hidden sizes of the
+# 1.5B (1536) and 7B (3584) geometries and a short odd-sized row.
+RMSNORM_CASES = [
+    dict(name="rmsnorm_1536", seed=31, rows=16, hidden=1536, eps=1e-6),
+    dict(name="rmsnorm_3584", seed=32, rows=8, hidden=3584, eps=1e-6),
+    dict(name="rmsnorm_104", seed=33, rows=8, hidden=104, eps=1e-6),
+]
+
+
+def make_rmsnorm_inputs(case: dict) -> dict[str, np.ndarray]:
+    rs = np.random.RandomState(case["seed"])
+    rows, hidden = case["rows"], case["hidden"]
+    x = rs.standard_normal((rows, hidden)).astype(np.float32) * np.float32(3.0)
+    x[rows // 2:] *= np.float32(40.0)  # large activations too
+    w = (np.float32(1.0) + np.float32(0.1) * rs.standard_normal(hidden)).astype(np.float32)
+    return {"x": x, "weight": w}

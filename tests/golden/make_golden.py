@@ -19,6 +19,17 @@ Inputs are drawn from numpy's legacy RandomState (a stream frozen across
 numpy versions) so the tests regenerate them from the seed; each fixture
 stores a SHA-256 of its inputs to catch any drift, the reference outputs,
 and SHA-256 digests of the caches after the reference's appends.
+
+Two more parts pin the steps around the decode in the rollout step:
+  sampling: the reference's _apply_top_p (paged_kv.py:418-434) on rows of
+            logits scaled as _sample_tokens scales them (paged_kv.py:437-450),
+            for every (temperature, top_p) of cases.SAMPLING_PARAMS; the
+            fixture stores the kept-token masks (sampling_<case>.npz);
+  rmsnorm:  the reference's fused_rmsnorm (fused_ops.py:118-148, Triton kernel
+            :34-77, under the interpreter) on bf16 rows; the fixture stores the
+            output bits (rmsnorm_<case>.npz).
+
+    python tests/golden/make_golden.py <reference checkout> [--only decode,sampling,rmsnorm]
 """
 
 from __future__ import annotations
@@ -43,13 +54,62 @@ def _sha(*arrays: np.ndarray) -> str:
     return h.hexdigest()
 
 
-def main(ref_root: str) -> None:
+def sampling_fixtures(ref, torch) -> None:
+    for case in cases.SAMPLING_CASES:
+        logits = torch.from_numpy(cases.make_sampling_logits(case)).to(getattr(torch, case["dtype"]))
+        masks = []
+        for temperature, top_p in cases.SAMPLING_PARAMS:
+            scaled = logits / max(temperature, 1e-6)  # _sample_tokens (paged_kv.py:446)
+            kept = torch.isfinite(ref._apply_top_p(scaled, top_p))
+            masks.append(np.packbits(kept.numpy(), axis=-1))
+        meta = {
+            "case": case["name"],
+            "params": cases.SAMPLING_PARAMS,
+            "logits_sha": _sha(cases.make_sampling_logits(case)),
+            "generator": "reference _apply_top_p (torch, CPU) on logits / max(T, 1e-6)",
+        }
+        np.savez_compressed(HERE / f"sampling_{case['name']}.npz", kept=np.stack(masks), meta=json.dumps(meta))
+        print("sampling", case["name"], [int(np.unpackbits(m, axis=-1).sum()) for m in masks])
+
+
+def rmsnorm_fixtures(torch) -> None:
+    from src.triton_kernels import fused_ops  # the reference module
+
+    # The rollout step runs the kernel on bf16 rows and a bf16 weight. Triton
+    # 3.6's interpreter multiplies two bf16 operands wrongly (the kernel's
+    # `normed * w`, fused_ops.py:74, comes out as garbage; a bf16 x fp32 product
+    # is right), so the kernel is run on fp32 tensors that hold the bf16 values:
+    # every step is the same (the loads are cast to fp32 anyway, `normed` is
+    # still rounded to bf16 by the kernel's own cast, :73), and the product of
+    # two bf16 values is exact in fp32, so rounding the fp32 output to bf16 gives
+    # the bf16 kernel's result (a bf16 product correctly rounded).
+    for case in cases.RMSNORM_CASES:
+        inp = cases.make_rmsnorm_inputs(case)
+        x = torch.from_numpy(inp["x"]).to(torch.bfloat16).float()
+        w = torch.from_numpy(inp["weight"]).to(torch.bfloat16).float()
+        y = fused_ops.fused_rmsnorm(x[:, None, :], w, case["eps"])[:, 0, :].to(torch.bfloat16)
+        meta = {
+            "case": case["name"],
+            "inputs_sha": cases.inputs_sha(inp),
+            "generator": "reference fused_rmsnorm (Triton kernel under TRITON_INTERPRET=1) on fp32 tensors "
+                         "holding the bf16 values, output rounded to bf16",
+        }
+        np.savez_compressed(HERE / f"{case['name']}.npz", out=y.contiguous().view(torch.int16).numpy(),
+                            meta=json.dumps(meta))
+        print(case["name"], tuple(y.shape))
+
+
+def main(ref_root: str, parts=("decode", "sampling", "rmsnorm")) -> None:
     os.environ["TRITON_INTERPRET"] = "1"
     sys.path.insert(0, ref_root)
     import torch
     from src.triton_kernels import paged_kv as ref  # the reference module
 
-    for case in cases.CASES:
+    if "sampling" in parts:
+        sampling_fixtures(ref, torch)
+    if "rmsnorm" in parts:
+        rmsnorm_fixtures(torch)
+    for case in (cases.CASES if "decode" in parts else []):
         inp = cases.make_inputs(case)
         t = cases.to_torch(inp, case["dtype"])
         G = case["hq"] // case["hkv"]
@@ -125,6 +185,12 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        sys.exit("usage: python tests/golden/make_golden.py <reference checkout>")
-    main(sys.argv[1])
+    args = sys.argv[1:]
+    parts = ("decode", "sampling", "rmsnorm")
+    if "--only" in args:
+        i = args.index("--only")
+        parts = tuple(args[i + 1].split(","))
+        del args[i:i + 2]
+    if len(args) != 1:
+        sys.exit("usage: python tests/golden/make_golden.py <reference checkout> [--only decode,sampling,rmsnorm]")
+    main(args[0], parts)

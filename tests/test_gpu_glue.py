@@ -80,3 +80,32 @@ def test_glue_rejects_unaligned_rows():
     x = torch.randn(4, 100, device=DEV).to(torch.bfloat16)  # 200-byte rows
     with pytest.raises(RuntimeError):
         ops.add_rmsnorm(x, torch.ones(100, device=DEV, dtype=torch.bfloat16), 1e-6)
+
+
+@pytest.mark.parametrize("name", ["rmsnorm_1536", "rmsnorm_3584", "rmsnorm_104"])
+def test_add_rmsnorm_matches_the_reference_rmsnorm_kernel(name):
+    """pkv_add_rmsnorm without a residual against the reference's fused_rmsnorm
+    (src/triton_kernels/fused_ops.py:34-77, the norm its rollout step calls,
+    paged_kv.py:706-710): the fixture (the reference kernel run by
+    tests/golden/make_golden.py) is reproduced bit for bit by oracle.rmsnorm with
+    the interpreter's truncating cast; with the GPU's nearest-even cast the
+    oracle is the reference's arithmetic, and the kernel must match it except
+    where the sum of squares, accumulated in another order, moves a product
+    across a rounding boundary (at most one bf16 step, on few elements)."""
+    import cases
+    from conftest import load_golden
+    from oracle import oracle
+
+    case = next(c for c in cases.RMSNORM_CASES if c["name"] == name)
+    ref_bits, _ = load_golden(name)
+    inp = cases.make_rmsnorm_inputs(case)
+    x = torch.from_numpy(inp["x"]).to(torch.bfloat16)
+    w = torch.from_numpy(inp["weight"]).to(torch.bfloat16)
+    assert torch.equal(oracle.rmsnorm(x, w, case["eps"], cast_rounding="rtz"),
+                       torch.from_numpy(ref_bits).view(torch.bfloat16))
+    want = oracle.rmsnorm(x, w, case["eps"])
+    out, _ = ops.add_rmsnorm(x.to(DEV), w.to(DEV), case["eps"])
+    out = out.cpu()
+    diff = (out.float() - want.float()).abs()
+    assert bool((diff <= want.float().abs() * 2.0 ** -7 + 1e-30).all())
+    assert float((out != want).float().mean()) < 0.01

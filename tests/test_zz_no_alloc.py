@@ -98,7 +98,7 @@ def test_no_alloc_matches_workspace_entry_point_on_two_calls(force_generic):
 
 def test_no_alloc_fp32_small_case_twice():
     args = _case(3, 4, 12, 2, 128, 16, [37, 128, 300, 511], torch.float32)
-    ref = _with_workspace(*args)
+    ref = _with_workspace(*args, pages_per_split=4)
     want = oracle.decode(*[t.cpu() for t in args])
     for _ in range(2):
         got = _no_alloc(*args, pages_per_split=4)
