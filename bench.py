@@ -338,7 +338,8 @@ def run_ours(args, rank, world, local):
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    wl = Workload(args.config, rank, world, args.layers, device, args.seqs, strong=args.scaling == "strong")
+    shard_world = args.shard_of or world  # --shard-of N: rank 0's shard of an N-GPU job, on this GPU alone
+    wl = Workload(args.config, rank, shard_world, args.layers, device, args.seqs, strong=args.scaling == "strong")
     L, B = wl.layers, wl.B
     stream = torch.cuda.current_stream(device)
 
@@ -429,7 +430,8 @@ def run_ours(args, rank, world, local):
     peak, peak_kind = measured_peaks()
     dec_bytes = wl.decode_bytes_layer() + (0 if args.separate_append else wl.append_bytes_layer())
     achieved = dec_bytes / (decode_avg_ms / 1e3) / 1e9
-    merges = 1 if wl.max_blocks > plan_pps(wl, args) else 0  # split-K merge launch per layer
+    chosen_pps = plan_pps(wl, args)  # the split length the plan kernel picked
+    merges = 1 if wl.max_blocks > split_floor(wl, args) else 0  # split-K merge launch per layer
     traffic_ratio = DECODE_DRAM_TRAFFIC_RATIO.get(wl.config)
     launches = args.steps * (1 + ((2 if args.separate_append else 1) + merges) * L)
 
@@ -458,8 +460,9 @@ def run_ours(args, rank, world, local):
             "dtype": "bf16",
             "data": "synthetic: seeded N(0,1) q/K/V/new tokens, seeded context lengths and random page permutations",
             "config": workload_config(args, world),
+            "shard_of": args.shard_of or None,
             "run": {
-                "pages_per_split": plan_pps(wl, args),
+                "pages_per_split": chosen_pps,
                 "step": ("1 plan per step, then per layer one launch that appends the token and decodes"
                          if not args.separate_append else "1 plan per step, then per layer append + decode launches"),
                 "launch": (f"the {args.steps} timed steps captured as one CUDA graph, replayed once (after "
@@ -514,10 +517,24 @@ def capture_steps(fn):
 
 
 def plan_pps(wl, args) -> int:
+    """Split length the plan kernel chose for this workload (read back from a plan)."""
+    from grpo_training_engine_b200 import ops
+
+    return ops.plan_decode(wl.ctx, wl.hq, wl.hkv, wl.d, wl.bs, wl.max_blocks,
+                           pages_per_split=args.pages_per_split).chosen_pages_per_split()
+
+
+def split_floor(wl, args) -> int:
+    """Shortest split the plan may choose: the merge launch runs whenever a
+    sequence can be longer than that (the workspace is sized for it)."""
     from grpo_training_engine_b200 import _lib
 
-    return int(_lib.load().pkv_decode_pages_per_split(wl.B, wl.hq, wl.hkv, wl.d, wl.max_blocks,
-                                                      args.pages_per_split))
+    lib = _lib.load()
+    ws = lib.pkv_decode_workspace_size(wl.B, wl.hq, wl.hkv, wl.d, wl.max_blocks, args.pages_per_split)
+    for p in range(8, 513, 8):  # the smallest length whose workspace equals the library's
+        if lib.pkv_decode_workspace_size(wl.B, wl.hq, wl.hkv, wl.d, wl.max_blocks, p) == ws:
+            return p
+    return int(lib.pkv_decode_pages_per_split(wl.B, wl.hq, wl.hkv, wl.d, wl.max_blocks, args.pages_per_split))
 
 
 def run_e2e(args, wl, world, device):
@@ -919,6 +936,9 @@ def main():
     ap.add_argument("--layers", type=int, default=None, help="override the layer count (diagnostics only)")
     ap.add_argument("--seqs", type=int, default=None,
                     help="override the sequence count (in all with strong scaling, per GPU with weak; diagnostics)")
+    ap.add_argument("--shard-of", type=int, default=0,
+                    help="diagnostics on one GPU: run rank 0's shard of an N-GPU job (the JSON line then "
+                         "describes that shard, not a whole job)")
     ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
                     help="strong: the config's sequences split over the GPUs (BASELINE's statement of the configs); "
                          "weak: every GPU gets the config's full sequence count")

@@ -57,12 +57,19 @@ constexpr int kBtRegs = 16;
 constexpr int32_t kMaxPagesPerSplit = kBtRegs * 32;
 // wait bound of every device wait under PKV_DECODE_TEST_WAIT_TIMEOUT
 constexpr uint32_t kTestWaitPolls = 4096;
+// Split-length cost model, in pages' worth of one CTA's streaming: the fixed
+// cost of a unit (cross-warp combine and pipeline refill, measured on B200 at
+// about 16 pages) and of merging split partials (the last split of a sequence
+// reads the others' partials back from L2 and writes the output).
+constexpr int64_t kUnitCost = 16, kMergeCost = 8;
+// Candidate split lengths the plan kernel weighs (multiples of 8 pages).
+constexpr int kMaxSplitCandidates = 64;
 
 // ---------------------------------------------------------------------------
 // workspace layout
 // ---------------------------------------------------------------------------
 struct WsLayout {
-  size_t hdr, seq_off, seq_nsplit, items, partials, total;
+  size_t hdr, seq_off, seq_nsplit, merge_cnt, items, partials, total;
   int64_t max_items;
   int32_t units_per_item;  // num_kv_heads * head_groups
   int32_t group_rows;      // query heads per head group (partial row count)
@@ -93,6 +100,7 @@ WsLayout ws_layout(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t max_bl
   w.hdr = off; off += 256;
   w.seq_off = off; off = align_up(off + sizeof(int32_t) * (size_t)B, 256);
   w.seq_nsplit = off; off = align_up(off + sizeof(int32_t) * (size_t)B, 256);
+  w.merge_cnt = off; off = align_up(off + sizeof(int32_t) * (size_t)B * w.units_per_item, 256);
   w.items = off; off = align_up(off + sizeof(int4) * (size_t)w.max_items, 256);
   w.partials = off;
   off = align_up(off + sizeof(float) * (size_t)w.max_items * w.units_per_item * w.part_floats, 256);
@@ -110,6 +118,8 @@ struct DecodeArgs {
   float *out;
   const void *kc;
   const void *vc;
+  // P: the longest split the plan may choose (shared-memory sizing); the
+  // plan's choice is hdr[1], which the kernels read
   int32_t B, Hq, Hkv, G, GR, HG, D, bs, num_blocks, max_blocks, P, upi, part_o, part_floats;
   int32_t q_dtype, kv_dtype;
   int32_t q_vec;    // q rows are 16-byte aligned and contiguous in head_dim
@@ -126,6 +136,9 @@ struct DecodeArgs {
   const int4 *items;  // per item {b, split, clamped ctx, splits of b}
   int64_t max_items;  // entries the item array holds (the plan fills the first total / upi)
   float *partials;
+  // splits of (sequence b, unit r) that finished, at b * upi + r: the last one
+  // merges (tensor-core kernel); zeroed by the plan, reset by the merging unit
+  int32_t *merge_cnt;
   int32_t *status;
   int32_t *sched;  // {next tail unit, CTAs done claiming}: the dynamic tail of the schedule
   // fused append (tensor-core kernel): the new token of sequence b, written at
@@ -175,8 +188,9 @@ __device__ __forceinline__ void store_out4(const DecodeArgs &a, int64_t idx, flo
   }
 }
 
-// Work unit w = (item, kv head, head group); the item descriptor comes from the plan.
-__device__ __forceinline__ Unit unit_from(const DecodeArgs &a, int32_t w, int4 it) {
+// Work unit w = (item, kv head, head group); the item descriptor comes from the
+// plan, P is the plan's split length.
+__device__ __forceinline__ Unit unit_from(const DecodeArgs &a, int32_t P, int32_t w, int4 it) {
   Unit u;
   const int32_t item = w / a.upi;
   const int32_t r = w - item * a.upi;
@@ -187,8 +201,8 @@ __device__ __forceinline__ Unit unit_from(const DecodeArgs &a, int32_t w, int4 i
   u.ctx = it.z;
   u.nsplit = it.w;
   const int32_t npages = (u.ctx + a.bs - 1) / a.bs;
-  u.p_begin = u.s * a.P;
-  u.p_end = min(u.p_begin + a.P, npages);
+  u.p_begin = u.s * P;
+  u.p_end = min(u.p_begin + P, npages);
   if (u.p_end < u.p_begin) u.p_end = u.p_begin;
   const int32_t g0 = u.hg * a.GR;
   u.gcount = min(a.GR, a.G - g0);
@@ -196,8 +210,8 @@ __device__ __forceinline__ Unit unit_from(const DecodeArgs &a, int32_t w, int4 i
   return u;
 }
 
-__device__ __forceinline__ Unit decode_unit(const DecodeArgs &a, int32_t w) {
-  return unit_from(a, w, a.items[w / a.upi]);
+__device__ __forceinline__ Unit decode_unit(const DecodeArgs &a, int32_t P, int32_t w) {
+  return unit_from(a, P, w, a.items[w / a.upi]);
 }
 
 // ---------------------------------------------------------------------------
@@ -257,14 +271,122 @@ __device__ __forceinline__ SeqSplits seq_splits(const int32_t *ctx, int32_t b, i
   return r;
 }
 
+// Split length for these lengths: P in {p_lo, p_lo + 8, ..., p_hi}, the one
+// whose launch the tensor-core kernel's schedule finishes first. Each of
+// kSimWarps warps takes candidates in turn and simulates the schedule exactly:
+// items are the full P-page splits, then the partial last splits by decreasing
+// length (the order this kernel writes), each expanded to upi units; CTA c of
+// `slots` takes unit c in round 0, 2 slots - 1 - c in round 1, and so on (the
+// snake). A CTA's time is its units' pages plus kUnitCost per unit; the launch
+// takes the largest CTA time, plus kMergeCost when some sequence is split.
+// Ties go to the longer split. B <= kMaxSimSeqs (the host enables this only
+// for fewer (sequence, kv head, head group) units than SMs). Whole block.
+constexpr int kSimWarps = 16;
+constexpr int kMaxSimSeqs = 160;
+
+__device__ int32_t choose_split(const int32_t *__restrict__ ctx, int32_t B, int32_t bs, int32_t cap,
+                                int32_t p_lo, int32_t p_hi, int32_t upi, int32_t slots) {
+  __shared__ int32_t s_pages[kMaxSimSeqs];
+  __shared__ int32_t s_rest[kSimWarps][kMaxSimSeqs];    // partial length per sequence (-1: none)
+  __shared__ int32_t s_sorted[kSimWarps][kMaxSimSeqs];  // partial lengths, longest first
+  __shared__ long long s_cost[kMaxSplitCandidates];
+  __shared__ int32_t s_maxp, s_choice;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int32_t ncand = min(kMaxSplitCandidates, (p_hi - p_lo) / 8 + 1);
+  if (tid == 0) s_maxp = 0;
+  __syncthreads();
+  if (tid < B) {
+    const int32_t c = min(max(ctx[tid], 0), cap);
+    s_pages[tid] = (c + bs - 1) / bs;
+    atomicMax(&s_maxp, s_pages[tid]);
+  }
+  __syncthreads();
+  const int32_t maxp = s_maxp;
+  if (warp < kSimWarps) {
+    int32_t *rest = s_rest[warp];
+    int32_t *sorted = s_sorted[warp];
+    for (int32_t k = warp; k < ncand; k += kSimWarps) {
+      const int32_t P = p_lo + 8 * k;
+      int32_t full = 0, parts = 0;
+      for (int32_t b = lane; b < B; b += 32) {
+        const int32_t pg = s_pages[b];
+        const int32_t f = pg / P, n = pg > 0 ? (pg + P - 1) / P : 1;
+        full += f;
+        parts += n > f ? 1 : 0;
+        rest[b] = n > f ? pg - f * P : -1;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        full += __shfl_xor_sync(0xffffffffu, full, o);
+        parts += __shfl_xor_sync(0xffffffffu, parts, o);
+      }
+      __syncwarp();
+      // rank of each partial split among the partials: longer first, ties by index
+      for (int32_t b = lane; b < B; b += 32) {
+        const int32_t r = rest[b];
+        if (r < 0) continue;
+        int32_t rank = 0;
+        for (int32_t j = 0; j < B; ++j) {
+          const int32_t x = rest[j];
+          rank += (x > r || (x == r && j < b)) ? 1 : 0;
+        }
+        sorted[rank] = r;
+      }
+      __syncwarp();
+      const int64_t units = (int64_t)upi * (full + parts);
+      const int64_t rounds = (units + slots - 1) / slots;
+      long long worst = 0;
+      for (int32_t c = lane; c < slots; c += 32) {
+        long long load = 0;
+        for (int64_t r = 0; r < rounds; ++r) {
+          const int64_t w = r * slots + ((r & 1) ? slots - 1 - c : c);
+          if (w >= units) continue;
+          const int64_t item = w / upi;
+          load += (item < full ? P : sorted[item - full]) + kUnitCost;
+        }
+        worst = max(worst, load);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) worst = max(worst, __shfl_xor_sync(0xffffffffu, worst, o));
+      if (lane == 0) s_cost[k] = worst + (maxp > P ? kMergeCost : 0);
+      __syncwarp();  // rest / sorted are rewritten for the next candidate
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    long long best = LLONG_MAX;
+    int32_t bestP = p_hi;
+    for (int32_t k = lane; k < ncand; k += 32) {
+      const int32_t Pc = p_lo + 8 * k;
+      if (s_cost[k] < best || (s_cost[k] == best && Pc > bestP)) {
+        best = s_cost[k];
+        bestP = Pc;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const long long ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int32_t op = __shfl_xor_sync(0xffffffffu, bestP, o);
+      if (ob < best || (ob == best && op > bestP)) {
+        best = ob;
+        bestP = op;
+      }
+    }
+    if (lane == 0) s_choice = bestP;
+  }
+  __syncthreads();
+  return s_choice;
+}
+
 // Items are ordered for the tensor-core kernel's snake schedule: every full P-page split first
 // (sequence order), then the partial last splits by decreasing length, so the
 // units left for the end of a launch are the shortest. Partial-result slots do
-// not depend on this order (they are indexed by seq_off[b] + split).
+// not depend on this order (they are indexed by seq_off[b] + split). P is p_hi,
+// or, when p_lo < p_hi, chosen from the lengths (choose_split); hdr[1] records it.
 __global__ void __launch_bounds__(kPlanThreads)
-plan_kernel(const int32_t *__restrict__ ctx, int32_t B, int32_t bs, int32_t max_blocks, int32_t P,
-            int32_t upi, int32_t *hdr, int32_t *seq_off, int32_t *seq_nsplit, int4 *items,
-            int32_t *status) {
+plan_kernel(const int32_t *__restrict__ ctx, int32_t B, int32_t bs, int32_t max_blocks, int32_t p_lo,
+            int32_t p_hi, int32_t slots, int32_t upi, int32_t *hdr, int32_t *seq_off,
+            int32_t *seq_nsplit, int32_t *merge_cnt, int4 *items, int32_t *status) {
   __shared__ int32_t warp_tot[kPlanThreads / 32];
   __shared__ int32_t bucket[kMaxPagesPerSplit + 1];  // partial splits per length, then cursors
   __shared__ int32_t carry_all, carry_full;
@@ -272,10 +394,13 @@ plan_kernel(const int32_t *__restrict__ ctx, int32_t B, int32_t bs, int32_t max_
   // for this grid before reading the plan)
   asm volatile("griddepcontrol.launch_dependents;");
   const int tid = threadIdx.x;
+  const int32_t cap = max_blocks * bs;
+  const int32_t P = (p_lo < p_hi && B <= kMaxSimSeqs) ? choose_split(ctx, B, bs, cap, p_lo, p_hi, upi, slots)
+                                                        : p_hi;
   for (int i = tid; i <= P; i += kPlanThreads) bucket[i] = 0;
+  for (int64_t i = tid; i < (int64_t)B * upi; i += kPlanThreads) merge_cnt[i] = 0;
   if (tid == 0) carry_all = carry_full = 0;
   __syncthreads();
-  const int32_t cap = max_blocks * bs;
   // pass 1: per-sequence offsets, full-split count, histogram of partial lengths
   for (int32_t base = 0; base < B; base += kPlanThreads) {
     const int32_t b = base + tid;
@@ -451,10 +576,11 @@ decode_generic_kernel(DecodeArgs a) {
   const KT *kc = reinterpret_cast<const KT *>(a.kc);
   const KT *vc = reinterpret_cast<const KT *>(a.vc);
   const int32_t total = a.hdr[0];
+  const int32_t P = a.hdr[1];
   CtaSync sync;
 
   for (int32_t w = blockIdx.x; w < total; w += gridDim.x) {
-    const Unit u = decode_unit(a, w);
+    const Unit u = decode_unit(a, P, w);
     const int32_t split_row = u.nsplit > 1 ? a.seq_off[u.b] + u.s : 0;  // used at the end
     for (int i = tid; i < GM * DP; i += kGenThreads) {
       const int g = i / DP, d = i - g * DP;
@@ -595,8 +721,9 @@ struct TcSmem {
   static constexpr size_t kQEmpty = kEmpty + 8 * NW * MD;
   static constexpr size_t kQFull = kQEmpty + 8 * QS;
   static constexpr size_t kGroup = kQFull + 8 * QS;
-  static constexpr size_t kXSlot = kGroup + 8;  // [NW] slot holding each warp's exchange rows
-  static constexpr size_t kXm = align_up(kXSlot + 4 * NW, 16);
+  // [NW] slot holding each warp's exchange rows, then the merge flag
+  static constexpr size_t kXSlot = kGroup + 8;
+  static constexpr size_t kXm = align_up(kXSlot + 4 * (NW + 1), 16);
   static constexpr size_t kXl = kXm + sizeof(float) * NW * kTcRows;
   static constexpr size_t kBt = kXl + sizeof(float) * NW * kTcRows;
   static size_t bytes(int32_t P) { return kBt + sizeof(int32_t) * (size_t)P + 1024; }
@@ -707,6 +834,7 @@ decode_tc_kernel(DecodeArgs a) {
   const int32_t total = a.hdr[0];
 
   if (warp == NW) {
+    const int32_t P = a.hdr[1];  // the plan's split length
     // =========================== producer warp ===========================
     // Schedule: the plan numbers units longest first. CTA c takes unit c in
     // round 0, 2G-1-c in round 1, 2G+c in round 2, ... (G = gridDim.x, "snake"
@@ -737,7 +865,7 @@ decode_tc_kernel(DecodeArgs a) {
     constexpr int kQVec = kTcRows * D * 2 / 16;  // 16-byte vectors of a query block
     constexpr int kQPerLane = (kQVec + 31) / 32;
     auto load_next = [&](int32_t w, int4 d) {
-      Unit u = unit_from(a, w, d);
+      Unit u = unit_from(a, P, w, d);
       const int32_t np = u.p_end - u.p_begin;
       srow = (w < total && u.nsplit > 1) ? a.seq_off[u.b] + u.s : 0;
       if (a.kn != nullptr && w < total && u.s == u.nsplit - 1 && u.ctx > 0 && lane < 2 * kRowChunks) {
@@ -809,7 +937,7 @@ decode_tc_kernel(DecodeArgs a) {
     bool ok = true;
     int32_t nunit = 0;  // units issued by this CTA (query slot = nunit % QS)
     while (w1 < total && ok) {
-      const Unit u = unit_from(a, w1, d1);
+      const Unit u = unit_from(a, P, w1, d1);
       const int32_t npages = u.p_end - u.p_begin;
       const int qs = nunit % QS;
       const int32_t split_row = srow;
@@ -1268,10 +1396,10 @@ decode_tc_kernel(DecodeArgs a) {
       // thread t owns query row g = t / (D/4) and columns 4c..4c+3, c = t % (D/4),
       // so the exchange reads and the output stores are 16 bytes wide and a
       // row's scale factors are computed once per thread for four columns
+      constexpr int kC4 = D / 4;
+      constexpr int kRowsPerPass = NW * 32 / kC4;
+      const int c4 = tid % kC4;
       {
-        constexpr int kC4 = D / 4;
-        constexpr int kRowsPerPass = NW * 32 / kC4;
-        const int c4 = tid % kC4;
         const float *xw[NW];  // each warp's exchange rows
 #pragma unroll
         for (int w = 0; w < NW; ++w)
@@ -1306,7 +1434,7 @@ decode_tc_kernel(DecodeArgs a) {
               store_out(a, op + (4 * c4 + 2) * a.o2, r.z);
               store_out(a, op + (4 * c4 + 3) * a.o2, r.w);
             }
-          } else {  // merged by merge_kernel after the launch
+          } else {  // one split of several: merged by the last split to finish
             float *part = a.partials +
                           ((int64_t)md.split_row * a.upi + u.kvh * a.HG + u.hg) * a.part_floats;
             *reinterpret_cast<float4 *>(part + a.part_o + g * D + 4 * c4) = O;
@@ -1317,6 +1445,8 @@ decode_tc_kernel(DecodeArgs a) {
           }
         }
       }
+      // the partial is visible to every CTA before this unit counts itself in
+      if (u.nsplit > 1) __threadfence();
       if (!sync()) {
         cp_async_wait_all();
         return;
@@ -1324,6 +1454,58 @@ decode_tc_kernel(DecodeArgs a) {
       // every consumer warp has read the unit's query rows and all exchange
       // rows: the query slot may be refilled
       if (tid == 0) mbar_arrive(&qempty[md.qslot]);
+      if (u.nsplit > 1) {
+        // ---- split-K merge by the last of the sequence's splits to finish:
+        // the splits' partials combined in split order, the arithmetic of
+        // merge_kernel (so the result does not depend on which split is last)
+        int32_t *cnt = a.merge_cnt + (int64_t)u.b * a.upi + u.kvh * a.HG + u.hg;
+        if (tid == 0) {
+          __threadfence();
+          const int32_t prev = atomicAdd(cnt, 1);
+          const bool last = prev == u.nsplit - 1;
+          if (last) *cnt = 0;  // all splits counted in: ready for the plan's next launch
+          __threadfence();
+          xslot[NW] = last ? 1 : 0;
+        }
+        if (!sync()) {
+          cp_async_wait_all();
+          return;
+        }
+        if (xslot[NW]) {
+          const int64_t stride = (int64_t)a.upi * a.part_floats;  // next split of the unit
+          const float *base = a.partials +
+                              ((int64_t)(md.split_row - u.s) * a.upi + u.kvh * a.HG + u.hg) * a.part_floats;
+          for (int g = tid / kC4; g < u.gcount; g += kRowsPerPass) {
+            float M = -INFINITY;
+            for (int32_t sp = 0; sp < u.nsplit; ++sp) M = fmaxf(M, __ldcg(base + sp * stride + g));
+            float L = 0.f;
+            float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (M != -INFINITY) {
+              for (int32_t sp = 0; sp < u.nsplit; ++sp) {
+                const float *p = base + sp * stride;
+                const float f = exp2_or_zero(__ldcg(p + g) - M);
+                L += f * __ldcg(p + a.GR + g);
+                const float4 x = __ldcg(reinterpret_cast<const float4 *>(p + a.part_o + g * D + 4 * c4));
+                O.x += f * x.x;
+                O.y += f * x.y;
+                O.z += f * x.z;
+                O.w += f * x.w;
+              }
+            }
+            const float den = fmaxf(L, 1e-6f);
+            const float4 r = make_float4(O.x / den, O.y / den, O.z / den, O.w / den);
+            const int64_t op = u.b * a.o0 + (int64_t)(u.qh0 + g) * a.o1;
+            if (a.out_vec) {
+              store_out4(a, op + 4 * c4, r);
+            } else {
+              store_out(a, op + (4 * c4 + 0) * a.o2, r.x);
+              store_out(a, op + (4 * c4 + 1) * a.o2, r.y);
+              store_out(a, op + (4 * c4 + 2) * a.o2, r.z);
+              store_out(a, op + (4 * c4 + 3) * a.o2, r.w);
+            }
+          }
+        }
+      }
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         m[nt][0] = m[nt][1] = -INFINITY;
@@ -1368,7 +1550,6 @@ int32_t resolve_pps(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t max_b
   const int64_t u0 = std::max<int64_t>(1, (int64_t)B * Hkv * ((G + rows - 1) / rows));
   const int64_t mb = std::max<int32_t>(max_blocks, 1);
   const int64_t sms = device_sms();
-  constexpr int64_t kUnitCost = 16, kMergeCost = 32;
   int64_t best_cost = INT64_MAX;
   int32_t best = kMaxPagesPerSplit;
   for (int32_t P = 8; P <= kMaxPagesPerSplit; P += 8) {
@@ -1381,6 +1562,35 @@ int32_t resolve_pps(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t max_b
     }
   }
   return best;
+}
+
+// Range of split lengths a plan may use. An explicit pages_per_split fixes it.
+// Otherwise it is resolve_pps's length, except when the batch has fewer
+// (sequence, kv head, head group) units than SMs: then the split is what fills
+// the GPU, and the host's assumption that every sequence is max_blocks long
+// can be far off in either direction (few long, ragged sequences), so the plan
+// kernel picks the length in [lo, kMaxPagesPerSplit] from the actual lengths.
+// lo keeps the launch at no more than 16 rounds of units even if every
+// sequence were max_blocks long, which also bounds the workspace (sized for lo).
+struct SplitRange {
+  int32_t lo, hi;
+};
+
+SplitRange resolve_split(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t max_blocks, int32_t pps) {
+  const int32_t hi = resolve_pps(B, Hq, Hkv, D, max_blocks, pps);
+  if (pps > 0 || max_blocks <= 8) return {hi, hi};
+  const int32_t G = Hq / Hkv;
+  const int32_t rows = group_rows_for(G, D);
+  const int64_t u0 = std::max<int64_t>(1, (int64_t)B * Hkv * ((G + rows - 1) / rows));
+  const int64_t sms = device_sms();
+  if (u0 >= sms || B > kMaxSimSeqs) return {hi, hi};
+  constexpr int32_t top = kMaxPagesPerSplit;
+  int64_t lo = ((int64_t)max_blocks * u0 + 16 * sms - 1) / (16 * sms);
+  lo = (lo + 7) / 8 * 8;
+  // at most kMaxSplitCandidates multiples of 8 up to the top
+  lo = std::max<int64_t>({8, lo, (int64_t)top - 8 * (kMaxSplitCandidates - 1)});
+  if (lo >= top) return {hi, hi};
+  return {(int32_t)lo, top};
 }
 
 // The tensor-core kernel copies whole (page, head) slabs of 16 x D 16-bit
@@ -1547,9 +1757,9 @@ extern "C" size_t pkv_decode_workspace_size(int32_t batch, int32_t num_q_heads,
   if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || max_blocks < 0 ||
       num_q_heads % num_kv_heads != 0)
     return 0;
-  const int32_t P =
-      resolve_pps(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, pages_per_split);
-  return ws_layout(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, P).total;
+  const SplitRange r =
+      resolve_split(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, pages_per_split);
+  return ws_layout(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, r.lo).total;
 }
 
 extern "C" int pkv_decode_kernel_kind(const void *k_cache, int32_t num_q_heads,
@@ -1576,9 +1786,9 @@ extern "C" int pkv_decode_plan(const int32_t *context_lens, int32_t batch, int32
     set_error_detail("max_blocks * block_size overflows int32");
     return PKV_ERR_INVALID_ARG;
   }
-  const int32_t P =
-      resolve_pps(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, pages_per_split);
-  const WsLayout w = ws_layout(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, P);
+  const SplitRange r =
+      resolve_split(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, pages_per_split);
+  const WsLayout w = ws_layout(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, r.lo);
   if (workspace == nullptr || workspace_bytes < w.total || !aligned_to(workspace, 256)) {
     set_error_detail("workspace needs %zu bytes (256-byte aligned), got %zu", w.total,
                      workspace_bytes);
@@ -1590,10 +1800,11 @@ extern "C" int pkv_decode_plan(const int32_t *context_lens, int32_t batch, int32
   }
   uint8_t *ws = static_cast<uint8_t *>(workspace);
   plan_kernel<<<1, kPlanThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      context_lens, batch, block_size, max_blocks, P, w.units_per_item,
+      context_lens, batch, block_size, max_blocks, r.lo, r.hi,
+      (int32_t)std::min<int64_t>(device_sms(), w.max_items * w.units_per_item), w.units_per_item,
       reinterpret_cast<int32_t *>(ws + w.hdr), reinterpret_cast<int32_t *>(ws + w.seq_off),
-      reinterpret_cast<int32_t *>(ws + w.seq_nsplit), reinterpret_cast<int4 *>(ws + w.items),
-      status);
+      reinterpret_cast<int32_t *>(ws + w.seq_nsplit), reinterpret_cast<int32_t *>(ws + w.merge_cnt),
+      reinterpret_cast<int4 *>(ws + w.items), status);
   return check_launch("plan_kernel");
 }
 
@@ -1629,9 +1840,9 @@ int decode_run_impl(const void *q, const void *kn, const void *vn, const void *k
       return PKV_ERR_ALIGNMENT;
   }
   if (batch == 0) return PKV_OK;
-  const int32_t P =
-      resolve_pps(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, pages_per_split);
-  const WsLayout w = ws_layout(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, P);
+  const SplitRange r =
+      resolve_split(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, pages_per_split);
+  const WsLayout w = ws_layout(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, r.lo);
   if (workspace == nullptr || workspace_bytes < w.total || !aligned_to(workspace, 256)) {
     set_error_detail("workspace needs %zu bytes (256-byte aligned), got %zu", w.total,
                      workspace_bytes);
@@ -1655,7 +1866,7 @@ int decode_run_impl(const void *q, const void *kn, const void *vn, const void *k
   a.bs = block_size;
   a.num_blocks = num_blocks;
   a.max_blocks = max_blocks;
-  a.P = P;
+  a.P = r.hi;
   a.upi = w.units_per_item;
   a.part_o = w.part_o;
   a.part_floats = w.part_floats;
@@ -1676,6 +1887,7 @@ int decode_run_impl(const void *q, const void *kn, const void *vn, const void *k
   a.items = reinterpret_cast<const int4 *>(ws + w.items);
   a.max_items = w.max_items;
   a.partials = reinterpret_cast<float *>(ws + w.partials);
+  a.merge_cnt = reinterpret_cast<int32_t *>(ws + w.merge_cnt);
   a.sched = reinterpret_cast<int32_t *>(ws + w.hdr) + 4;
   a.status = status;
   a.max_polls = kMaxPolls;
@@ -1740,8 +1952,9 @@ int decode_run_impl(const void *q, const void *kn, const void *vn, const void *k
     }
   }
   if (rc) return rc;
-  // sequences longer than one split left partials: merge them (stream-ordered)
-  if (max_blocks > P) {
+  // the CUDA-core kernel leaves the partials of split sequences to the merge
+  // kernel (stream-ordered); the tensor-core kernel merges them itself
+  if (!tc && max_blocks > r.lo) {
     if (w.units_per_item > 65535) {
       set_error_detail("num_kv_heads x head groups = %d exceeds the merge grid", w.units_per_item);
       return PKV_ERR_UNSUPPORTED;

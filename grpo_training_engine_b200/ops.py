@@ -239,6 +239,9 @@ class DecodePlan:
     makes one plan and calls ``paged_attention_decode(..., plan=plan)`` per
     layer. The workspace is also the split-K scratch of every call that uses
     the plan: calls sharing a plan must be ordered on one stream.
+    ``pages_per_split`` is the split-length argument every call of the plan
+    passes (0: the library's heuristic); ``chosen_pages_per_split()`` reads the
+    length the plan kernel used back from the workspace (a device sync).
     """
 
     batch: int
@@ -250,6 +253,10 @@ class DecodePlan:
     pages_per_split: int
     workspace: torch.Tensor
     context_lens: torch.Tensor
+
+    def chosen_pages_per_split(self) -> int:
+        """The split length the plan kernel wrote into the workspace header."""
+        return int(self.workspace[:8].view(torch.int32)[1].item())
 
     def matches(self, batch, num_q_heads, num_kv_heads, head_dim, block_size, max_blocks) -> bool:
         return (self.batch, self.num_q_heads, self.num_kv_heads, self.head_dim, self.block_size, self.max_blocks) == (
@@ -264,12 +271,18 @@ def decode_workspace_bytes(batch, num_q_heads, num_kv_heads, head_dim, max_block
 
 
 def _pages_per_split(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, num_splits, pages_per_split) -> int:
+    """The split-length argument of the C ABI: pages_per_split, or the length
+    that caps the splits per sequence at num_splits, or 0 (the library's
+    heuristic, which lets the plan kernel pick the length from the actual
+    context lengths when the batch has fewer units than SMs)."""
     if pages_per_split <= 0 and num_splits and num_splits > 0:
         pages_per_split = max(1, math.ceil(max(max_blocks, 1) / num_splits))
-    return _lib.check(
+    pages_per_split = max(0, int(pages_per_split))
+    _lib.check(
         "pkv_decode_pages_per_split",
         _lib.load().pkv_decode_pages_per_split(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, pages_per_split),
     )
+    return pages_per_split
 
 
 def plan_decode(

@@ -176,14 +176,25 @@ int pkv_gather(const void *k_cache, const void *v_cache,
  * grouped-query layout (one cache head serves G consecutive query heads).
  *
  * Long contexts are split into chunks of pages_per_split pages; partial
- * (max, sum, acc) triples go to the caller's workspace and a merge kernel,
- * launched on the same stream, combines them in chunk order.
- * pages_per_split == 0 selects the library's heuristic for the current
- * device.
+ * (max, sum, acc) triples go to the caller's workspace and are combined in
+ * chunk order. pages_per_split == 0 selects the library's heuristic for the
+ * current device.
  *
  * pkv_decode = pkv_decode_plan + pkv_decode_run. The plan depends only on
  * context_lens (and the sizes), so a caller that runs many layers with the
  * same context_lens may plan once and run per layer on the same workspace.
+ * After a launch that set PKV_DEV_WAIT_TIMEOUT, plan again before the next
+ * run on that workspace (the plan's scheduling and merge counters may have
+ * been left mid-count).
+ *
+ * pages_per_split == 0: pkv_decode_pages_per_split returns the library's
+ * estimate for sequences of max_blocks pages. When the batch has fewer
+ * (sequence, kv head, head group) units than the device has SMs, the plan
+ * kernel instead picks the split length (a multiple of 8, up to 512) from the
+ * actual lengths, by simulating its schedule; the workspace size accounts for
+ * that. With the tensor-core kernel the last split of a sequence to finish
+ * merges the split partials inside the same launch; the CUDA-core kernel
+ * launches the merge kernel after it.
  */
 int32_t pkv_decode_pages_per_split(int32_t batch, int32_t num_q_heads,
                                    int32_t num_kv_heads, int32_t head_dim,

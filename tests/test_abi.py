@@ -93,7 +93,9 @@ def test_default_split_length_cost_model():
     assert pps(64, 28, 4, 128, 2048, 0) == 512    # config 5: the longest splits
     p = pps(4, 12, 2, 128, 2048, 0)               # 8 long sequences: split to fill the SMs once
     assert 8 * -(-2048 // p) <= 148 and 8 * -(-2048 // (p + 8)) < 148 <= 8 * -(-2048 // (p - 8))
-    assert pps(4, 12, 2, 128, 33, 0) >= 33        # short contexts are never split
+    # a few short sequences leave most SMs idle: split them (the tensor-core
+    # kernel merges inside the launch, so a split costs no extra launch)
+    assert pps(4, 12, 2, 128, 33, 0) < 33
 
 
 def test_kernel_kind_selection():

@@ -73,7 +73,7 @@ def _step_vs_oracle(q, kc, vc, bt, ctx, kn, vn, expect_merge: bool | None = None
     status = torch.zeros(1, dtype=torch.int32, device=DEV)
     plan = plan_decode(ctx, q.shape[1], kc.shape[1], D, BS, bt.shape[1], status=status)
     if expect_merge is not None:
-        assert (bt.shape[1] > plan.pages_per_split) == expect_merge
+        assert (bt.shape[1] > plan.chosen_pages_per_split()) == expect_merge
     out = paged_attention_decode(q, kc, vc, bt, ctx, plan=plan, k_new=kn, v_new=vn, status=status)
     torch.cuda.synchronize()
     assert int(status.item()) == 0
@@ -118,4 +118,58 @@ def test_config5_qwen7b_long_context_split_k_at_size():
     lens = np.exp(rs.uniform(np.log(4096), np.log(32768), size=64)).astype(np.int64)
     tables, nb = _private_tables(lens)
     err, plan = _step_vs_oracle(*_pool(5, tables, nb, lens, 28, 4), expect_merge=True)
-    assert err <= ATOL["bfloat16"], (err, plan.pages_per_split)
+    assert err <= ATOL["bfloat16"], (err, plan.chosen_pages_per_split())
+
+
+def _expected_split(lens, upi: int, max_blocks: int, sms: int, hi: int = 512) -> int:
+    """The plan kernel's choice of split length (choose_split in pkv_decode.cu),
+    restated: for P = lo, lo + 8, ..., 512, simulate the snake schedule of the
+    units (full splits, then partial splits longest first, upi units per item)
+    on the launch's CTAs and take the P whose busiest CTA (pages + 16 per unit)
+    finishes first, + 32 when a sequence is split; ties to the longer split."""
+    B = len(lens)
+    u0 = B * upi
+    lo = -(-max_blocks * u0 // (16 * sms))
+    lo = max(8, -(-lo // 8) * 8, hi - 8 * 63)
+    slots = min(sms, B * -(-max_blocks // lo) * upi)
+    pages = [math.ceil(int(n) / BS) for n in lens]
+    best, best_p = None, hi
+    for P in range(lo, hi + 1, 8):
+        full = sum(p // P for p in pages)
+        parts = sorted((p - (p // P) * P for p in pages if max(1, -(-p // P)) > p // P), reverse=True)
+        lengths = [P] * full + parts
+        units = upi * len(lengths)
+        load = [0] * slots
+        for r in range(-(-units // slots)):
+            for c in range(slots):
+                w = r * slots + (slots - 1 - c if r & 1 else c)
+                if w < units:
+                    load[c] += lengths[w // upi] + 16
+        cost = max(load) + (32 if max(pages) > P else 0)
+        if best is None or cost < best or (cost == best and P > best_p):
+            best, best_p = cost, P
+    return best_p
+
+
+def test_config5_eight_gpu_shard_split_chosen_from_the_lengths():
+    """Config 5 strong-scaled to 8 GPUs leaves a GPU 8 long sequences (32 units of
+    (sequence, kv head) for 148 SMs): the plan kernel picks the split length
+    from their actual lengths by simulating its schedule (not the host's
+    all-sequences-at-max-length estimate), and the result still matches the
+    oracle."""
+    from grpo_training_engine_b200 import _lib
+    from grpo_training_engine_b200.sharding import lpt_assign
+
+    rs = np.random.RandomState(51)
+    lens_all = np.exp(rs.uniform(np.log(4096), np.log(32768), size=64)).astype(np.int64)
+    lens = [int(lens_all[i]) for i in lpt_assign(lens_all.tolist(), 8)[0]]
+    tables, nb = _private_tables(lens)
+    args = _pool(6, tables, nb, lens, 28, 4)
+    max_blocks = args[3].shape[1]
+    err, plan = _step_vs_oracle(*args)
+    assert err <= ATOL["bfloat16"], err
+    host = _lib.load().pkv_decode_pages_per_split(len(lens), 28, 4, D, max_blocks, 0)
+    chosen = plan.chosen_pages_per_split()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    assert chosen == _expected_split(lens, 4, max_blocks, sms), (chosen, host)
+    assert chosen != host

@@ -9,8 +9,9 @@ waits for an element that never comes, the other warps then wait at the unit
 barrier for that warp, and the producer waits for a ring slot the warp never
 frees. Nothing faults or traps; the waits simply run out. The test checks
 that the launch ends promptly, that the status word carries the timeout bit,
-and that a normal decode on the same stream right after it is correct (the
-context is still usable and the plan's scheduling counters were reset).
+and that a normal decode on the same stream right after it, with a new plan
+(a launch that timed out may leave a split's merge counter mid-count, so its
+plan is not reused), is correct: the context is still usable.
 """
 
 from __future__ import annotations
@@ -67,8 +68,10 @@ def test_wait_timeout_is_reported_and_the_context_stays_usable(pages_per_split):
     assert elapsed < 10.0, elapsed  # the short bounds end the launch in milliseconds
     assert int(status.item()) & _lib.DEV_WAIT_TIMEOUT
 
-    # the same stream, the same plan workspace: a normal decode is correct
+    # the same stream, a new plan in the same workspace: a normal decode is correct
     status.zero_()
+    plan = plan_decode(ctxd, hq, hkv, d, bs, bt.shape[1], pages_per_split=pages_per_split, workspace=ws,
+                       status=status)
     out2 = paged_attention_decode(qd, kd, vd, btd, ctxd, plan=plan, status=status)
     torch.cuda.synchronize()
     assert int(status.item()) == 0
