@@ -45,34 +45,30 @@ def _stale(target: Path, deps: list[Path]) -> bool:
 
 
 def build_library(force: bool = False, verbose: bool = False) -> Path:
-    """Compile libpkv.so if any source or header is newer than it."""
+    """Compile libpkv.so if any source or header is newer than it: each source
+    to an object in parallel, then one link."""
+    from concurrent.futures import ThreadPoolExecutor
+
     deps = [CSRC / s for s in SOURCES] + list(CSRC.glob("*.cuh")) + [INCLUDE / "pkv.h"]
     if not force and not _stale(LIB_PATH, deps):
         return LIB_PATH
     vscript = CSRC / "pkv.map"
     tmp = LIB_PATH.with_suffix(".so.tmp")
-    cmd = [
-        _nvcc(),
-        "-O3",
-        "-std=c++17",
-        *ARCH_FLAGS,
-        "-lineinfo",
-        "-Xcompiler",
-        "-fPIC",
-        "-shared",
-        "-I",
-        str(INCLUDE),
-        "-Xlinker",
-        f"--version-script={vscript}",
-        "-o",
-        str(tmp),
-        *[str(CSRC / s) for s in SOURCES],
-    ]
-    if verbose:
-        print(" ".join(cmd), file=sys.stderr)
-    res = subprocess.run(cmd, capture_output=True, text=True)
-    if res.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+    common = [_nvcc(), "-O3", "-std=c++17", *ARCH_FLAGS, "-lineinfo", "-Xcompiler", "-fPIC", "-I", str(INCLUDE)]
+    objdir = PKG_DIR / "_build"
+    objdir.mkdir(exist_ok=True)
+
+    def run(cmd):
+        if verbose:
+            print(" ".join(cmd), file=sys.stderr)
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+
+    objs = [objdir / (Path(s).stem + ".o") for s in SOURCES]
+    with ThreadPoolExecutor(max_workers=len(SOURCES)) as pool:
+        list(pool.map(run, [common + ["-c", str(CSRC / s), "-o", str(o)] for s, o in zip(SOURCES, objs)]))
+    run([*common, "-shared", "-Xlinker", f"--version-script={vscript}", "-o", str(tmp), *map(str, objs)])
     os.replace(tmp, LIB_PATH)
     return LIB_PATH
 

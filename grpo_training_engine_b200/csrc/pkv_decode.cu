@@ -26,8 +26,9 @@
 //   decode_tc_kernel      bf16/fp16 cache, block_size 16, head_dim 64/128.
 //                         A producer warp schedules units and publishes, per
 //                         consumer warp, the pages to read (plus staged
-//                         query rows); each of 7 (head_dim 128) or 8 (64)
-//                         consumer warps streams its own K and V pages into a
+//                         query rows); each of 9 (head_dim 128; 7 when it
+//                         also applies RoPE) or 8 (64) consumer warps
+//                         streams its own K and V pages into a
 //                         smem ring with 16-byte cp.async (one commit group per
 //                         page, issued S - 1 pages ahead) and computes
 //                         K.q^T and V^T.P^T with m16n8k16 tensor-core MMAs
@@ -280,7 +281,7 @@ __device__ __forceinline__ SeqSplits seq_splits(const int32_t *ctx, int32_t b, i
 // snake). A CTA's time is its units' pages plus kUnitCost per unit; the launch
 // takes the largest CTA time, plus kMergeCost when some sequence is split.
 // Ties go to the longer split. B <= kMaxSimSeqs (the host enables this only
-// for fewer (sequence, kv head, head group) units than SMs). Whole block.
+// for such batches). Whole block.
 constexpr int kSimWarps = 16;
 constexpr int kMaxSimSeqs = 160;
 
@@ -786,7 +787,7 @@ __device__ __forceinline__ uint4 shfl_xor_u4(uint4 v, int m) {
                     __shfl_xor_sync(0xffffffffu, v.z, m), __shfl_xor_sync(0xffffffffu, v.w, m));
 }
 
-template <typename T, int D, int NW, int S, bool kExactP, int NT>
+template <typename T, int D, int NW, int S, bool kExactP, int NT, bool kRope>
 __global__ void __launch_bounds__((NW + 1) * 32, 1)
 decode_tc_kernel(DecodeArgs a) {
   static_assert(NT == 1 || NT == 2, "one or two tiles of 8 query heads");
@@ -878,7 +879,7 @@ decode_tc_kernel(DecodeArgs a) {
         const int32_t pi = lane + 32 * i;
         btr[i] = (w < total && pi < np) ? a.bt[u.b * a.bt0 + (int64_t)(u.p_begin + pi) * a.bt1] : -1;
       }
-      if (a.rcos != nullptr && w < total) {
+      if (kRope && a.rcos != nullptr && w < total) {
         const int64_t off = (u.b * a.rcs + 8 * (lane % kRowChunks)) * 2;
         rc = *reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(a.rcos) + off);
         rs = *reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(a.rsin) + off);
@@ -1013,7 +1014,7 @@ decode_tc_kernel(DecodeArgs a) {
       publish(0, 1);
       __syncwarp();
       // query rows (and the appended K/V row) -> the unit's query slot
-      if (a.rcos != nullptr) {  // RoPE: the partner chunk (other half of the head) is in lane ^ D/16
+      if (kRope && a.rcos != nullptr) {  // RoPE: the partner chunk (other half of the head) is in lane ^ D/16
         const bool second = (lane % kRowChunks) >= kRowChunks / 2;
 #pragma unroll
         for (int i = 0; i < kQPerLane; ++i)
@@ -1565,13 +1566,15 @@ int32_t resolve_pps(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t max_b
 }
 
 // Range of split lengths a plan may use. An explicit pages_per_split fixes it.
-// Otherwise it is resolve_pps's length, except when the batch has fewer
-// (sequence, kv head, head group) units than SMs: then the split is what fills
-// the GPU, and the host's assumption that every sequence is max_blocks long
-// can be far off in either direction (few long, ragged sequences), so the plan
-// kernel picks the length in [lo, kMaxPagesPerSplit] from the actual lengths.
-// lo keeps the launch at no more than 16 rounds of units even if every
-// sequence were max_blocks long, which also bounds the workspace (sized for lo).
+// Otherwise it is resolve_pps's length, except for batches of at most
+// kMaxSimSeqs sequences: there a few units more or less per CTA decide the
+// launch time, and the host's assumption that every sequence is max_blocks
+// long can be far off in either direction (ragged lengths), so the plan kernel
+// picks the length in [lo, top] from the actual lengths by simulating its
+// schedule. top = max_blocks rounded up to 8 (longer splits split nothing),
+// at most kMaxPagesPerSplit; lo keeps the launch at no more than 16 rounds of
+// units even if every sequence were max_blocks long, which also bounds the
+// workspace (sized for lo).
 struct SplitRange {
   int32_t lo, hi;
 };
@@ -1583,8 +1586,8 @@ SplitRange resolve_split(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t 
   const int32_t rows = group_rows_for(G, D);
   const int64_t u0 = std::max<int64_t>(1, (int64_t)B * Hkv * ((G + rows - 1) / rows));
   const int64_t sms = device_sms();
-  if (u0 >= sms || B > kMaxSimSeqs) return {hi, hi};
-  constexpr int32_t top = kMaxPagesPerSplit;
+  if (B > kMaxSimSeqs) return {hi, hi};
+  const int32_t top = std::min<int32_t>(kMaxPagesPerSplit, (max_blocks + 7) / 8 * 8);
   int64_t lo = ((int64_t)max_blocks * u0 + 16 * sms - 1) / (16 * sms);
   lo = (lo + 7) / 8 * 8;
   // at most kMaxSplitCandidates multiples of 8 up to the top
@@ -1687,20 +1690,22 @@ int launch_generic_d(const DecodeArgs &a, cudaStream_t st, int64_t max_units) {
 }
 
 // Tensor-core kernel configuration: consumer warps and a per-warp ring of S
-// pages. head_dim 128: 7 consumer warps x 3 x 8 KB = 168 KB of K/V staging; with
-// the producer that is exactly two warps per SM sub-partition (8 consumers put
-// three on one of them), and measured on B200 it streams ~2% faster than 8 x 3
-// (config 4: 102.0% vs 100.1% of the copy peak; config 5 92.4% vs 90.9%) and
-// on par with 6 x 4. head_dim 64: 8 x 6 x 4 KB.
-template <typename T, int D, bool kExactP, int NT>
+// pages. head_dim 128 without RoPE (158 registers for one head tile): 9
+// consumer warps x 2 x 8 KB = 144 KB of K/V staging; measured on B200 against
+// 7 x 3, 8 x 3 and 11 x 2 it is the fastest (config 4 694 us per layer vs 704
+// for 7 x 3, config 5 292 vs 295, their 8-GPU shards 1.5-2% faster, config 3
+// unchanged). With RoPE in the producer the kernel takes 218 registers, which
+// leaves room for 7 consumer warps (+ the producer: two warps per SM
+// sub-partition) x 3 x 8 KB = 168 KB. head_dim 64: 8 x 6 x 4 KB.
+template <typename T, int D, bool kExactP, int NT, bool kRope>
 int launch_tc_x(const DecodeArgs &a, cudaStream_t st, int64_t max_units) {
-  constexpr int kTcWarps = D == 128 ? 7 : 8;
-  constexpr int S = D == 128 ? 3 : 6;
+  constexpr int kTcWarps = D == 128 ? (kRope ? 7 : 9) : 8;
+  constexpr int S = D == 128 ? (kRope ? 3 : 2) : 6;
   using L = TcSmem<D, kTcWarps, S>;
   static_assert(L::kBt + sizeof(int32_t) * kMaxPagesPerSplit + 1024 <= 227 * 1024,
                 "tensor-core decode exceeds the 227 KB of shared memory per CTA");
   const size_t smem = L::bytes(a.P);
-  auto kern = decode_tc_kernel<T, D, kTcWarps, S, kExactP, NT>;
+  auto kern = decode_tc_kernel<T, D, kTcWarps, S, kExactP, NT, kRope>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return check_launch("cudaFuncSetAttribute(tc)");
@@ -1728,13 +1733,21 @@ int launch_tc_x(const DecodeArgs &a, cudaStream_t st, int64_t max_units) {
   return check_launch("decode_tc_kernel");
 }
 
-template <typename T, int D>
-int launch_tc_t(const DecodeArgs &a, cudaStream_t st, int64_t max_units, int32_t flags) {
+template <typename T, int D, bool kRope>
+int launch_tc_r(const DecodeArgs &a, cudaStream_t st, int64_t max_units, int32_t flags) {
   // query heads of a head group: up to 8 in one MMA n-tile, up to 16 in two
   const bool two = a.GR > 8;
   if (flags & PKV_DECODE_EXACT_P)
-    return two ? launch_tc_x<T, D, true, 2>(a, st, max_units) : launch_tc_x<T, D, true, 1>(a, st, max_units);
-  return two ? launch_tc_x<T, D, false, 2>(a, st, max_units) : launch_tc_x<T, D, false, 1>(a, st, max_units);
+    return two ? launch_tc_x<T, D, true, 2, kRope>(a, st, max_units)
+               : launch_tc_x<T, D, true, 1, kRope>(a, st, max_units);
+  return two ? launch_tc_x<T, D, false, 2, kRope>(a, st, max_units)
+             : launch_tc_x<T, D, false, 1, kRope>(a, st, max_units);
+}
+
+template <typename T, int D>
+int launch_tc_t(const DecodeArgs &a, cudaStream_t st, int64_t max_units, int32_t flags) {
+  return a.rcos != nullptr ? launch_tc_r<T, D, true>(a, st, max_units, flags)
+                           : launch_tc_r<T, D, false>(a, st, max_units, flags);
 }
 
 }  // namespace

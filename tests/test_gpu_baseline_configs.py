@@ -121,14 +121,15 @@ def test_config5_qwen7b_long_context_split_k_at_size():
     assert err <= ATOL["bfloat16"], (err, plan.chosen_pages_per_split())
 
 
-def _expected_split(lens, upi: int, max_blocks: int, sms: int, hi: int = 512) -> int:
+def _expected_split(lens, upi: int, max_blocks: int, sms: int) -> int:
     """The plan kernel's choice of split length (choose_split in pkv_decode.cu),
-    restated: for P = lo, lo + 8, ..., 512, simulate the snake schedule of the
+    restated: for P = lo, lo + 8, ..., top, simulate the snake schedule of the
     units (full splits, then partial splits longest first, upi units per item)
     on the launch's CTAs and take the P whose busiest CTA (pages + 16 per unit)
     finishes first, + 32 when a sequence is split; ties to the longer split."""
     B = len(lens)
     u0 = B * upi
+    hi = min(512, -(-max_blocks // 8) * 8)
     lo = -(-max_blocks * u0 // (16 * sms))
     lo = max(8, -(-lo // 8) * 8, hi - 8 * 63)
     slots = min(sms, B * -(-max_blocks // lo) * upi)
