@@ -61,8 +61,11 @@ constexpr uint32_t kTestWaitPolls = 4096;
 // Split-length cost model, in pages' worth of one CTA's streaming: the fixed
 // cost of a unit (cross-warp combine and pipeline refill, measured on B200 at
 // about 16 pages) and of merging split partials (the last split of a sequence
-// reads the others' partials back from L2 and writes the output).
-constexpr int64_t kUnitCost = 16, kMergeCost = 8;
+// counts in, reads the others' partials back from L2 and writes the output:
+// ~2 us in a per-warp trace, about 16 pages), and the extra cost of every unit
+// of a split sequence (its partial store, fence and count-in barrier: ~1.5 us
+// more per unit than an unsplit one in the same trace, about 12 pages).
+constexpr int64_t kUnitCost = 16, kMergeCost = 16, kSplitUnitCost = 12;
 // Candidate split lengths the plan kernel weighs (multiples of 8 pages).
 constexpr int kMaxSplitCandidates = 64;
 
@@ -278,29 +281,35 @@ __device__ __forceinline__ SeqSplits seq_splits(const int32_t *ctx, int32_t b, i
 // items are the full P-page splits, then the partial last splits by decreasing
 // length (the order this kernel writes), each expanded to upi units; CTA c of
 // `slots` takes unit c in round 0, 2 slots - 1 - c in round 1, and so on (the
-// snake). A CTA's time is its units' pages plus kUnitCost per unit; the launch
-// takes the largest CTA time, plus kMergeCost when some sequence is split.
+// snake). A CTA's time is its units' pages plus kUnitCost per unit (plus
+// kSplitUnitCost for a unit of a split sequence); the launch takes the largest
+// CTA time, plus kMergeCost when some sequence is split.
 // Ties go to the longer split. B <= kMaxSimSeqs (the host enables this only
 // for such batches). Whole block.
 constexpr int kSimWarps = 16;
-constexpr int kMaxSimSeqs = 160;
+constexpr int kMaxSimSeqs = 256;
 
 __device__ int32_t choose_split(const int32_t *__restrict__ ctx, int32_t B, int32_t bs, int32_t cap,
                                 int32_t p_lo, int32_t p_hi, int32_t upi, int32_t slots) {
+  static_assert(kMaxSimSeqs % 4 == 0, "rest rows are read as int4");
   __shared__ int32_t s_pages[kMaxSimSeqs];
-  __shared__ int32_t s_rest[kSimWarps][kMaxSimSeqs];    // partial length per sequence (-1: none)
-  __shared__ int32_t s_sorted[kSimWarps][kMaxSimSeqs];  // partial lengths, longest first
+  __shared__ __align__(16) int32_t s_rest[kSimWarps][kMaxSimSeqs];  // partial length per sequence (-1: none)
+  __shared__ int32_t s_sorted[kSimWarps][kMaxSimSeqs];               // partial lengths, longest first
   __shared__ long long s_cost[kMaxSplitCandidates];
   __shared__ int32_t s_maxp, s_choice;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int32_t ncand = min(kMaxSplitCandidates, (p_hi - p_lo) / 8 + 1);
   if (tid == 0) s_maxp = 0;
   __syncthreads();
+  int32_t mp = 0;
   if (tid < B) {
     const int32_t c = min(max(ctx[tid], 0), cap);
-    s_pages[tid] = (c + bs - 1) / bs;
-    atomicMax(&s_maxp, s_pages[tid]);
+    mp = (c + bs - 1) / bs;
+    s_pages[tid] = mp;
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mp = max(mp, __shfl_xor_sync(0xffffffffu, mp, o));
+  if (lane == 0 && mp > 0) atomicMax(&s_maxp, mp);
   __syncthreads();
   const int32_t maxp = s_maxp;
   if (warp < kSimWarps) {
@@ -309,12 +318,19 @@ __device__ int32_t choose_split(const int32_t *__restrict__ ctx, int32_t B, int3
     for (int32_t k = warp; k < ncand; k += kSimWarps) {
       const int32_t P = p_lo + 8 * k;
       int32_t full = 0, parts = 0;
-      for (int32_t b = lane; b < B; b += 32) {
-        const int32_t pg = s_pages[b];
-        const int32_t f = pg / P, n = pg > 0 ? (pg + P - 1) / P : 1;
-        full += f;
-        parts += n > f ? 1 : 0;
-        rest[b] = n > f ? pg - f * P : -1;
+      const int32_t B4 = (B + 3) & ~3;
+      for (int32_t b = lane; b < B4; b += 32) {
+        int32_t r = -1;  // rows past B never rank
+        if (b < B) {
+          const int32_t pg = s_pages[b];
+          const int32_t f = pg / P, n = pg > 0 ? (pg + P - 1) / P : 1;
+          full += f;
+          parts += n > f ? 1 : 0;
+          // a partial split's cost: its pages, plus the split overhead when the
+          // sequence has other splits (the last split of a multi-split sequence)
+          r = n > f ? pg - f * P + (f > 0 ? (int32_t)kSplitUnitCost : 0) : -1;
+        }
+        rest[b] = r;
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
@@ -322,28 +338,36 @@ __device__ int32_t choose_split(const int32_t *__restrict__ ctx, int32_t B, int3
         parts += __shfl_xor_sync(0xffffffffu, parts, o);
       }
       __syncwarp();
-      // rank of each partial split among the partials: longer first, ties by index
+      // rank of each partial split among the partials: longer first, ties by
+      // index (four lengths per 16-byte load, independent loads unrolled)
       for (int32_t b = lane; b < B; b += 32) {
         const int32_t r = rest[b];
         if (r < 0) continue;
         int32_t rank = 0;
-        for (int32_t j = 0; j < B; ++j) {
-          const int32_t x = rest[j];
-          rank += (x > r || (x == r && j < b)) ? 1 : 0;
+#pragma unroll 4
+        for (int32_t j = 0; j < B4; j += 4) {
+          const int4 x = *reinterpret_cast<const int4 *>(rest + j);
+          rank += (x.x > r || (x.x == r && j < b)) ? 1 : 0;
+          rank += (x.y > r || (x.y == r && j + 1 < b)) ? 1 : 0;
+          rank += (x.z > r || (x.z == r && j + 2 < b)) ? 1 : 0;
+          rank += (x.w > r || (x.w == r && j + 3 < b)) ? 1 : 0;
         }
         sorted[rank] = r;
       }
       __syncwarp();
-      const int64_t units = (int64_t)upi * (full + parts);
-      const int64_t rounds = (units + slots - 1) / slots;
+      // P >= lo keeps the full splits within 16 rounds of the CTAs, so the
+      // units (full + one partial per sequence and unit) fit 32 bits
+      const int32_t units = upi * (full + parts);
+      const int32_t rounds = (units + slots - 1) / slots;
       long long worst = 0;
       for (int32_t c = lane; c < slots; c += 32) {
         long long load = 0;
-        for (int64_t r = 0; r < rounds; ++r) {
-          const int64_t w = r * slots + ((r & 1) ? slots - 1 - c : c);
+        for (int32_t r = 0; r < rounds; ++r) {
+          const int32_t w = r * slots + ((r & 1) ? slots - 1 - c : c);
           if (w >= units) continue;
-          const int64_t item = w / upi;
-          load += (item < full ? P : sorted[item - full]) + kUnitCost;
+          const int32_t item = w / upi;
+          // full splits are (nearly always) splits of longer sequences
+          load += (item < full ? P + kSplitUnitCost : sorted[item - full]) + kUnitCost;
         }
         worst = max(worst, load);
       }

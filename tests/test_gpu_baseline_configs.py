@@ -125,8 +125,9 @@ def _expected_split(lens, upi: int, max_blocks: int, sms: int) -> int:
     """The plan kernel's choice of split length (choose_split in pkv_decode.cu),
     restated: for P = lo, lo + 8, ..., top, simulate the snake schedule of the
     units (full splits, then partial splits longest first, upi units per item)
-    on the launch's CTAs and take the P whose busiest CTA (pages + 16 per unit)
-    finishes first, + 32 when a sequence is split; ties to the longer split."""
+    on the launch's CTAs and take the P whose busiest CTA (pages + 16 per unit,
+    + 12 per unit of a split sequence) finishes first, + 16 when a sequence is
+    split; ties to the longer split."""
     B = len(lens)
     u0 = B * upi
     hi = min(512, -(-max_blocks // 8) * 8)
@@ -137,8 +138,11 @@ def _expected_split(lens, upi: int, max_blocks: int, sms: int) -> int:
     best, best_p = None, hi
     for P in range(lo, hi + 1, 8):
         full = sum(p // P for p in pages)
-        parts = sorted((p - (p // P) * P for p in pages if max(1, -(-p // P)) > p // P), reverse=True)
-        lengths = [P] * full + parts
+        # a unit of a split sequence costs 12 pages more (the last partial of a
+        # split sequence, and every full split)
+        parts = sorted((p - (p // P) * P + (12 if p // P else 0) for p in pages if max(1, -(-p // P)) > p // P),
+                       reverse=True)
+        lengths = [P + 12] * full + parts
         units = upi * len(lengths)
         load = [0] * slots
         for r in range(-(-units // slots)):
@@ -146,7 +150,7 @@ def _expected_split(lens, upi: int, max_blocks: int, sms: int) -> int:
                 w = r * slots + (slots - 1 - c if r & 1 else c)
                 if w < units:
                     load[c] += lengths[w // upi] + 16
-        cost = max(load) + (32 if max(pages) > P else 0)
+        cost = max(load) + (16 if max(pages) > P else 0)
         if best is None or cost < best or (cost == best and P > best_p):
             best, best_p = cost, P
     return best_p

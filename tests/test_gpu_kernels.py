@@ -432,9 +432,14 @@ ROPE_SHAPES = [
 @pytest.mark.parametrize("shape", ROPE_SHAPES, ids=lambda s: f"b{s[0]}q{s[1]}kv{s[2]}d{s[3]}")
 @pytest.mark.parametrize("splits", [0, 3])
 def test_rope_in_decode_equals_rope_then_fused_decode(shape, splits):
-    """RoPE inside the decode launch gives the bits of rope_qk followed by the fused
-    append + decode: the same output and the same cache bytes, also when q / k / v
-    are column views of one stacked projection output."""
+    """RoPE inside the decode launch against rope_qk followed by the fused append +
+    decode, also when q / k / v are column views of one stacked projection
+    output: the rotated K row lands in the cache bit for bit, and both outputs
+    match the oracle on the rotated inputs. For head_dim 64 both calls run the
+    same kernel configuration and agree bit for bit; for head_dim 128 the RoPE
+    launch runs 7 consumer warps (its registers allow no more) and the plain one
+    9, so pages meet the softmax in other warps and the bf16-rounded weights
+    differ within the decode tolerance."""
     from grpo_training_engine_b200 import ops
 
     batch, hq, hkv, d, bs, dtype, ctxs = shape
@@ -457,13 +462,17 @@ def test_rope_in_decode_equals_rope_then_fused_decode(shape, splits):
                                  rope=(cos, sin), status=status)
     torch.cuda.synchronize()
     assert int(status.item()) == 0
-    assert torch.equal(got, ref)
     assert _sha(kc1, vc1) == _sha(kc2, vc2)
-    # contiguous inputs, 16-bit output
+    want = oracle.decode(q1.cpu(), kc1.cpu(), vc1.cpu(), bt.cpu(), ctx.cpu())
+    tol = ATOL[str(dtype).split(".")[1]]
+    assert _maxabs(got, want) <= tol and _maxabs(ref, want) <= tol, (_maxabs(got, want), _maxabs(ref, want))
+    if d == 64:
+        assert torch.equal(got, ref)
+    # contiguous inputs, 16-bit output: the cast of the fp32 output of the same launch
     got16 = paged_attention_decode(q_lin.contiguous().view(batch, hq, d), kc2.clone(), vc2.clone(), bt, ctx,
                                    num_splits=splits, k_new=k_lin.contiguous().view(batch, hkv, d), v_new=v1,
                                    rope=(cos, sin), out_dtype=dtype)
-    assert torch.equal(got16, ref.to(dtype))
+    assert torch.equal(got16, got.to(dtype))
 
 
 def test_rope_in_decode_refuses_what_it_cannot_serve():
