@@ -277,24 +277,26 @@ __device__ __forceinline__ SeqSplits seq_splits(const int32_t *ctx, int32_t b, i
 
 // Split length for these lengths: P in {p_lo, p_lo + 8, ..., p_hi}, the one
 // whose launch the tensor-core kernel's schedule finishes first. Each of
-// kSimWarps warps takes candidates in turn and simulates the schedule exactly:
-// items are the full P-page splits, then the partial last splits by decreasing
+// kSimWarps warps takes candidates in turn and simulates the schedule: items
+// are the full P-page splits, then the partial last splits by decreasing
 // length (the order this kernel writes), each expanded to upi units; CTA c of
 // `slots` takes unit c in round 0, 2 slots - 1 - c in round 1, and so on (the
 // snake). A CTA's time is its units' pages plus kUnitCost per unit (plus
 // kSplitUnitCost for a unit of a split sequence); the launch takes the largest
-// CTA time, plus kMergeCost when some sequence is split.
-// Ties go to the longer split. B <= kMaxSimSeqs (the host enables this only
-// for such batches). Whole block.
+// CTA time, plus kMergeCost when some sequence is split. The partial splits are
+// ordered by a histogram of their costs in 8-page bins (a unit's cost is taken
+// as its bin's upper edge, within 8 pages), so a candidate costs O(B / 32 +
+// rounds x log bins) per lane. Ties go to the longer split. B <= kMaxSimSeqs
+// (the host enables this only for such batches). Whole block.
 constexpr int kSimWarps = 16;
-constexpr int kMaxSimSeqs = 256;
+constexpr int kMaxSimSeqs = kPlanThreads;
+constexpr int kSimBins = (kMaxPagesPerSplit + (int)kSplitUnitCost) / 8 + 2;
 
 __device__ int32_t choose_split(const int32_t *__restrict__ ctx, int32_t B, int32_t bs, int32_t cap,
                                 int32_t p_lo, int32_t p_hi, int32_t upi, int32_t slots) {
-  static_assert(kMaxSimSeqs % 4 == 0, "rest rows are read as int4");
   __shared__ int32_t s_pages[kMaxSimSeqs];
-  __shared__ __align__(16) int32_t s_rest[kSimWarps][kMaxSimSeqs];  // partial length per sequence (-1: none)
-  __shared__ int32_t s_sorted[kSimWarps][kMaxSimSeqs];               // partial lengths, longest first
+  __shared__ int32_t s_hist[kSimWarps][kSimBins];   // partial splits per cost bin
+  __shared__ int32_t s_above[kSimWarps][kSimBins];  // partial splits in higher bins
   __shared__ long long s_cost[kMaxSplitCandidates];
   __shared__ int32_t s_maxp, s_choice;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -313,24 +315,24 @@ __device__ int32_t choose_split(const int32_t *__restrict__ ctx, int32_t B, int3
   __syncthreads();
   const int32_t maxp = s_maxp;
   if (warp < kSimWarps) {
-    int32_t *rest = s_rest[warp];
-    int32_t *sorted = s_sorted[warp];
+    int32_t *hist = s_hist[warp];
+    int32_t *above = s_above[warp];
     for (int32_t k = warp; k < ncand; k += kSimWarps) {
       const int32_t P = p_lo + 8 * k;
+      for (int i = lane; i < kSimBins; i += 32) hist[i] = 0;
+      __syncwarp();
       int32_t full = 0, parts = 0;
-      const int32_t B4 = (B + 3) & ~3;
-      for (int32_t b = lane; b < B4; b += 32) {
-        int32_t r = -1;  // rows past B never rank
-        if (b < B) {
-          const int32_t pg = s_pages[b];
-          const int32_t f = pg / P, n = pg > 0 ? (pg + P - 1) / P : 1;
-          full += f;
-          parts += n > f ? 1 : 0;
-          // a partial split's cost: its pages, plus the split overhead when the
-          // sequence has other splits (the last split of a multi-split sequence)
-          r = n > f ? pg - f * P + (f > 0 ? (int32_t)kSplitUnitCost : 0) : -1;
+      for (int32_t b = lane; b < B; b += 32) {
+        const int32_t pg = s_pages[b];
+        const int32_t f = pg / P, n = pg > 0 ? (pg + P - 1) / P : 1;
+        full += f;
+        if (n > f) {
+          // the last split's cost: its pages, plus the split overhead when the
+          // sequence has other splits
+          const int32_t cost = pg - f * P + (f > 0 ? (int32_t)kSplitUnitCost : 0);
+          atomicAdd(&hist[cost >> 3], 1);
+          ++parts;
         }
-        rest[b] = r;
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
@@ -338,21 +340,12 @@ __device__ int32_t choose_split(const int32_t *__restrict__ ctx, int32_t B, int3
         parts += __shfl_xor_sync(0xffffffffu, parts, o);
       }
       __syncwarp();
-      // rank of each partial split among the partials: longer first, ties by
-      // index (four lengths per 16-byte load, independent loads unrolled)
-      for (int32_t b = lane; b < B; b += 32) {
-        const int32_t r = rest[b];
-        if (r < 0) continue;
-        int32_t rank = 0;
-#pragma unroll 4
-        for (int32_t j = 0; j < B4; j += 4) {
-          const int4 x = *reinterpret_cast<const int4 *>(rest + j);
-          rank += (x.x > r || (x.x == r && j < b)) ? 1 : 0;
-          rank += (x.y > r || (x.y == r && j + 1 < b)) ? 1 : 0;
-          rank += (x.z > r || (x.z == r && j + 2 < b)) ? 1 : 0;
-          rank += (x.w > r || (x.w == r && j + 3 < b)) ? 1 : 0;
+      if (lane == 0) {  // partial splits in bins above each bin
+        int32_t acc = 0;
+        for (int i = kSimBins - 1; i >= 0; --i) {
+          above[i] = acc;
+          acc += hist[i];
         }
-        sorted[rank] = r;
       }
       __syncwarp();
       // P >= lo keeps the full splits within 16 rounds of the CTAs, so the
@@ -366,15 +359,28 @@ __device__ int32_t choose_split(const int32_t *__restrict__ ctx, int32_t B, int3
           const int32_t w = r * slots + ((r & 1) ? slots - 1 - c : c);
           if (w >= units) continue;
           const int32_t item = w / upi;
-          // full splits are (nearly always) splits of longer sequences
-          load += (item < full ? P + kSplitUnitCost : sorted[item - full]) + kUnitCost;
+          int32_t cost;
+          if (item < full) {
+            cost = P + (int32_t)kSplitUnitCost;  // full splits are (nearly always) of longer sequences
+          } else {
+            // bin of the (item - full)-th longest partial: the lowest bin with at
+            // most that many partials above it
+            const int32_t j = item - full;
+            int32_t lo_b = 0, hi_b = kSimBins - 1;
+            while (lo_b < hi_b) {
+              const int32_t mid = (lo_b + hi_b) >> 1;
+              if (above[mid] <= j) hi_b = mid; else lo_b = mid + 1;
+            }
+            cost = lo_b * 8 + 7;
+          }
+          load += cost + kUnitCost;
         }
         worst = max(worst, load);
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) worst = max(worst, __shfl_xor_sync(0xffffffffu, worst, o));
       if (lane == 0) s_cost[k] = worst + (maxp > P ? kMergeCost : 0);
-      __syncwarp();  // rest / sorted are rewritten for the next candidate
+      __syncwarp();  // hist / above are rewritten for the next candidate
     }
   }
   __syncthreads();

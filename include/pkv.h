@@ -188,7 +188,7 @@ int pkv_gather(const void *k_cache, const void *v_cache,
  * been left mid-count).
  *
  * pages_per_split == 0: pkv_decode_pages_per_split returns the library's
- * estimate for sequences of max_blocks pages. For batches of at most 256
+ * estimate for sequences of max_blocks pages. For batches of at most 1024
  * sequences the plan kernel instead picks the split length (a multiple of 8,
  * up to 512) from the actual lengths, by simulating its schedule; the
  * workspace size accounts for that. With the tensor-core kernel the last split of a sequence to finish

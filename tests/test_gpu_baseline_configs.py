@@ -126,8 +126,9 @@ def _expected_split(lens, upi: int, max_blocks: int, sms: int) -> int:
     restated: for P = lo, lo + 8, ..., top, simulate the snake schedule of the
     units (full splits, then partial splits longest first, upi units per item)
     on the launch's CTAs and take the P whose busiest CTA (pages + 16 per unit,
-    + 12 per unit of a split sequence) finishes first, + 16 when a sequence is
-    split; ties to the longer split."""
+    + 12 per unit of a split sequence; a partial split's cost at the upper edge
+    of its 8-page bin) finishes first, + 16 when a sequence is split; ties to the
+    longer split."""
     B = len(lens)
     u0 = B * upi
     hi = min(512, -(-max_blocks // 8) * 8)
@@ -139,9 +140,10 @@ def _expected_split(lens, upi: int, max_blocks: int, sms: int) -> int:
     for P in range(lo, hi + 1, 8):
         full = sum(p // P for p in pages)
         # a unit of a split sequence costs 12 pages more (the last partial of a
-        # split sequence, and every full split)
-        parts = sorted((p - (p // P) * P + (12 if p // P else 0) for p in pages if max(1, -(-p // P)) > p // P),
-                       reverse=True)
+        # split sequence, and every full split); partial costs are taken at the
+        # upper edge of their 8-page bin
+        parts = sorted(((p - (p // P) * P + (12 if p // P else 0)) // 8 * 8 + 7
+                        for p in pages if max(1, -(-p // P)) > p // P), reverse=True)
         lengths = [P + 12] * full + parts
         units = upi * len(lengths)
         load = [0] * slots
