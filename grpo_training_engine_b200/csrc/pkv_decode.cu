@@ -284,9 +284,9 @@ __device__ __forceinline__ SeqSplits seq_splits(const int32_t *ctx, int32_t b, i
 // snake). A CTA's time is its units' pages plus kUnitCost per unit (plus
 // kSplitUnitCost for a unit of a split sequence); the launch takes the largest
 // CTA time, plus kMergeCost when some sequence is split. The partial splits are
-// ordered by a histogram of their costs in 8-page bins (a unit's cost is taken
-// as its bin's upper edge, within 8 pages), so a candidate costs O(B / 32 +
-// rounds x log bins) per lane. Ties go to the longer split. B <= kMaxSimSeqs
+// ordered by a counting sort of their costs in 8-page bins (a unit's cost is
+// taken as its bin's upper edge, within 8 pages), so a candidate costs
+// O(B / 32 + rounds) per lane. Ties go to the longer split. B <= kMaxSimSeqs
 // (the host enables this only for such batches). Whole block.
 constexpr int kSimWarps = 16;
 constexpr int kMaxSimSeqs = kPlanThreads;
@@ -294,9 +294,10 @@ constexpr int kSimBins = (kMaxPagesPerSplit + (int)kSplitUnitCost) / 8 + 2;
 
 __device__ int32_t choose_split(const int32_t *__restrict__ ctx, int32_t B, int32_t bs, int32_t cap,
                                 int32_t p_lo, int32_t p_hi, int32_t upi, int32_t slots) {
+  static_assert(kSimBins <= 96 && kSimBins * 8 < 32768, "three bins per lane; int16 costs");
   __shared__ int32_t s_pages[kMaxSimSeqs];
-  __shared__ int32_t s_hist[kSimWarps][kSimBins];   // partial splits per cost bin
-  __shared__ int32_t s_above[kSimWarps][kSimBins];  // partial splits in higher bins
+  __shared__ int32_t s_hist[kSimWarps][kSimBins];        // partial splits per cost bin
+  __shared__ int16_t s_sorted[kSimWarps][kMaxSimSeqs];  // partial split costs, highest first
   __shared__ long long s_cost[kMaxSplitCandidates];
   __shared__ int32_t s_maxp, s_choice;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -316,7 +317,7 @@ __device__ int32_t choose_split(const int32_t *__restrict__ ctx, int32_t B, int3
   const int32_t maxp = s_maxp;
   if (warp < kSimWarps) {
     int32_t *hist = s_hist[warp];
-    int32_t *above = s_above[warp];
+    int16_t *sorted = s_sorted[warp];
     for (int32_t k = warp; k < ncand; k += kSimWarps) {
       const int32_t P = p_lo + 8 * k;
       for (int i = lane; i < kSimBins; i += 32) hist[i] = 0;
@@ -340,11 +341,28 @@ __device__ int32_t choose_split(const int32_t *__restrict__ ctx, int32_t B, int3
         parts += __shfl_xor_sync(0xffffffffu, parts, o);
       }
       __syncwarp();
-      if (lane == 0) {  // partial splits in bins above each bin
-        int32_t acc = 0;
-        for (int i = kSimBins - 1; i >= 0; --i) {
-          above[i] = acc;
-          acc += hist[i];
+      {
+        // counting sort: lane l owns bins 3l .. 3l + 2; the partials in higher
+        // bins come first (a suffix scan over the lanes), then each lane writes
+        // its bins' costs in place
+        int32_t h[3], own = 0;
+#pragma unroll
+        for (int e = 0; e < 3; ++e) {
+          const int i = 3 * lane + e;
+          h[e] = i < kSimBins ? hist[i] : 0;
+          own += h[e];
+        }
+        int32_t suf = own;  // inclusive sum over lanes >= this one
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int32_t y = __shfl_down_sync(0xffffffffu, suf, o);
+          if (lane + o < 32) suf += y;
+        }
+        int32_t pos = suf - own;  // partials in the bins of higher lanes
+#pragma unroll
+        for (int e = 2; e >= 0; --e) {
+          for (int32_t x = 0; x < h[e]; ++x) sorted[pos + x] = (int16_t)((3 * lane + e) * 8 + 7);
+          pos += h[e];
         }
       }
       __syncwarp();
@@ -359,20 +377,8 @@ __device__ int32_t choose_split(const int32_t *__restrict__ ctx, int32_t B, int3
           const int32_t w = r * slots + ((r & 1) ? slots - 1 - c : c);
           if (w >= units) continue;
           const int32_t item = w / upi;
-          int32_t cost;
-          if (item < full) {
-            cost = P + (int32_t)kSplitUnitCost;  // full splits are (nearly always) of longer sequences
-          } else {
-            // bin of the (item - full)-th longest partial: the lowest bin with at
-            // most that many partials above it
-            const int32_t j = item - full;
-            int32_t lo_b = 0, hi_b = kSimBins - 1;
-            while (lo_b < hi_b) {
-              const int32_t mid = (lo_b + hi_b) >> 1;
-              if (above[mid] <= j) hi_b = mid; else lo_b = mid + 1;
-            }
-            cost = lo_b * 8 + 7;
-          }
+          // full splits are (nearly always) of longer sequences
+          const int32_t cost = item < full ? P + (int32_t)kSplitUnitCost : (int32_t)sorted[item - full];
           load += cost + kUnitCost;
         }
         worst = max(worst, load);
@@ -380,7 +386,7 @@ __device__ int32_t choose_split(const int32_t *__restrict__ ctx, int32_t B, int3
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) worst = max(worst, __shfl_xor_sync(0xffffffffu, worst, o));
       if (lane == 0) s_cost[k] = worst + (maxp > P ? kMergeCost : 0);
-      __syncwarp();  // hist / above are rewritten for the next candidate
+      __syncwarp();  // hist / sorted are rewritten for the next candidate
     }
   }
   __syncthreads();
@@ -1617,6 +1623,9 @@ SplitRange resolve_split(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t 
   const int64_t u0 = std::max<int64_t>(1, (int64_t)B * Hkv * ((G + rows - 1) / rows));
   const int64_t sms = device_sms();
   if (B > kMaxSimSeqs) return {hi, hi};
+  // no split needed and at least one unit per SM: splitting can only add
+  // units and merges (and the simulation costs plan time), so keep hi
+  if (hi >= max_blocks && u0 >= sms) return {hi, hi};
   const int32_t top = std::min<int32_t>(kMaxPagesPerSplit, (max_blocks + 7) / 8 * 8);
   int64_t lo = ((int64_t)max_blocks * u0 + 16 * sms - 1) / (16 * sms);
   lo = (lo + 7) / 8 * 8;
