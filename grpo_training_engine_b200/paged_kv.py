@@ -172,8 +172,12 @@ def paged_kv_decode(
     block_tables = block_tables.to(torch.int32)
     scale = 1.0 / math.sqrt(head_dim)
 
+    any_finished = False
     for step in range(max_new_tokens):
-        if finished.all():
+        # one host sync per step, as the reference's finished.all() check
+        all_done, any_finished = (
+            torch.stack([finished.all(), finished.any()]).tolist() if step else (False, False))
+        if all_done:
             break
         q, k_new, v_new = qkv_proj_fn(last_tokens)
         if q.ndim != 3 or q.shape[0] != batch_size or q.shape[2] != head_dim or q.shape[1] % num_heads != 0:
@@ -184,9 +188,18 @@ def paged_kv_decode(
         if k_new.stride() != v_new.stride():
             v_new = v_new.contiguous()
             k_new = k_new.contiguous()
-        ops.paged_kv_append(k_new, v_new, k_cache, v_cache, block_tables, context_lens)
-        context_lens = context_lens + (~finished).to(context_lens.dtype)
-        attn_out = ops.paged_attention_decode(q, k_cache, v_cache, block_tables, context_lens, scale=scale)
+        if not any_finished:
+            # every row advances: append at the pre-step length and attend over
+            # one more, in one launch (pkv_append_decode_run)
+            context_lens = context_lens + 1
+            attn_out = ops.paged_attention_decode(q, k_cache, v_cache, block_tables, context_lens, scale=scale,
+                                                  k_new=k_new, v_new=v_new)
+        else:
+            # finished rows write their token past their (unchanged) length, as
+            # the reference does (paged_kv.py:914-938): append, then decode
+            ops.paged_kv_append(k_new, v_new, k_cache, v_cache, block_tables, context_lens)
+            context_lens = context_lens + (~finished).to(context_lens.dtype)
+            attn_out = ops.paged_attention_decode(q, k_cache, v_cache, block_tables, context_lens, scale=scale)
         logits = logits_fn(attn_out)
         if logits.ndim != 2 or logits.shape[0] != batch_size:
             raise ValueError("logits_fn must return [B, vocab] logits.")
