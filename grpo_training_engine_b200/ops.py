@@ -15,6 +15,8 @@ Reference correspondence (src/triton_kernels/paged_kv.py):
 
 from __future__ import annotations
 
+import contextlib
+import functools
 import math
 from dataclasses import dataclass
 from typing import Optional
@@ -22,6 +24,21 @@ from typing import Optional
 import torch
 
 from . import _lib
+
+
+@functools.lru_cache(maxsize=512)
+def _strides(values: tuple) -> object:
+    """ctypes int64 array of a stride tuple, built once per distinct tuple (the
+    library only reads it; the arrays are kept alive by the cache)."""
+    return _lib.i64_array(values)
+
+
+_NULL_CTX = contextlib.nullcontext()
+
+
+def _device_ctx(dev: torch.device):
+    """torch.cuda.device(dev) only when dev is not already the current device."""
+    return _NULL_CTX if dev.index == torch.cuda.current_device() else torch.cuda.device(dev)
 
 _DTYPES = {
     torch.float32: _lib.DTYPE_F32,
@@ -126,14 +143,14 @@ def paged_kv_append(
     bt = _as_i32(block_tables)
     ctx = _as_i32(context_lens)
     lib = _lib.load()
-    with torch.cuda.device(dev):
+    with _device_ctx(dev):
         _lib.check(
             "pkv_append",
             lib.pkv_append(
                 k_new.data_ptr(), v_new.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
                 bt.data_ptr(), ctx.data_ptr(), batch, heads, head_dim, block_size, num_blocks,
-                bt.shape[1], _lib.i64_array(k_new.stride()), _lib.i64_array(k_cache.stride()),
-                _lib.i64_array(bt.stride()), _dtype_code(k_cache, "k_cache"), _status_ptr(status),
+                bt.shape[1], _strides(k_new.stride()), _strides(k_cache.stride()),
+                _strides(bt.stride()), _dtype_code(k_cache, "k_cache"), _status_ptr(status),
                 _stream(dev),
             ),
         )
@@ -175,14 +192,14 @@ def paged_kv_append_prompt(
     sp = None if start_pos is None else _as_i32(start_pos)
     ln = None if lens is None else _as_i32(lens)
     lib = _lib.load()
-    with torch.cuda.device(dev):
+    with _device_ctx(dev):
         _lib.check(
             "pkv_append_prompt",
             lib.pkv_append_prompt(
                 k.data_ptr(), v.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), bt.data_ptr(),
                 _lib.ptr(sp), _lib.ptr(ln), batch, heads, seq_len, head_dim, block_size, num_blocks,
-                bt.shape[1], _lib.i64_array(k.stride()), _lib.i64_array(k_cache.stride()),
-                _lib.i64_array(bt.stride()), _dtype_code(k_cache, "k_cache"), _status_ptr(status),
+                bt.shape[1], _strides(k.stride()), _strides(k_cache.stride()),
+                _strides(bt.stride()), _dtype_code(k_cache, "k_cache"), _status_ptr(status),
                 _stream(dev),
             ),
         )
@@ -213,14 +230,14 @@ def gather_kv(
     k_out = torch.empty((batch, heads, max_tokens, head_dim), dtype=k_cache.dtype, device=dev)
     v_out = torch.empty_like(k_out)
     lib = _lib.load()
-    with torch.cuda.device(dev):
+    with _device_ctx(dev):
         _lib.check(
             "pkv_gather",
             lib.pkv_gather(
                 k_cache.data_ptr(), v_cache.data_ptr(), bt.data_ptr(), ctx.data_ptr(),
                 k_out.data_ptr(), v_out.data_ptr(), batch, heads, head_dim, block_size, num_blocks,
-                bt.shape[1], max_tokens, _lib.i64_array(k_cache.stride()),
-                _lib.i64_array(bt.stride()), _lib.i64_array(k_out.stride()),
+                bt.shape[1], max_tokens, _strides(k_cache.stride()),
+                _strides(bt.stride()), _strides(k_out.stride()),
                 _dtype_code(k_cache, "k_cache"), _status_ptr(status), _stream(dev),
             ),
         )
@@ -311,7 +328,7 @@ def plan_decode(
     if workspace is None or workspace.numel() * workspace.element_size() < need:
         workspace = torch.empty(need, dtype=torch.uint8, device=dev)
     lib = _lib.load()
-    with torch.cuda.device(dev):
+    with _device_ctx(dev):
         _lib.check(
             "pkv_decode_plan",
             lib.pkv_decode_plan(
@@ -424,41 +441,41 @@ def paged_attention_decode(
                 raise ValueError("rope cos / sin must be matching [batch, head_dim] tensors of q's dtype "
                                  "with contiguous rows.")
             _require_cuda(cos, sin)
-            with torch.cuda.device(dev):
+            with _device_ctx(dev):
                 _lib.check(
                     "pkv_rope_append_decode_run",
                     lib.pkv_rope_append_decode_run(
                         q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), cos.data_ptr(), sin.data_ptr(),
                         cos.stride(0), k_cache.data_ptr(), v_cache.data_ptr(), bt.data_ptr(),
                         plan.context_lens.data_ptr(), out.data_ptr(), batch, hq, hkv, head_dim, block_size,
-                        num_blocks, max_blocks, _lib.i64_array(q.stride()), _lib.i64_array(k_new.stride()),
-                        _lib.i64_array(k_cache.stride()), _lib.i64_array(bt.stride()), _lib.i64_array(out.stride()),
+                        num_blocks, max_blocks, _strides(q.stride()), _strides(k_new.stride()),
+                        _strides(k_cache.stride()), _strides(bt.stride()), _strides(out.stride()),
                         _dtype_code(q, "q"), _dtype_code(k_cache, "k_cache"), float(scale), plan.pages_per_split,
                         flags, ws.data_ptr(), ws.numel() * ws.element_size(), _status_ptr(status), _stream(dev),
                     ),
                 )
             return out
-        with torch.cuda.device(dev):
+        with _device_ctx(dev):
             _lib.check(
                 "pkv_append_decode_run",
                 lib.pkv_append_decode_run(
                     q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
                     bt.data_ptr(), plan.context_lens.data_ptr(), out.data_ptr(), batch, hq, hkv, head_dim,
-                    block_size, num_blocks, max_blocks, _lib.i64_array(q.stride()), _lib.i64_array(k_new.stride()),
-                    _lib.i64_array(k_cache.stride()), _lib.i64_array(bt.stride()), _lib.i64_array(out.stride()),
+                    block_size, num_blocks, max_blocks, _strides(q.stride()), _strides(k_new.stride()),
+                    _strides(k_cache.stride()), _strides(bt.stride()), _strides(out.stride()),
                     _dtype_code(q, "q"), _dtype_code(k_cache, "k_cache"), float(scale), plan.pages_per_split,
                     flags, ws.data_ptr(), ws.numel() * ws.element_size(), _status_ptr(status), _stream(dev),
                 ),
             )
         return out
-    with torch.cuda.device(dev):
+    with _device_ctx(dev):
         _lib.check(
             "pkv_decode_run",
             lib.pkv_decode_run(
                 q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), bt.data_ptr(), plan.context_lens.data_ptr(),
                 out.data_ptr(), batch, hq, hkv, head_dim, block_size, num_blocks, max_blocks,
-                _lib.i64_array(q.stride()), _lib.i64_array(k_cache.stride()), _lib.i64_array(bt.stride()),
-                _lib.i64_array(out.stride()), _dtype_code(q, "q"), _dtype_code(k_cache, "k_cache"),
+                _strides(q.stride()), _strides(k_cache.stride()), _strides(bt.stride()),
+                _strides(out.stride()), _dtype_code(q, "q"), _dtype_code(k_cache, "k_cache"),
                 float(scale), plan.pages_per_split, flags, ws.data_ptr(), ws.numel() * ws.element_size(),
                 _status_ptr(status), _stream(dev),
             ),
@@ -491,7 +508,7 @@ def add_rmsnorm(
     dev = _require_cuda(x, weight, residual)
     out = torch.empty_like(x, memory_format=torch.contiguous_format)
     total = torch.empty_like(out) if residual is not None else None
-    with torch.cuda.device(dev):
+    with _device_ctx(dev):
         _lib.check(
             "pkv_add_rmsnorm",
             _lib.load().pkv_add_rmsnorm(
@@ -510,7 +527,7 @@ def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
         raise ValueError("gate and up must be matching [rows, cols] tensors with contiguous rows.")
     dev = _require_cuda(gate, up)
     out = torch.empty(gate.shape, dtype=gate.dtype, device=dev)
-    with torch.cuda.device(dev):
+    with _device_ctx(dev):
         _lib.check(
             "pkv_silu_mul",
             _lib.load().pkv_silu_mul(gate.data_ptr(), up.data_ptr(), out.data_ptr(), gate.shape[0], gate.shape[1],
@@ -555,7 +572,7 @@ def rope_qk(
             raise ValueError("k_out must match k: [rows, heads * head_dim] with contiguous rows.")
         _require_cuda(k_out)
         ko, k_rows = k_out.view(rows, num_kv_heads, head_dim), k_out.stride(0)
-    with torch.cuda.device(dev):
+    with _device_ctx(dev):
         _lib.check(
             "pkv_rope_qk",
             _lib.load().pkv_rope_qk(q.data_ptr(), k.data_ptr(), cos.data_ptr(), sin.data_ptr(), qo.data_ptr(),
@@ -598,7 +615,7 @@ def sample_top_p(
     u = torch.rand(batch, device=dev, dtype=torch.float32, generator=generator)
     out = torch.empty(batch, dtype=torch.int64, device=dev)
     lib = _lib.load()
-    with torch.cuda.device(dev):
+    with _device_ctx(dev):
         _lib.check(
             "pkv_sample_top_p",
             lib.pkv_sample_top_p(logits.data_ptr(), _dtype_code(logits, "logits"), batch, vocab, logits.stride(0),
@@ -616,7 +633,7 @@ def decode_kernel_kind(q: torch.Tensor, k_cache: torch.Tensor, force_generic: bo
     kind = _lib.check(
         "pkv_decode_kernel_kind",
         _lib.load().pkv_decode_kernel_kind(
-            k_cache.data_ptr(), hq, hkv, head_dim, block_size, _lib.i64_array(k_cache.stride()),
+            k_cache.data_ptr(), hq, hkv, head_dim, block_size, _strides(k_cache.stride()),
             _dtype_code(q, "q"), _dtype_code(k_cache, "k_cache"),
             _lib.DECODE_FORCE_GENERIC if force_generic else 0,
         ),
