@@ -15,7 +15,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libpkv.so"
 
-ABI_VERSION = 8  # PKV_ABI_VERSION in include/pkv.h
+ABI_VERSION = 9  # PKV_ABI_VERSION in include/pkv.h
 
 SAMPLE_FORCE_RADIX = 1  # PKV_SAMPLE_FORCE_RADIX
 
@@ -39,6 +39,8 @@ DECODE_FORCE_GENERIC = 1
 DECODE_EXACT_P = 2
 DECODE_OUT_Q_DTYPE = 4  # PKV_DECODE_OUT_Q_DTYPE
 DECODE_TEST_WAIT_TIMEOUT = 1 << 30  # PKV_DECODE_TEST_WAIT_TIMEOUT (tests of the bounded waits only)
+LINEAR_NONE = 0  # PKV_LINEAR_NONE
+LINEAR_SILU_GATE = 1  # PKV_LINEAR_SILU_GATE
 NOALLOC_SCRATCH_BYTES = 32 << 20  # PKV_NOALLOC_SCRATCH_BYTES in include/pkv.h
 
 _i32 = C.c_int32
@@ -99,6 +101,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _i64p, _i64p, _i64p, _i64p, _i32, _i32, C.c_float, _i32, _i32, _vp, _vp],
     ),
     "pkv_decode_kernel_kind": (C.c_int, [_vp, _i32, _i32, _i32, _i32, _i64p, _i32, _i32, _i32]),
+    "pkv_linear": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, C.c_int64, C.c_int64, C.c_int64, _i32,
+                             _i32, _vp, _vp]),
 }
 
 

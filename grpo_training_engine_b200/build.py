@@ -22,7 +22,7 @@ CSRC = PKG_DIR / "csrc"
 INCLUDE = REPO_DIR / "include"
 LIB_PATH = PKG_DIR / "libpkv.so"
 
-SOURCES = ["pkv_copy.cu", "pkv_decode.cu", "pkv_noalloc.cu", "pkv_sample.cu", "pkv_glue.cu"]
+SOURCES = ["pkv_copy.cu", "pkv_decode.cu", "pkv_noalloc.cu", "pkv_sample.cu", "pkv_glue.cu", "pkv_linear.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -586,6 +586,72 @@ def rope_qk(
 # ---------------------------------------------------------------------------
 # sampling
 # ---------------------------------------------------------------------------
+# ---------------------------------------------------------------------------
+# projections of the decode step (tcgen05 GEMM)
+# ---------------------------------------------------------------------------
+def linear_supported(x: torch.Tensor, weight: torch.Tensor) -> bool:
+    """Whether linear() serves these operands: CUDA bf16 / fp16 x and weight of
+    one dtype, in_features a multiple of 64, 16-byte aligned rows with
+    contiguous columns."""
+    return (x.is_cuda and weight.is_cuda and x.dtype == weight.dtype and x.dtype in (torch.bfloat16, torch.float16)
+            and x.ndim == 2 and weight.ndim == 2 and x.shape[1] == weight.shape[1] and x.shape[1] % 64 == 0
+            and x.stride(1) == 1 and weight.stride(1) == 1 and x.stride(0) % 8 == 0 and weight.stride(0) % 8 == 0
+            and x.data_ptr() % 16 == 0 and weight.data_ptr() % 16 == 0)
+
+
+def linear(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    bias: Optional[torch.Tensor] = None,
+    *,
+    out: Optional[torch.Tensor] = None,
+    silu_gate: bool = False,
+    weight_up: Optional[torch.Tensor] = None,
+    status: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """``x @ weight.T (+ bias)`` for the few activation rows of a decode step,
+    on the tcgen05 tensor cores (C ABI pkv_linear): x [rows, K], weight in
+    nn.Linear's [N, K] layout, fp32 accumulation, output in x's dtype.
+
+    silu_gate=True: weight is the gate_proj weight [n, K] and weight_up the
+    up_proj weight (or, without weight_up, weight is the two stacked, [2 n, K]);
+    the result [rows, n] is ``silu(x @ gate.T) * (x @ up.T)`` with the rounding
+    of HF Qwen2MLP (each GEMM output, the activation and the product rounded to
+    the dtype). Rows beyond 128 run as further launches of 128 rows.
+    """
+    if not linear_supported(x, weight):
+        raise ValueError("linear needs CUDA bf16/fp16 x [rows, K] and weight [N, K] of one dtype, K a multiple of "
+                         "64, contiguous 16-byte aligned rows.")
+    dev = _require_cuda(x, weight, bias, out, status, weight_up)
+    rows, k = x.shape
+    if weight_up is not None:
+        if not silu_gate or weight_up.shape != weight.shape or weight_up.stride() != weight.stride() \
+                or weight_up.dtype != weight.dtype or weight_up.data_ptr() % 16 != 0:
+            raise ValueError("weight_up must match weight (shape, strides, dtype) and needs silu_gate.")
+        n = weight.shape[0]
+    else:
+        n = weight.shape[0] // 2 if silu_gate else weight.shape[0]
+    if silu_gate and ((weight_up is None and weight.shape[0] % 2 != 0) or bias is not None):
+        raise ValueError("silu_gate needs gate / up weights (separate, or stacked [2 n, K]) and no bias.")
+    if bias is not None and (bias.dtype != x.dtype or bias.numel() != n or bias.stride(0) != 1):
+        raise ValueError("bias must be a contiguous [N] tensor of x's dtype.")
+    if out is None:
+        out = torch.empty(rows, n, dtype=x.dtype, device=dev)
+    elif out.dtype != x.dtype or tuple(out.shape) != (rows, n) or out.stride(1) != 1:
+        raise ValueError(f"out must be a [rows, {n}] tensor of x's dtype with contiguous rows.")
+    lib = _lib.load()
+    act = _lib.LINEAR_SILU_GATE if silu_gate else _lib.LINEAR_NONE
+    code = _dtype_code(x, "x")
+    with _device_ctx(dev):
+        st = _stream(dev)
+        for r0 in range(0, rows, 128):
+            r = min(128, rows - r0)
+            _lib.check("pkv_linear", lib.pkv_linear(
+                x[r0:].data_ptr(), weight.data_ptr(), _lib.ptr(weight_up), _lib.ptr(bias), out[r0:].data_ptr(), r, n,
+                k, x.stride(0), weight.stride(0), out.stride(0), code, act, _status_ptr(status), st))
+    return out
+
+
 def sample_top_p(
     logits: torch.Tensor,
     temperature: float,

@@ -422,11 +422,23 @@ def paged_kv_decode_model(
             return mod(h)
         return h @ st[0] if st[1] is None else torch.addmm(st[1], h, st[0])
 
+    # The MLP's projections run on the tcgen05 projection kernel (ops.linear)
+    # straight from the modules' own weights: gate and up with the SiLU gate in
+    # one launch, then down. Plain bias-free bf16 nn.Linear modules with
+    # in_features a multiple of 64 (every Qwen2 MLP); no copies are made.
+    def _tc_mlp_ok(mlp) -> bool:
+        mods = [getattr(mlp, n, None) for n in ("gate_proj", "up_proj", "down_proj")]
+        return all(type(m) is torch.nn.Linear and m.bias is None and m.weight.dtype == torch.bfloat16
+                   and m.weight.is_cuda and m.weight.is_contiguous() and m.in_features % 64 == 0
+                   and m.weight.data_ptr() % 16 == 0 for m in mods) \
+            and mods[0].out_features % 64 == 0 and mods[0].weight.shape == mods[1].weight.shape
+    tc_mlp = [bool(fused_glue and silu_mlp and _tc_mlp_ok(layer.mlp)) for layer in layers]
+
     # the copies need as much memory as those weights; without twice that free
     # (the trainer may hold most of the GPU) the modules are called as they are
-    proj_bytes = sum(m.weight.numel() * m.weight.element_size() for layer in layers
+    proj_bytes = sum(m.weight.numel() * m.weight.element_size() for i, layer in enumerate(layers)
                      for owner, names in ((layer.self_attn, ("q_proj", "k_proj", "v_proj", "o_proj")),
-                                          (layer.mlp, ("gate_proj", "up_proj", "down_proj")))
+                                          (layer.mlp, () if tc_mlp[i] else ("gate_proj", "up_proj", "down_proj")))
                      for m in (getattr(owner, n, None) for n in names)
                      if isinstance(getattr(m, "weight", None), torch.Tensor)) if fused_glue else 0
     if fused_glue and device.type == "cuda" and torch.cuda.mem_get_info(device)[0] < 2 * proj_bytes:
@@ -436,9 +448,10 @@ def paged_kv_decode_model(
     qkv_stack = [_stack((layer.self_attn.q_proj, layer.self_attn.k_proj, layer.self_attn.v_proj))
                  if fused_glue_copies else None for layer in layers]
     o_stack = [_stack((layer.self_attn.o_proj,)) if fused_glue_copies else None for layer in layers]
-    gate_up_stack = [_stack((layer.mlp.gate_proj, layer.mlp.up_proj)) if fused_glue_copies and silu_mlp else None
-                     for layer in layers]
-    down_stack = [_stack((layer.mlp.down_proj,)) if fused_glue_copies and silu_mlp else None for layer in layers]
+    gate_up_stack = [_stack((layer.mlp.gate_proj, layer.mlp.up_proj))
+                     if fused_glue_copies and silu_mlp and not tc_mlp[i] else None for i, layer in enumerate(layers)]
+    down_stack = [_stack((layer.mlp.down_proj,)) if fused_glue_copies and silu_mlp and not tc_mlp[i] else None
+                  for i, layer in enumerate(layers)]
     head_stack = _stack((lm_head,)) if fused_glue_copies else None
     q_cols, kv_cols = num_heads * head_dim, num_kv_heads * head_dim
     # With stacked q / k / v on the tensor-core decode, RoPE runs inside the
@@ -459,6 +472,9 @@ def paged_kv_decode_model(
         mlp = layer.mlp
         if not silu_mlp:
             return mlp(h)
+        if tc_mlp[layer_idx] and ops.linear_supported(h, mlp.gate_proj.weight):
+            act = ops.linear(h, mlp.gate_proj.weight, silu_gate=True, weight_up=mlp.up_proj.weight)
+            return ops.linear(act, mlp.down_proj.weight)
         st = gate_up_stack[layer_idx]
         if st is None:
             return _linear(down_stack[layer_idx], mlp.down_proj, ops.silu_mul(mlp.gate_proj(h), mlp.up_proj(h)))

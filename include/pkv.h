@@ -37,9 +37,9 @@
 extern "C" {
 #endif
 
-#define PKV_ABI_VERSION 8  /* 2: pkv_append_decode_run, 3: pkv_sample_top_p, 4: rmsnorm, rope, 5: silu_mul,
+#define PKV_ABI_VERSION 9  /* 2: pkv_append_decode_run, 3: pkv_sample_top_p, 4: rmsnorm, rope, 5: silu_mul,
                               6: pkv_sample_top_p flags, 7: pkv_rope_qk output strides,
-                              8: pkv_rope_append_decode_run */
+                              8: pkv_rope_append_decode_run, 9: pkv_linear */
 
 /* Element types. The reference stores the cache in bfloat16
  * (paged_kv.py:409-410, 629-633); float32 is accepted because the reference
@@ -358,6 +358,39 @@ int pkv_decode_noalloc(const void *q, const void *k_cache, const void *v_cache,
                        int32_t q_dtype, int32_t kv_dtype, float scale,
                        int32_t pages_per_split, int32_t flags, int32_t *status,
                        void *stream);
+
+/*
+ * pkv_linear — one projection of a rollout decode step on the tcgen05 tensor
+ * cores: out[r, j] = sum_k x[r, k] * W[j, k] (+ bias[j]) for r < rows <= 128,
+ * j < n, with fp32 accumulation and the result rounded to the 16-bit dtype of
+ * x, W and out (bf16 or fp16, all the same). W has nn.Linear's layout
+ * [out_features, in_features] (row stride w_stride elements), so the weights
+ * are read as they lie. Replaces the nn.Linear calls of the reference's fused
+ * decode step: q/k/v (src/triton_kernels/fused_ops.py:198-219), o_proj
+ * (paged_kv.py:789), gate/up and down (fused_ops.py:184-195) and the LM head
+ * (fused_ops.py:231).
+ *
+ * act = PKV_LINEAR_SILU_GATE: W holds the gate rows [n, k] and the up rows
+ * come from w_up ([n, k], same row stride), or, with w_up NULL, W is the gate
+ * rows stacked over the up rows ([2 n, k]); out[r, j] = T(T(silu(g)) * u) with
+ * g = T(x . gate[j]) and u = T(x . up[j]) — the MLP's act_fn(gate_proj(x)) *
+ * up_proj(x) rounded as HF Qwen2MLP rounds it (the reference's fused_silu_mul,
+ * fused_ops.py:79-103); n a multiple of 64, no bias. w_up must be NULL for
+ * PKV_LINEAR_NONE.
+ *
+ * Requirements: in_features a multiple of 64; x, W and out 16-byte aligned
+ * with row strides that are multiples of 8 elements. No workspace: the split-K
+ * partials stay on chip (the splits of a column tile are one thread-block
+ * cluster that adds them in split order, so results are deterministic).
+ */
+enum {
+    PKV_LINEAR_NONE = 0,
+    PKV_LINEAR_SILU_GATE = 1
+};
+
+int pkv_linear(const void *x, const void *w, const void *w_up, const void *bias, void *out,
+               int32_t rows, int32_t n, int32_t k, int64_t x_stride, int64_t w_stride,
+               int64_t out_stride, int32_t dtype, int32_t act, int32_t *status, void *stream);
 
 /*
  * Which decode kernel pkv_decode_run would launch for these arguments:
