@@ -15,7 +15,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libpkv.so"
 
-ABI_VERSION = 9  # PKV_ABI_VERSION in include/pkv.h
+ABI_VERSION = 10  # PKV_ABI_VERSION in include/pkv.h
 
 SAMPLE_FORCE_RADIX = 1  # PKV_SAMPLE_FORCE_RADIX
 
@@ -41,6 +41,7 @@ DECODE_OUT_Q_DTYPE = 4  # PKV_DECODE_OUT_Q_DTYPE
 DECODE_TEST_WAIT_TIMEOUT = 1 << 30  # PKV_DECODE_TEST_WAIT_TIMEOUT (tests of the bounded waits only)
 LINEAR_NONE = 0  # PKV_LINEAR_NONE
 LINEAR_SILU_GATE = 1  # PKV_LINEAR_SILU_GATE
+LINEAR_WEIGHTS_STATIC = 0x100  # PKV_LINEAR_WEIGHTS_STATIC (flag OR'd into act)
 NOALLOC_SCRATCH_BYTES = 32 << 20  # PKV_NOALLOC_SCRATCH_BYTES in include/pkv.h
 
 _i32 = C.c_int32

@@ -54,6 +54,11 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(const T *x, c
   using V = Vec16<T>;
   constexpr int kV = V::kV;
   __shared__ float red[kNormThreads / 32];
+  // Programmatic dependent launch: the next kernel (a projection) may place
+  // its CTAs and start its weight stream now; this grid waits for the
+  // previous one before its first load.
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int64_t b = blockIdx.x;
   const int tid = threadIdx.x;
   float v[kNormVecs][kV];
@@ -178,24 +183,38 @@ extern "C" int pkv_add_rmsnorm(const void *x, const void *residual, const void *
   const int64_t strides[] = {x_stride, residual ? residual_stride : 0, sum_out ? sum_stride : 0, out_stride};
   for (int64_t st : strides)
     if ((st * es) % 16 != 0) return PKV_ERR_ALIGNMENT;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)rows);
+  cfg.blockDim = dim3(kNormThreads);
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
   switch (dtype) {
     case PKV_DTYPE_BF16:
-      add_rmsnorm_kernel<__nv_bfloat16><<<rows, kNormThreads, 0, st>>>(
-          (const __nv_bfloat16 *)x, (const __nv_bfloat16 *)residual, (const __nv_bfloat16 *)weight,
-          (__nv_bfloat16 *)sum_out, (__nv_bfloat16 *)out, hidden, x_stride, residual_stride, sum_stride,
-          out_stride, eps);
+      e = cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel<__nv_bfloat16>, (const __nv_bfloat16 *)x,
+                             (const __nv_bfloat16 *)residual, (const __nv_bfloat16 *)weight,
+                             (__nv_bfloat16 *)sum_out, (__nv_bfloat16 *)out, (int)hidden, x_stride,
+                             residual_stride, sum_stride, out_stride, eps);
       break;
     case PKV_DTYPE_F16:
-      add_rmsnorm_kernel<__half><<<rows, kNormThreads, 0, st>>>(
-          (const __half *)x, (const __half *)residual, (const __half *)weight, (__half *)sum_out,
-          (__half *)out, hidden, x_stride, residual_stride, sum_stride, out_stride, eps);
+      e = cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel<__half>, (const __half *)x, (const __half *)residual,
+                             (const __half *)weight, (__half *)sum_out, (__half *)out, (int)hidden, x_stride,
+                             residual_stride, sum_stride, out_stride, eps);
       break;
     default:
-      add_rmsnorm_kernel<float><<<rows, kNormThreads, 0, st>>>(
-          (const float *)x, (const float *)residual, (const float *)weight, (float *)sum_out, (float *)out,
-          hidden, x_stride, residual_stride, sum_stride, out_stride, eps);
+      e = cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel<float>, (const float *)x, (const float *)residual,
+                             (const float *)weight, (float *)sum_out, (float *)out, (int)hidden, x_stride,
+                             residual_stride, sum_stride, out_stride, eps);
       break;
+  }
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error_detail("pkv_add_rmsnorm: %s", cudaGetErrorString(e));
+    return PKV_ERR_CUDA;
   }
   return check_launch("pkv_add_rmsnorm");
 }

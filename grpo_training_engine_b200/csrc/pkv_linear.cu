@@ -65,6 +65,7 @@ struct LinArgs {
   int64_t out_stride;
   int32_t rows, n, kblocks, tiles, splits;
   int32_t up_row;      // SiLU gate: first up row in the up tensor map (n when stacked under gate)
+  int32_t static_w;    // W / w_up are written by no kernel in flight: stream them before the dependency wait
   uint32_t max_polls;
 };
 
@@ -77,7 +78,7 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
 }
 
 // 2-D tiled TMA load of box (x, y) of the tensor map into shared memory,
-// completing on `bar` (no multicast).
+// completing on `bar`; this CTA's own shared memory is the only destination.
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int32_t x, int32_t y,
                                             uint64_t *bar) {
   asm volatile(
@@ -296,10 +297,24 @@ linear_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CU
   const int kb1 = (int)((int64_t)(split + 1) * a.kblocks / a.splits);
   const int nkb = kb1 - kb0;  // >= 1: the host keeps splits <= kblocks
 
+  // W tiles of K block i (the gate and up rows for the SiLU gate) into stage s
+  auto load_w = [&](int s, int i) {
+    const int kx = (kb0 + i) * kLinBK;
+    if constexpr (ACT == kActSiluGate) {
+      tma_load_2d(sb + s * L::kB, &tw, kx, n0, &full[s]);                          // gate rows
+      tma_load_2d(sb + s * L::kB + L::kB / 2, &tu, kx, a.up_row + n0, &full[s]);  // up rows
+    } else {
+      tma_load_2d(sb + s * L::kB, &tw, kx, n0, &full[s]);
+    }
+  };
+  // stages whose W tiles are issued before the dependency wait
+  const int pre = a.static_w ? (nkb < S ? nkb : S) : 0;
+
   // Programmatic dependent launch: the next kernel in the stream may place its
   // CTAs on SMs this grid frees, and it waits (griddepcontrol.wait) for this
   // grid to complete before it reads memory; this grid likewise initialises
-  // its barriers and TMEM before waiting for the previous kernel.
+  // its barriers and TMEM (and, with static weights, starts its weight
+  // stream) before waiting for the previous kernel.
   asm volatile("griddepcontrol.launch_dependents;");
   if (threadIdx.x == 32) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tx)) : "memory");
@@ -315,6 +330,12 @@ linear_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CU
     // make the initialised barriers visible to the async proxy (TMA, tcgen05)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    // the first stages' weights: each stage's barrier expects its x tile too,
+    // which is loaded after the wait
+    for (int i = 0; i < pre; ++i) {
+      mbar_expect_tx(&full[i], L::kA + L::kB);
+      load_w(i, i);
+    }
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -340,15 +361,11 @@ linear_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CU
           flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
           break;
         }
-        const int kx = (kb0 + i) * kLinBK;
-        mbar_expect_tx(&full[s], L::kA + L::kB);
-        tma_load_2d(sa + s * L::kA, &tx, kx, 0, &full[s]);
-        if constexpr (ACT == kActSiluGate) {
-          tma_load_2d(sb + s * L::kB, &tw, kx, n0, &full[s]);                          // gate rows
-          tma_load_2d(sb + s * L::kB + L::kB / 2, &tu, kx, a.up_row + n0, &full[s]);  // up rows
-        } else {
-          tma_load_2d(sb + s * L::kB, &tw, kx, n0, &full[s]);
+        if (i >= pre) {  // (stages below `pre` have their W tiles and byte count already)
+          mbar_expect_tx(&full[s], L::kA + L::kB);
+          load_w(s, i);
         }
+        tma_load_2d(sa + s * L::kA, &tx, (kb0 + i) * kLinBK, 0, &full[s]);
         ++issued;
       }
       // the last load of each stage has landed before the CTA (and its shared
@@ -607,7 +624,9 @@ extern "C" int pkv_linear(const void *x, const void *w, const void *w_up, const 
     set_error_detail("pkv_linear: x, W and out must be bf16 or fp16");
     return PKV_ERR_UNSUPPORTED;
   }
-  if (act != 0 && act != 1) {
+  const bool static_w = (act & PKV_LINEAR_WEIGHTS_STATIC) != 0;
+  act &= ~PKV_LINEAR_WEIGHTS_STATIC;
+  if (act != PKV_LINEAR_NONE && act != PKV_LINEAR_SILU_GATE) {
     set_error_detail("pkv_linear: unknown activation %d", act);
     return PKV_ERR_INVALID_ARG;
   }
@@ -662,6 +681,7 @@ extern "C" int pkv_linear(const void *x, const void *w, const void *w_up, const 
   a.tiles = p.tiles;
   a.splits = p.splits;
   a.up_row = w_up != nullptr ? 0 : n;
+  a.static_w = static_w ? 1 : 0;
   a.max_polls = kMaxPolls;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   return bf16 ? lin_dispatch<__nv_bfloat16>(tx, tw, tu, a, p.bn, act, st)

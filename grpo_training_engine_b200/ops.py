@@ -608,6 +608,7 @@ def linear(
     silu_gate: bool = False,
     weight_up: Optional[torch.Tensor] = None,
     status: Optional[torch.Tensor] = None,
+    weights_static: bool = False,
 ) -> torch.Tensor:
     """``x @ weight.T (+ bias)`` for the few activation rows of a decode step,
     on the tcgen05 tensor cores (C ABI pkv_linear): x [rows, K], weight in
@@ -618,6 +619,10 @@ def linear(
     the result [rows, n] is ``silu(x @ gate.T) * (x @ up.T)`` with the rounding
     of HF Qwen2MLP (each GEMM output, the activation and the product rounded to
     the dtype). Rows beyond 128 run as further launches of 128 rows.
+
+    weights_static=True promises that no kernel still queued on the stream
+    writes weight / weight_up (model weights during generation): the launch
+    then streams its first weight tiles while the previous kernel finishes.
     """
     if not linear_supported(x, weight):
         raise ValueError("linear needs CUDA bf16/fp16 x [rows, K] and weight [N, K] of one dtype, K a multiple of "
@@ -641,6 +646,8 @@ def linear(
         raise ValueError(f"out must be a [rows, {n}] tensor of x's dtype with contiguous rows.")
     lib = _lib.load()
     act = _lib.LINEAR_SILU_GATE if silu_gate else _lib.LINEAR_NONE
+    if weights_static:
+        act |= _lib.LINEAR_WEIGHTS_STATIC
     code = _dtype_code(x, "x")
     with _device_ctx(dev):
         st = _stream(dev)

@@ -424,13 +424,21 @@ def paged_kv_decode_model(
 
     # The MLP's projections run on the tcgen05 projection kernel (ops.linear)
     # straight from the modules' own weights: gate and up with the SiLU gate in
-    # one launch, then down. Plain bias-free bf16 nn.Linear modules with
-    # in_features a multiple of 64 (every Qwen2 MLP); no copies are made.
+    # one launch, then down. Plain bias-free 16-bit nn.Linear modules with
+    # in_features a multiple of 64 (every Qwen2 MLP); no copies are made. The
+    # weights do not change during generation, so each launch starts
+    # streaming them while the previous kernel finishes (weights_static).
+    # q / k / v, o_proj and the LM head stay on cuBLAS: on pkv_linear the
+    # first two made the 1.5B rollout step ~4% slower (their ~6 MB of weights
+    # take less time than each CTA's re-read of the activation rows and the
+    # split-K reduction), and the LM head's 150k columns are ~4 waves of
+    # 256-column tiles whose short last wave costs more than cuBLAS's schedule.
     def _tc_mlp_ok(mlp) -> bool:
         mods = [getattr(mlp, n, None) for n in ("gate_proj", "up_proj", "down_proj")]
-        return all(type(m) is torch.nn.Linear and m.bias is None and m.weight.dtype == torch.bfloat16
-                   and m.weight.is_cuda and m.weight.is_contiguous() and m.in_features % 64 == 0
-                   and m.weight.data_ptr() % 16 == 0 for m in mods) \
+        return all(type(m) is torch.nn.Linear and m.bias is None and m.weight.dtype == embeddings.weight.dtype
+                   and m.weight.dtype in (torch.bfloat16, torch.float16) and m.weight.is_cuda
+                   and m.weight.is_contiguous() and m.in_features % 64 == 0 and m.weight.data_ptr() % 16 == 0
+                   for m in mods) \
             and mods[0].out_features % 64 == 0 and mods[0].weight.shape == mods[1].weight.shape
     tc_mlp = [bool(fused_glue and silu_mlp and _tc_mlp_ok(layer.mlp)) for layer in layers]
 
@@ -473,8 +481,9 @@ def paged_kv_decode_model(
         if not silu_mlp:
             return mlp(h)
         if tc_mlp[layer_idx] and ops.linear_supported(h, mlp.gate_proj.weight):
-            act = ops.linear(h, mlp.gate_proj.weight, silu_gate=True, weight_up=mlp.up_proj.weight)
-            return ops.linear(act, mlp.down_proj.weight)
+            act = ops.linear(h, mlp.gate_proj.weight, silu_gate=True, weight_up=mlp.up_proj.weight,
+                             weights_static=True)
+            return ops.linear(act, mlp.down_proj.weight, weights_static=True)
         st = gate_up_stack[layer_idx]
         if st is None:
             return _linear(down_stack[layer_idx], mlp.down_proj, ops.silu_mul(mlp.gate_proj(h), mlp.up_proj(h)))

@@ -37,9 +37,10 @@
 extern "C" {
 #endif
 
-#define PKV_ABI_VERSION 9  /* 2: pkv_append_decode_run, 3: pkv_sample_top_p, 4: rmsnorm, rope, 5: silu_mul,
+#define PKV_ABI_VERSION 10 /* 2: pkv_append_decode_run, 3: pkv_sample_top_p, 4: rmsnorm, rope, 5: silu_mul,
                               6: pkv_sample_top_p flags, 7: pkv_rope_qk output strides,
-                              8: pkv_rope_append_decode_run, 9: pkv_linear */
+                              8: pkv_rope_append_decode_run, 9: pkv_linear,
+                              10: PKV_LINEAR_WEIGHTS_STATIC */
 
 /* Element types. The reference stores the cache in bfloat16
  * (paged_kv.py:409-410, 629-633); float32 is accepted because the reference
@@ -378,6 +379,14 @@ int pkv_decode_noalloc(const void *q, const void *k_cache, const void *v_cache,
  * fused_ops.py:79-103); n a multiple of 64, no bias. w_up must be NULL for
  * PKV_LINEAR_NONE.
  *
+ * act | PKV_LINEAR_WEIGHTS_STATIC: the caller guarantees that no kernel still
+ * in flight in `stream` writes W or w_up (model weights during generation).
+ * The launch is a programmatic dependent launch either way; with this flag
+ * each CTA starts streaming its first W tiles into shared memory before it
+ * waits for the previous kernel in the stream, so the weight stream overlaps
+ * that kernel's tail and this launch's own ramp. x, the bias and out are
+ * touched only after the wait.
+ *
  * Requirements: in_features a multiple of 64; x, W and out 16-byte aligned
  * with row strides that are multiples of 8 elements. No workspace: the split-K
  * partials stay on chip (the splits of a column tile are one thread-block
@@ -385,7 +394,8 @@ int pkv_decode_noalloc(const void *q, const void *k_cache, const void *v_cache,
  */
 enum {
     PKV_LINEAR_NONE = 0,
-    PKV_LINEAR_SILU_GATE = 1
+    PKV_LINEAR_SILU_GATE = 1,
+    PKV_LINEAR_WEIGHTS_STATIC = 0x100  /* flag, OR'd into act */
 };
 
 int pkv_linear(const void *x, const void *w, const void *w_up, const void *bias, void *out,

@@ -22,7 +22,7 @@ def _declared() -> set[str]:
 
 def test_library_loads():
     lib = _lib.load()
-    assert lib.pkv_abi_version() == _lib.ABI_VERSION == 9
+    assert lib.pkv_abi_version() == _lib.ABI_VERSION == 10
 
 
 def test_every_declared_symbol_is_exported():

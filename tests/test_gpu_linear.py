@@ -107,3 +107,54 @@ def test_linear_rejects_what_it_cannot_serve():
     assert not ops.linear_supported(x, w)
     with pytest.raises(ValueError):
         ops.linear(x, w)
+
+
+@pytest.mark.parametrize("shape", [(128, 2048, 1536, True), (128, 1536, 8960, False), (37, 1536, 1536, False),
+                                   (128, 151936, 1536, False)],
+                         ids=lambda s: f"r{s[0]}n{s[1]}k{s[2]}{'b' if s[3] else ''}")
+def test_linear_static_weights_same_bits(shape):
+    """weights_static only moves the first weight tiles before the dependency
+    wait: the result is bit-identical."""
+    rows, n, k, bias = shape
+    x, w, b = _operands(11 + n, rows, n, k, torch.bfloat16, bias)
+    plain = ops.linear(x, w, b)
+    static = ops.linear(x, w, b, weights_static=True)
+    torch.cuda.synchronize()
+    assert torch.equal(plain, static)
+
+
+def test_linear_static_weights_reads_x_after_the_previous_kernel():
+    """x is rewritten in place by the kernel just before each launch (and by
+    the previous projection in a chain): a launch that read x before its
+    dependency wait would see the old values."""
+    k, n = 1536, 2048
+    g = torch.Generator(device=DEV).manual_seed(5)
+    x0 = torch.randn(128, k, device=DEV, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, device=DEV, generator=g) / k ** 0.5).to(torch.bfloat16)
+    xbuf = torch.empty_like(x0)
+    outs = []
+    for i in range(6):
+        xbuf.copy_(x0 * (i + 1))  # the previous kernel in the stream writes x
+        outs.append(ops.linear(xbuf, w, weights_static=True))
+    torch.cuda.synchronize()
+    for i, o in enumerate(outs):
+        assert torch.equal(o, ops.linear((x0 * (i + 1)).contiguous(), w)), i
+    # rmsnorm -> gate/up (SiLU) -> down, each consuming the previous launch's output
+    inter = 8960
+    gate = (torch.randn(inter, k, device=DEV, generator=g) / k ** 0.5).to(torch.bfloat16)
+    up = (torch.randn(inter, k, device=DEV, generator=g) / k ** 0.5).to(torch.bfloat16)
+    down = (torch.randn(k, inter, device=DEV, generator=g) / inter ** 0.5).to(torch.bfloat16)
+    nw = (1 + 0.1 * torch.randn(k, device=DEV, generator=g)).to(torch.bfloat16)
+    res = torch.randn(128, k, device=DEV, generator=g).to(torch.bfloat16)
+    chained = []
+    for i in range(3):
+        h, _ = ops.add_rmsnorm(x0 * (i + 1), nw, 1e-6, residual=res)
+        a = ops.linear(h, gate, silu_gate=True, weight_up=up, weights_static=True)
+        chained.append(ops.linear(a, down, weights_static=True))
+    torch.cuda.synchronize()
+    for i, o in enumerate(chained):
+        h, _ = ops.add_rmsnorm(x0 * (i + 1), nw, 1e-6, residual=res)
+        torch.cuda.synchronize()
+        a = ops.linear(h, gate, silu_gate=True, weight_up=up)
+        torch.cuda.synchronize()
+        assert torch.equal(o, ops.linear(a, down)), i
