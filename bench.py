@@ -362,10 +362,11 @@ def run_ours(args, rank, world, local):
             if args.separate_append:
                 pkv.paged_attention_decode(wl.q[layer], kc, vc, wl.block_tables, wl.ctx, out=wl.out[layer],
                                            plan=plan, exact=args.exact)
-            else:  # one launch: append the token at ctx - 1 and attend over ctx
+            else:  # one launch: append the token at ctx - 1 and attend over ctx; every layer after the
+                # first follows the previous layer's decode launch and may schedule its pages before it ends
                 pkv.paged_attention_decode(wl.q[layer], kc, vc, wl.block_tables, wl.ctx, out=wl.out[layer],
                                            plan=plan, exact=args.exact, k_new=wl.k_new[layer],
-                                           v_new=wl.v_new[layer])
+                                           v_new=wl.v_new[layer], early_start=layer > 0)
             if ev_pairs is not None and layer == L - 1:
                 ev_pairs[0][1].record()
         return plan
@@ -463,7 +464,8 @@ def run_ours(args, rank, world, local):
             "shard_of": args.shard_of or None,
             "run": {
                 "pages_per_split": chosen_pps,
-                "step": ("1 plan per step, then per layer one launch that appends the token and decodes"
+                "step": ("1 plan per step, then per layer one launch that appends the token and decodes (layers "
+                         "after the first with early start: pages scheduled before the previous launch ends)"
                          if not args.separate_append else "1 plan per step, then per layer append + decode launches"),
                 "launch": (f"the {args.steps} timed steps captured as one CUDA graph, replayed once (after "
                            f"{args.warmup} eager warm-up steps and one untimed replay)" if args.graph else
@@ -602,7 +604,8 @@ def run_e2e(args, wl, world, device):
                                            exact=args.exact)
             else:
                 pkv.paged_attention_decode(q_d[layer], kc, vc, wl.block_tables, ctx, out=out_d[layer], plan=plan,
-                                           exact=args.exact, k_new=kn_d[layer], v_new=vn_d[layer])
+                                           exact=args.exact, k_new=kn_d[layer], v_new=vn_d[layer],
+                                           early_start=layer > 0)
             done[layer].record(comp)
             with torch.cuda.stream(back):
                 back.wait_event(done[layer])

@@ -38,6 +38,7 @@ DEV_WAIT_TIMEOUT = 4
 DECODE_FORCE_GENERIC = 1
 DECODE_EXACT_P = 2
 DECODE_OUT_Q_DTYPE = 4  # PKV_DECODE_OUT_Q_DTYPE
+DECODE_EARLY_START = 8  # PKV_DECODE_EARLY_START
 DECODE_TEST_WAIT_TIMEOUT = 1 << 30  # PKV_DECODE_TEST_WAIT_TIMEOUT (tests of the bounded waits only)
 LINEAR_NONE = 0  # PKV_LINEAR_NONE
 LINEAR_SILU_GATE = 1  # PKV_LINEAR_SILU_GATE

@@ -160,6 +160,11 @@ struct DecodeArgs {
   // only): CTA 0's producer never publishes consumer warp 0's first element
   uint32_t max_polls, max_tries;
   int32_t withhold;
+  // PKV_DECODE_EARLY_START (tensor-core kernel): the plan, block tables,
+  // context lengths and caches are not written by the previous kernel in the
+  // stream, so the first unit's pages are scheduled and loaded before the
+  // dependency wait
+  int32_t early;
 };
 
 struct Unit {
@@ -848,10 +853,17 @@ decode_tc_kernel(DecodeArgs a) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int MD = L::MD, QS = L::QS;
   static_assert(NW * MD <= (NW + 1) * 32 && QS <= (NW + 1) * 32, "one thread per mbarrier");
-  // Programmatic dependent launch: the next launch in the stream may place its
-  // CTAs on SMs this grid frees; each of its threads waits (griddepcontrol.wait
-  // below) for this grid to complete before it reads global memory.
-  asm volatile("griddepcontrol.launch_dependents;");
+  // Programmatic dependent launch. Each thread first waits for the previous
+  // kernel in the stream (griddepcontrol.wait: it is complete and its writes
+  // are visible) and only then lets the next launch place its CTAs on the SMs
+  // this grid frees. A launch queued behind this one therefore finds every
+  // kernel before this one complete, which is what PKV_DECODE_EARLY_START on
+  // the next layer's launch relies on.
+  auto dep_wait = [] {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+  };
+  const bool early = a.early != 0;
   if (tid < NW * MD) {
     mbar_init(&full[tid], 1);
     mbar_init(&empty[tid], 1);
@@ -863,14 +875,17 @@ decode_tc_kernel(DecodeArgs a) {
   if (tid == 0) mbar_init(group, NW);
   fence_mbar_init();
   __syncthreads();
-  // Only shared memory was touched so far. From here on the previous kernel in
-  // the stream (which may have written q, the new rows, the caches or the
-  // plan) is complete and its writes are visible.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-
-  const int32_t total = a.hdr[0];
+  // Only shared memory was touched so far. Past dep_wait() the previous
+  // kernel in the stream (which may have written q, the new rows, the caches
+  // or the plan) is complete and its writes are visible. With early start the
+  // producer reads the plan and the first unit's block-table entries and
+  // publishes its pages, and each consumer warp issues its first page, before
+  // waiting; q, the new rows, RoPE's cos / sin, the schedule counters and
+  // every global write stay behind the wait.
+  if (!early) dep_wait();
 
   if (warp == NW) {
+    const int32_t total = a.hdr[0];
     const int32_t P = a.hdr[1];  // the plan's split length
     // =========================== producer warp ===========================
     // Schedule: the plan numbers units longest first. CTA c takes unit c in
@@ -901,19 +916,25 @@ decode_tc_kernel(DecodeArgs a) {
     constexpr int kRowChunks = D / 8;    // 16-byte chunks of one K or V row
     constexpr int kQVec = kTcRows * D * 2 / 16;  // 16-byte vectors of a query block
     constexpr int kQPerLane = (kQVec + 31) / 32;
-    auto load_next = [&](int32_t w, int4 d) {
+    // plan-side loads of a unit: its partial-result row and block-table entries
+    auto load_bt = [&](int32_t w, int4 d) {
       Unit u = unit_from(a, P, w, d);
       const int32_t np = u.p_end - u.p_begin;
       srow = (w < total && u.nsplit > 1) ? a.seq_off[u.b] + u.s : 0;
-      if (a.kn != nullptr && w < total && u.s == u.nsplit - 1 && u.ctx > 0 && lane < 2 * kRowChunks) {
-        const int which = lane / kRowChunks, cc = lane % kRowChunks;
-        const uint8_t *src = reinterpret_cast<const uint8_t *>(which ? a.vn : a.kn);
-        nkv = *reinterpret_cast<const uint4 *>(src + (u.b * a.n0 + (int64_t)u.kvh * a.n1) * 2 + 16 * cc);
-      }
 #pragma unroll
       for (int i = 0; i < kBtRegs; ++i) {
         const int32_t pi = lane + 32 * i;
         btr[i] = (w < total && pi < np) ? a.bt[u.b * a.bt0 + (int64_t)(u.p_begin + pi) * a.bt1] : -1;
+      }
+    };
+    // input-side loads (what the previous kernel may have written): the new
+    // K / V rows, RoPE's cos / sin and the query rows
+    auto load_in = [&](int32_t w, int4 d) {
+      Unit u = unit_from(a, P, w, d);
+      if (a.kn != nullptr && w < total && u.s == u.nsplit - 1 && u.ctx > 0 && lane < 2 * kRowChunks) {
+        const int which = lane / kRowChunks, cc = lane % kRowChunks;
+        const uint8_t *src = reinterpret_cast<const uint8_t *>(which ? a.vn : a.kn);
+        nkv = *reinterpret_cast<const uint4 *>(src + (u.b * a.n0 + (int64_t)u.kvh * a.n1) * 2 + 16 * cc);
       }
       if (kRope && a.rcos != nullptr && w < total) {
         const int64_t off = (u.b * a.rcs + 8 * (lane % kRowChunks)) * 2;
@@ -943,6 +964,10 @@ decode_tc_kernel(DecodeArgs a) {
         qr[i] = x;
       }
     };
+    auto load_next = [&](int32_t w, int4 d) {
+      load_bt(w, d);
+      load_in(w, d);
+    };
     const int32_t c = (int32_t)blockIdx.x;
     // the descriptors of rounds 0 and 1 are loaded together with the unit
     // count instead of after it (indices clamped into the item array; a
@@ -963,12 +988,17 @@ decode_tc_kernel(DecodeArgs a) {
       return w < total ? (int32_t)w : total;
     };
     int32_t fetched = 0;  // lane 0: the outstanding claim
-    if (lane == 0 && R <= 2) fetched = atomicAdd(&a.sched[0], 1);  // round 2 is counted
     int32_t round = 0;
     int32_t w1 = unit_at(0), w2 = unit_at(1);
     int4 d1 = w1 < total ? r0 : none;
     int4 d2 = w2 < total ? r1 : none;
-    load_next(w1, d1);
+    bool waited = !early;  // past dep_wait()
+    if (waited) {
+      if (lane == 0 && R <= 2) fetched = atomicAdd(&a.sched[0], 1);  // round 2 is counted
+      load_next(w1, d1);
+    } else {
+      load_bt(w1, d1);  // the rest after the first unit's pages are out
+    }
 
     int32_t kcount = 0;  // lane cw < NW: elements published to consumer warp cw
     bool ok = true;
@@ -1049,6 +1079,14 @@ decode_tc_kernel(DecodeArgs a) {
       };
       publish(0, 1);
       __syncwarp();
+      if (!waited) {
+        // early start: the first unit's pages are being loaded; now the
+        // previous kernel, then what it may have written
+        dep_wait();
+        waited = true;
+        if (lane == 0 && R <= 2) fetched = atomicAdd(&a.sched[0], 1);
+        load_in(w1, d1);
+      }
       // query rows (and the appended K/V row) -> the unit's query slot
       if (kRope && a.rcos != nullptr) {  // RoPE: the partner chunk (other half of the head) is in lane ^ D/16
         const bool second = (lane % kRowChunks) >= kRowChunks / 2;
@@ -1103,16 +1141,6 @@ decode_tc_kernel(DecodeArgs a) {
       w2 = w3;
       d2 = d3;
     }
-    if (lane == 0) {
-      // This CTA claims no more units. The last CTA to get here resets the
-      // counters so the plan can drive the next launch.
-      __threadfence();
-      const int done = atomicAdd(&a.sched[1], 1);
-      if (done == (int)gridDim.x - 1) {
-        atomicExch(&a.sched[0], 0);
-        atomicExch(&a.sched[1], 0);
-      }
-    }
     if (lane < NW && ok) {  // a stop element to each consumer warp
       const int32_t k = kcount++;
       const int slot = lane * MD + (k % MD);
@@ -1126,6 +1154,18 @@ decode_tc_kernel(DecodeArgs a) {
         md.work = -1;
         meta[slot] = md;
         mbar_arrive(&full[slot]);
+      }
+    }
+    // (a CTA without units, or stopped by a timeout, under early start)
+    if (!waited) dep_wait();
+    if (lane == 0) {
+      // This CTA claims no more units. The last CTA to get here resets the
+      // counters so the plan can drive the next launch.
+      __threadfence();
+      const int done = atomicAdd(&a.sched[1], 1);
+      if (done == (int)gridDim.x - 1) {
+        atomicExch(&a.sched[0], 0);
+        atomicExch(&a.sched[1], 0);
       }
     }
     return;
@@ -1218,8 +1258,17 @@ decode_tc_kernel(DecodeArgs a) {
     }
     cp_async_commit();  // one group per element, possibly empty
   };
+  if (early) {
+    // the first element is published before the producer's dependency wait:
+    // its page loads start now, the rest after this warp's own wait
+    issue(0);
+    dep_wait();
 #pragma unroll 1
-  for (int32_t e = 0; e < S - 1; ++e) issue(e);
+    for (int32_t e = 1; e < S - 1; ++e) issue(e);
+  } else {
+#pragma unroll 1
+    for (int32_t e = 0; e < S - 1; ++e) issue(e);
+  }
 
   for (int32_t k = 0;; ++k) {
     issue(k + S - 1);
@@ -1951,6 +2000,7 @@ int decode_run_impl(const void *q, const void *kn, const void *vn, const void *k
     a.max_tries = kTestWaitPolls;
     a.withhold = 1;
   }
+  a.early = (flags & PKV_DECODE_EARLY_START) ? 1 : 0;
   const int64_t max_units = w.max_items * w.units_per_item;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const bool tc = tc_eligible(k_cache, v_cache, num_q_heads, num_kv_heads, head_dim, block_size,

@@ -359,6 +359,7 @@ def paged_attention_decode(
     v_new: Optional[torch.Tensor] = None,
     out_dtype: Optional[torch.dtype] = None,
     rope: Optional[tuple[torch.Tensor, torch.Tensor]] = None,
+    early_start: bool = False,
 ) -> torch.Tensor:
     """Single-query attention over the paged cache; returns fp32 [B, Hq, D].
 
@@ -387,6 +388,17 @@ def paged_attention_decode(
     out_dtype=q.dtype (bf16 / fp16 q) returns the output in q's dtype, each
     fp32 result rounded to nearest: the values of ``.to(q.dtype)`` of the fp32
     output, without a separate conversion launch.
+
+    early_start=True promises that the previous kernel queued on the stream
+    wrote none of the plan, the block tables, the context lengths and the
+    caches, and that the kernels before it are complete once it lets this
+    launch start: true for every layer's decode launch of a step after the
+    first (each follows an earlier decode launch, which lets the next launch
+    start only after its own wait), not for the first (behind the plan) nor
+    one behind a separate append. The tensor-core launch then schedules its
+    first unit and starts loading its pages before that kernel has finished;
+    q, the new rows and cos / sin are still read after it. Results are
+    unchanged.
     """
     _check_cache_pair(k_cache, v_cache)
     if q.ndim != 3:
@@ -421,6 +433,8 @@ def paged_attention_decode(
     if rope is not None and k_new is None:
         raise ValueError("rope needs k_new / v_new (RoPE runs with the fused append).")
     flags = (_lib.DECODE_FORCE_GENERIC if force_generic else 0) | (_lib.DECODE_EXACT_P if exact else 0)
+    if early_start:
+        flags |= _lib.DECODE_EARLY_START
     if out.dtype != torch.float32:
         flags |= _lib.DECODE_OUT_Q_DTYPE
     if k_new is not None or v_new is not None:

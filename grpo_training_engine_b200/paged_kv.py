@@ -513,7 +513,8 @@ def paged_kv_decode_model(
             k_cache, v_cache = pool.layer(layer_idx)
             # append at context_lens and attend over new_context_lens: one fused call
             attn_out = ops.paged_attention_decode(q1, k_cache, v_cache, block_tables, new_context_lens,
-                                                  scale=scale, plan=plan, k_new=k1, v_new=v1)
+                                                  scale=scale, plan=plan, k_new=k1, v_new=v1,
+                                                  early_start=layer_idx > 0)
             attn_out = attn_out.to(hidden.dtype).reshape(batch_size, 1, num_heads * head_dim)
             hidden = residual + attn.o_proj(attn_out)
             residual = hidden
@@ -539,12 +540,15 @@ def paged_kv_decode_model(
             q_lin, k_lin, v_lin = _qkv(layer_idx, attn, h)
             k_cache, v_cache = pool.layer(layer_idx)
             v1 = v_lin.view(batch_size, num_kv_heads, head_dim)
+            # every layer after the first: the last kernel before the plan, block tables and this layer's
+            # cache changed is the previous layer's decode launch, so this one may schedule its pages early
+            early = layer_idx > 0
             if rope_in_decode:
                 # RoPE, append at context_lens and attention over new_context_lens: one launch
                 attn_out = ops.paged_attention_decode(
                     q_lin.view(batch_size, num_heads, head_dim), k_cache, v_cache, block_tables,
                     new_context_lens, scale=scale, plan=plan, k_new=k_lin.view(batch_size, num_kv_heads, head_dim),
-                    v_new=v1, rope=(cos, sin), out_dtype=hidden.dtype)
+                    v_new=v1, rope=(cos, sin), out_dtype=hidden.dtype, early_start=early)
             else:
                 # stacked: the keys rotate in place, so k and v are views of one buffer with equal strides
                 q1, k1 = ops.rope_qk(q_lin, k_lin, cos, sin, num_heads, num_kv_heads, head_dim,
@@ -552,7 +556,7 @@ def paged_kv_decode_model(
                 # append at context_lens and attend over new_context_lens: one fused call
                 attn_out = ops.paged_attention_decode(q1, k_cache, v_cache, block_tables, new_context_lens,
                                                       scale=scale, plan=plan, k_new=k1, v_new=v1,
-                                                      out_dtype=hidden.dtype)
+                                                      out_dtype=hidden.dtype, early_start=early)
             o = _linear(o_stack[layer_idx], attn.o_proj, attn_out.reshape(batch_size, num_heads * head_dim))
             ln = layer.post_attention_layernorm
             h2, hidden = ops.add_rmsnorm(o, ln.weight, ln.variance_epsilon, residual=hidden)

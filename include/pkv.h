@@ -40,7 +40,7 @@ extern "C" {
 #define PKV_ABI_VERSION 10 /* 2: pkv_append_decode_run, 3: pkv_sample_top_p, 4: rmsnorm, rope, 5: silu_mul,
                               6: pkv_sample_top_p flags, 7: pkv_rope_qk output strides,
                               8: pkv_rope_append_decode_run, 9: pkv_linear,
-                              10: PKV_LINEAR_WEIGHTS_STATIC */
+                              10: PKV_LINEAR_WEIGHTS_STATIC, PKV_DECODE_EARLY_START */
 
 /* Element types. The reference stores the cache in bfloat16
  * (paged_kv.py:409-410, 629-633); float32 is accepted because the reference
@@ -80,6 +80,22 @@ enum {
     PKV_DECODE_OUT_Q_DTYPE = 4,   /* out holds q's dtype (bf16 or fp16; fp32 q:
                                      no change): each fp32 result rounded to
                                      nearest, as a cast of the fp32 output   */
+    PKV_DECODE_EARLY_START = 8,   /* tensor-core kernel: the caller promises
+                                     that the previous kernel in the stream
+                                     wrote none of the plan (workspace),
+                                     block tables, context lengths and
+                                     caches, and that every kernel before it
+                                     is complete once it lets this launch
+                                     start. Both hold when it is an earlier
+                                     decode launch after the plan (a decode
+                                     launch lets the next launch start only
+                                     after its own wait): the layers after the
+                                     first of a step, not the first (behind the
+                                     plan) nor one behind a separate append.
+                                     The launch then schedules its first unit
+                                     and starts loading its pages before
+                                     waiting for that kernel; q, the new rows
+                                     and cos / sin are read after the wait. */
     PKV_DECODE_TEST_WAIT_TIMEOUT = 1 << 30 /* TEST ONLY (tensor-core kernel):
                                      every device wait gives up after 4096
                                      polls instead of seconds' worth, and the
