@@ -834,6 +834,76 @@ def run_rollout(args):
     }), flush=True)
 
 
+# ----------------------------------------------------------------------------- projection GEMM
+def run_linear(args):
+    """The projections of one layer of the 1.5B rollout step plus its LM head (128 rows, bf16) on
+    pkv_linear against cuBLAS. Per shape, one call on each of n copies of the weights (n >= 4, the
+    copies together > 3 x L2, so every call streams its weights from HBM) is captured as one CUDA
+    graph and replayed back to back; time per call = the fastest of three replays / n (CUDA events),
+    after --warmup eager calls. pkv_linear runs with PKV_LINEAR_WEIGHTS_STATIC, as in the rollout step; cuBLAS multiplies
+    by an input-major copy (what the model path passes it), and the SiLU gate adds pkv_silu_mul."""
+    from grpo_training_engine_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    hid, inter, vocab, rows = 1536, 8960, 151936, 128
+    shapes = [("qkv_bias", 2048, hid, True, False), ("o_proj", hid, hid, False, False),
+              ("gate_up_silu", inter, hid, False, True), ("down", hid, inter, False, False),
+              ("lm_head", vocab, hid, False, False)]
+    out = []
+    for name, n, k, with_bias, silu in shapes:
+        wrows = 2 * n if silu else n
+        wbytes = wrows * k * 2
+        calls = max(4, math.ceil(3 * 126e6 / wbytes))  # copies together > 3 x L2
+        ws = [(torch.randn(wrows, k, device=dev, generator=g) / k ** 0.5).to(torch.bfloat16) for _ in range(calls)]
+        wts = [w.t().contiguous() for w in ws]
+        x = torch.randn(rows, k, device=dev, generator=g).to(torch.bfloat16)
+        b = torch.randn(n, device=dev, generator=g).to(torch.bfloat16) if with_bias else None
+        o_ours = torch.empty(rows, n, dtype=torch.bfloat16, device=dev)
+
+        def ours(i):
+            ops.linear(x, ws[i], b, silu_gate=silu, out=o_ours, weights_static=True)
+
+        def cublas(i):
+            wt = wts[i]
+            if silu:
+                gu = x @ wt
+                ops.silu_mul(gu[:, :n], gu[:, n:])
+            elif b is not None:
+                torch.addmm(b, x, wt)
+            else:
+                x @ wt
+
+        times = {}
+        for label, fn in (("ours", ours), ("cublas", cublas)):
+            for i in range(args.warmup):
+                fn(i)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for i in range(calls):
+                    fn(i)
+            best = float("inf")
+            for _ in range(3):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                graph.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                best = min(best, e0.elapsed_time(e1) * 1e3 / calls)
+            times[label] = best
+            del graph
+        out.append({"name": name, "n": n, "k": k, "weight_bytes": wbytes, "calls_per_replay": calls,
+                    "ours_us": round(times["ours"], 2), "cublas_us": round(times["cublas"], 2),
+                    "ours_GBps": round(wbytes / times["ours"] / 1e3, 1),
+                    "cublas_GBps": round(wbytes / times["cublas"] / 1e3, 1)})
+        del ws, wts
+        torch.cuda.empty_cache()
+    print(json.dumps({"metric": "projection GEMMs of the 1.5B rollout step (128 rows, bf16): us per call",
+                      "unit": "us", "timing": "calls on distinct weight copies replayed back to back as one CUDA "
+                      "graph; fastest of 3 replays / calls", "shapes": out}), flush=True)
+
+
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args, rank, world):
     """CPU restatement of the reference algorithm on the host cores (the reference is
@@ -956,6 +1026,8 @@ def main():
                     help="with --rollout: per-kernel time of one graph-replayed step (torch profiler)")
     ap.add_argument("--rollout", action="store_true",
                     help="time the model-level rollout step (eager vs CUDA graph) instead of the decode path")
+    ap.add_argument("--linear", action="store_true",
+                    help="time the projection GEMM (pkv_linear) against cuBLAS on the rollout step's shapes")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
@@ -967,6 +1039,9 @@ def main():
         args.warmup = 3
     if args.rollout:
         run_rollout(args)
+        return
+    if args.linear:
+        run_linear(args)
         return
     rank, world, local = dist_setup(args)
     if args.impl == "reference":

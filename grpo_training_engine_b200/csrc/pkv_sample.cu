@@ -117,9 +117,12 @@ __device__ __forceinline__ uint32_t low_bits(int n) { return n >= 32 ? FULL : (1
 // of KV; anything past the row), match(v, b) a bit per token of it. Three
 // levels of counts: contiguous warp ranges of the row, the 32 sub-ranges of
 // the chosen warp's range, the 32 lane slices of the chosen sub-range; the
-// chosen lane walks its slice.
-template <int KV, typename Load, typename Match>
-__device__ __forceinline__ int find_rth(int V, int r, Load load, Match match, int *s_cnt, int *s_res) {
+// chosen lane walks its slice. count_full(v, b) gives the number of matching
+// tokens of a vector wholly inside the range being counted (popc of match by
+// default; the 16-bit path counts with per-halfword min / max).
+template <int KV, typename Load, typename Match, typename CountFull>
+__device__ __forceinline__ int find_rth(int V, int r, Load load, Match match, CountFull count_full, int *s_cnt,
+                                        int *s_res) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int kInFlight = 4;
   const int sub = ((V + kSampleThreads - 1) / kSampleThreads + KV - 1) / KV * KV;  // per lane
@@ -137,7 +140,11 @@ __device__ __forceinline__ int find_rth(int V, int r, Load load, Match match, in
 #pragma unroll
       for (int h = 0; h < kInFlight; ++h) {
         const int b = b0 + h * 32 * KV;
-        if (b < hi) c += __popc(match(v[h], b) & low_bits(hi - b));
+        if (b + KV <= hi) {
+          c += count_full(v[h], b);
+        } else if (b < hi) {
+          c += __popc(match(v[h], b) & low_bits(hi - b));
+        }
       }
     }
     return __reduce_add_sync(FULL, c);
@@ -410,7 +417,9 @@ __device__ __forceinline__ void radix_top_p(const SampleArgs &a, uint8_t *sample
       r = (target - above) / pc;
     }
     __syncthreads();
-    token = find_rth<kVec>(V, (int)min(r, (unsigned long long)V), load, match_key(gkey), s_cnt, &s_res);
+    const auto mk = match_key(gkey);
+    token = find_rth<kVec>(V, (int)min(r, (unsigned long long)V), load, mk,
+                           [&](const uint4 &v, int b) { return __popc(mk(v, b)); }, s_cnt, &s_res);
   }
   if (tid == 0) a.out[blockIdx.x] = token >= 0 ? token : 0;
 }
@@ -532,31 +541,39 @@ __global__ void __launch_bounds__(kSampleThreads, 1) top_p16_kernel(SampleArgs a
   int khi = (int)min(kmax0 + kMargin, 0xffffu);
   int klo = max(khi - kWindow + 1, 0);
   // count the tokens of one vector: a vector of one pattern (flat or padded
-  // rows) takes one increment, any other one increment per token
+  // rows) takes one increment, any other one increment per token. A full
+  // vector's keys are made two per 32-bit word (each 16-bit half h becomes
+  // h ^ 0xffff when negative, h ^ 0x8000 otherwise), and their running max is
+  // a per-halfword max; a token outside the window [klo, khi] (k - klo wraps
+  // past the span) is not counted.
+  uint32_t span = (uint32_t)(khi - klo);  // (reset when the window moves)
+  uint32_t km2 = 0;  // per-halfword max of the full vectors' keys
   auto count_vec = [&](const uint4 &v, int base) {
-    uint32_t k[kVec];
     if (base + kVec <= V) {
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      uint32_t kw[4];
 #pragma unroll
-      for (int j = 0; j < kVec; ++j) k[j] = key16(half_at(v, j));
-    } else {
+      for (int q = 0; q < 4; ++q) kw[q] = w[q] ^ ((((w[q] >> 15) & 0x10001u) * 0x7fffu) | 0x80008000u);
+      km2 = __vimax3_u16x2(km2, __vimax3_u16x2(kw[0], kw[1], kw[2]), kw[3]);
+      if (((kw[0] ^ kw[1]) | (kw[0] ^ kw[2]) | (kw[0] ^ kw[3]) | ((kw[0] ^ (kw[0] >> 16)) & 0xffffu)) == 0u) {
+        const uint32_t i = (kw[0] & 0xffffu) - (uint32_t)klo;
+        if (i <= span) atomicAdd(&cnt[i], (uint32_t)kVec);
+        return;
+      }
 #pragma unroll
-      for (int j = 0; j < kVec; ++j) k[j] = key_at(v, base, j);
-    }
-    bool same = true;
-#pragma unroll
-    for (int j = 1; j < kVec; ++j) same &= k[j] == k[0];
-    if (same) {
-      if (k[0] != kNoKey) {
-        km = max(km, k[0]);
-        if (k[0] - (uint32_t)klo <= (uint32_t)(khi - klo)) atomicAdd(&cnt[k[0] - klo], (uint32_t)kVec);
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t i0 = (kw[q] & 0xffffu) - (uint32_t)klo, i1 = (kw[q] >> 16) - (uint32_t)klo;
+        if (i0 <= span) atomicAdd(&cnt[i0], 1u);
+        if (i1 <= span) atomicAdd(&cnt[i1], 1u);
       }
       return;
     }
 #pragma unroll
-    for (int j = 0; j < kVec; ++j) {
-      if (k[j] == kNoKey) continue;
-      km = max(km, k[j]);
-      if (k[j] - (uint32_t)klo <= (uint32_t)(khi - klo)) atomicAdd(&cnt[k[j] - klo], 1u);
+    for (int j = 0; j < kVec; ++j) {  // the row's last, partial vector
+      const uint32_t k = key_at(v, base, j);
+      if (k == kNoKey) continue;
+      km = max(km, k);
+      if (k - (uint32_t)klo <= span) atomicAdd(&cnt[k - klo], 1u);
     }
   };
   auto count_rest = [&](int from) {
@@ -571,7 +588,7 @@ __global__ void __launch_bounds__(kSampleThreads, 1) top_p16_kernel(SampleArgs a
 #pragma unroll
   for (int h = 0; h < kInFlight; ++h) count_vec(v0[h], tid * kVec + h * kStep);
   count_rest(kInFlight * kStep);
-  const uint32_t kmax = block_max(km);
+  const uint32_t kmax = block_max(max(km, max(km2 & 0xffffu, km2 >> 16)));
 
   // scaled value of the pattern with key k, and its mass relative to the max
   const float smax = Bits16<L>::to_float(sbits(kmax));
@@ -585,6 +602,7 @@ __global__ void __launch_bounds__(kSampleThreads, 1) top_p16_kernel(SampleArgs a
     // the window from the row max: [kmax - kWindow + 1, kmax]
     khi = (int)kmax;
     klo = max(khi - kWindow + 1, 0);
+    span = (uint32_t)(khi - klo);
     if (klo > 0 && pfix(emass((uint32_t)klo - 1)) != 0) {  // massful patterns beyond any window
       radix_top_p<L, KEY_BITS>(a, sample_smem);
       return;
@@ -792,7 +810,21 @@ __global__ void __launch_bounds__(kSampleThreads, 1) top_p16_kernel(SampleArgs a
       if (((half_at(v, j) - rlo) & 0xffffu) <= rspan) msk |= 1u << j;
     return msk;  // bits past the row are masked by the caller
   };
-  const int token = s_hi >= s_lo ? find_rth<kVec>(V, s_r, load, match, s_cnt, &s_res) : -1;
+  // a full vector's matches: per halfword, min(max(h, rlo), rlo + rspan) == h
+  // exactly for the matching patterns (rlo + rspan <= 0xffff); the other
+  // halfwords leave a non-zero xor, clamped to 1 and summed
+  const uint32_t rlo2 = rlo * 0x10001u, rhi2 = (rlo + rspan) * 0x10001u;
+  const auto count_full = [&](const uint4 &v, int) -> int {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t miss = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t c = __vimin3_u16x2(__vimax3_u16x2(w[q], rlo2, rlo2), rhi2, rhi2);
+      miss += __vimin3_u16x2(c ^ w[q], 0x10001u, 0x10001u);
+    }
+    return kVec - (int)((miss & 0xffffu) + (miss >> 16));
+  };
+  const int token = s_hi >= s_lo ? find_rth<kVec>(V, s_r, load, match, count_full, s_cnt, &s_res) : -1;
   if (tid == 0) a.out[blockIdx.x] = token >= 0 ? token : 0;
 }
 
