@@ -125,3 +125,37 @@ def test_ops_reject_cpu_tensors_with_reference_message():
         paged_attention_decode(torch.zeros(1, 4, 8, dtype=torch.bfloat16), kc, kc.clone(), bt, ctx)
     with pytest.raises(ValueError, match="must be divisible"):
         paged_attention_decode(torch.zeros(1, 3, 8, dtype=torch.bfloat16), kc, kc.clone(), bt, ctx)
+
+
+def test_linear_host_checks_without_a_gpu():
+    """pkv_linear refuses what it cannot serve before touching the GPU; a call
+    that passes every check stops at the tensor-map encoder here (no driver)."""
+    lib = _lib.load()
+    A = C.c_void_p(1 << 20)  # 16-byte aligned fake device addresses (never dereferenced)
+    B = C.c_void_p(1 << 21)
+    O = C.c_void_p(1 << 22)
+    bf16, none, silu, static = _lib.DTYPE_BF16, _lib.LINEAR_NONE, _lib.LINEAR_SILU_GATE, _lib.LINEAR_WEIGHTS_STATIC
+
+    def call(x=A, w=B, w_up=None, bias=None, out=O, rows=128, n=1536, k=1536, xs=1536, ws=1536, os_=1536,
+             dtype=bf16, act=none):
+        return lib.pkv_linear(x, w, w_up, bias, out, rows, n, k, xs, ws, os_, dtype, act, None, None)
+
+    assert call(rows=0) == _lib.ERR_INVALID_ARG
+    assert call(rows=129) == _lib.ERR_INVALID_ARG
+    assert call(n=0) == _lib.ERR_INVALID_ARG
+    assert call(dtype=_lib.DTYPE_F32) == _lib.ERR_UNSUPPORTED
+    assert call(act=2) == _lib.ERR_INVALID_ARG
+    assert call(act=static | 2) == _lib.ERR_INVALID_ARG
+    assert call(k=100, xs=100, ws=100) == _lib.ERR_UNSUPPORTED          # K not a multiple of 64
+    assert call(act=silu, n=1000, os_=1000) == _lib.ERR_UNSUPPORTED     # the gate needs n % 64 == 0
+    assert call(act=silu, bias=A) == _lib.ERR_UNSUPPORTED               # and no bias
+    assert call(w_up=A) == _lib.ERR_INVALID_ARG                         # w_up only with the gate
+    assert call(x=None) == _lib.ERR_INVALID_ARG
+    assert call(x=C.c_void_p((1 << 20) + 2)) == _lib.ERR_ALIGNMENT
+    assert call(xs=1000) == _lib.ERR_ALIGNMENT                          # row stride < k
+    assert call(os_=1537) == _lib.ERR_ALIGNMENT                         # out rows not 16-byte multiples
+    assert "pkv_linear" in _lib.last_detail()
+    # every check passes (the static-weights flag, the gate with separate up rows): only the
+    # tensor-map encoder, which needs the driver, is left
+    for act, w_up in ((none, None), (static, None), (silu | static, A), (silu, None)):
+        assert call(act=act, w_up=w_up) == _lib.ERR_TENSOR_MAP, act
