@@ -38,8 +38,13 @@
 // Three passes over the row; the only per-token shared-memory work is the
 // count increment.
 //
-// fp32 logits, and rows whose window does not fit (fp16 at high temperature;
-// a +inf or NaN logit; all -inf), take the radix path: the max, then the cut
+// fp32 logits (top_p32_kernel) sum exact masses per bin of the distance
+// below the row max and sort only the tokens of the bin where the cut, and
+// then the draw, falls (described above the kernel).
+//
+// Rows neither count path serves (fp16 at high temperature; a +inf or NaN
+// logit; all -inf; fp32 rows whose cut bin holds more tokens than the sort
+// buffer), and PKV_SAMPLE_FORCE_RADIX, take the radix path: the max, then the cut
 // by a radix select over 8-bit digits of the order key of the scaled logit
 // (two passes for bf16, three for fp16, four for fp32), each pass a 256-bin
 // histogram of mass (one per warp, lanes with equal digits summed with warp
@@ -828,6 +833,322 @@ __global__ void __launch_bounds__(kSampleThreads, 1) top_p16_kernel(SampleArgs a
   if (tid == 0) a.out[blockIdx.x] = token >= 0 ? token : 0;
 }
 
+// ---------------------------------------------------------------------------
+// fp32 logits: exact masses per value bin, the tokens of one or two bins sorted
+// ---------------------------------------------------------------------------
+// A token's mass depends on its distance d = max - x below the row max (x the
+// scaled logit), and is 0 in 2^-40 fixed point once d > 28.4. The span
+// [0, kSpan32) of d is cut into kBins32 equal bins; a bin index is
+// floor(d x kBins32 / kSpan32), monotone in x, so tokens of one scaled value
+// (a group) share a bin, and bins run from the max downwards. One pass sums
+// the exact fixed-point masses per bin (64-bit shared atomics); a block scan
+// of the bins finds the bin where the running mass passes a threshold (the
+// cut, then the draw's target) exactly; one more pass collects that bin's
+// tokens (order key, index) into shared memory, where they are sorted by value
+// (descending) and index (ascending) and walked group by group with the
+// masses, cut and draw rule of the other paths. Rows it cannot serve (a NaN
+// or +inf, all -inf, a bin with more tokens than the buffer holds: flat or
+// tie-heavy rows) take the radix path.
+constexpr int kBins32 = 16384;     // 128 KB of 64-bit masses
+constexpr float kSpan32 = 28.5f;   // e^-28.5 x 2^40 < 0.5: no mass beyond
+constexpr int kCand = 8192;        // tokens of a bin held for sorting: 64 KB
+static_assert(kBins32 * 8 + kCand * 8 <= kHistBytes + kTableBytes, "the fp32 path uses the same dynamic smem");
+
+__global__ void __launch_bounds__(kSampleThreads, 1) top_p32_kernel(SampleArgs a) {
+  extern __shared__ __align__(16) uint8_t sample_smem[];
+  unsigned long long *bmass = reinterpret_cast<unsigned long long *>(sample_smem);  // [kBins32]
+  unsigned long long *cand = bmass + kBins32;                                       // [kCand]
+  __shared__ unsigned long long red64[kSampleWarps];
+  __shared__ unsigned long long s_u64;
+  __shared__ uint32_t redk[kSampleWarps];
+  __shared__ int s_hit, s_n;
+
+  if (a.flags & PKV_SAMPLE_FORCE_RADIX) {
+    radix_top_p<float, 32>(a, sample_smem);
+    return;
+  }
+  const float *row = reinterpret_cast<const float *>(a.logits) + (int64_t)blockIdx.x * a.row_stride;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int V = a.vocab;
+  const float t = a.temperature;
+  constexpr int kVec = 4;
+  constexpr int kStep = kSampleThreads * kVec;
+  const bool vec_ok = (reinterpret_cast<uintptr_t>(row) & 15u) == 0;
+  const uint32_t kPosInfKey = order_key(INFINITY), kNegInfKey = order_key(-INFINITY);
+  auto pfix = [](float e) -> unsigned long long { return __float2ull_rn(e * 1099511627776.0f); };  // * 2^40
+
+  // raw logits of tokens [base, base + 4); -inf past the row
+  auto fetch_raw = [&](int base, float(&r)[kVec]) {
+    if (vec_ok && base + kVec <= V) {
+      const float4 v = __ldg(reinterpret_cast<const float4 *>(row + base));
+      r[0] = v.x;
+      r[1] = v.y;
+      r[2] = v.z;
+      r[3] = v.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) r[j] = base + j < V ? row[base + j] : -INFINITY;
+    }
+  };
+  // ---- 1. the row max; any NaN (a key below -inf's or above +inf's). The
+  // scaling by 1 / T (T > 0) is monotone and correctly rounded, so the max
+  // scaled value is the scaled max raw value: no division here.
+  uint32_t km = 0;
+  bool nan_seen = false;
+  for (int b0 = tid * kVec; b0 < V; b0 += kStep) {
+    float r[kVec];
+    fetch_raw(b0, r);
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+      if (b0 + j >= V) continue;
+      const uint32_t k = order_key(r[j]);
+      km = max(km, k);
+      nan_seen |= k < kNegInfKey;
+    }
+  }
+  km = __reduce_max_sync(FULL, km);
+  if (lane == 0) redk[warp] = km;
+  for (int i = tid; i < kBins32; i += kSampleThreads) bmass[i] = 0ull;
+  const bool any_nan = __syncthreads_or(nan_seen ? 1 : 0) != 0;
+  const uint32_t kmax = __reduce_max_sync(FULL, redk[lane]);  // of the raw values
+  if (any_nan || kmax >= kPosInfKey || kmax <= kNegInfKey) {
+    radix_top_p<float, 32>(a, sample_smem);
+    return;
+  }
+  const float smax = __fdiv_rn(key_value(kmax), t);
+  const float inv_w = (float)kBins32 / kSpan32;
+  // raw values that certainly lie below the span (scaled distance > 28.5 by a
+  // margin): massless, no division needed
+  const float raw_floor = (smax - kSpan32 - 1.f) * t - 1e-5f * fabsf((smax - kSpan32 - 1.f) * t);
+  auto bin_of = [&](float x) -> int {  // kBins32: beyond the span (no mass)
+    const float d = smax - x;
+    return d < kSpan32 ? min((int)(d * inv_w), kBins32 - 1) : kBins32;
+  };
+
+  // ---- 2. exact masses per bin and of the row
+  unsigned long long tot = 0;
+  for (int b0 = tid * kVec; b0 < V; b0 += kStep) {
+    float x[kVec];
+    fetch_raw(b0, x);
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+      if (b0 + j >= V || x[j] < raw_floor) continue;
+      x[j] = __fdiv_rn(x[j], t);
+      const int b = bin_of(x[j]);
+      if (b < kBins32) {
+        const unsigned long long p = pfix(expf(x[j] - smax));
+        if (p) atomicAdd(&bmass[b], p);
+        tot += p;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(FULL, tot, o);
+  if (lane == 0) red64[warp] = tot;
+  __syncthreads();
+  unsigned long long total = red64[lane];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(FULL, total, o);
+  __syncthreads();
+
+  // exclusive block scan of one value per thread: (the thread's prefix, the
+  // per-thread inclusive value is prefix + v)
+  auto block_excl = [&](unsigned long long v) -> unsigned long long {
+    unsigned long long inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned long long u = __shfl_up_sync(FULL, inc, o);
+      if (lane >= o) inc += u;
+    }
+    if (lane == 31) red64[warp] = inc;
+    __syncthreads();
+    unsigned long long wpre = 0;
+    for (int w = 0; w < warp; ++w) wpre += red64[w];
+    __syncthreads();
+    return wpre + inc - v;
+  };
+
+  // ---- the first bin whose running mass (inclusive) exceeds thr, and the
+  // mass of the bins before it; -1 when none does
+  constexpr int kBinsPerThread = kBins32 / kSampleThreads;
+  auto first_bin_over = [&](unsigned long long thr, unsigned long long &before) -> int {
+    unsigned long long local = 0;
+#pragma unroll
+    for (int q = 0; q < kBinsPerThread; ++q) local += bmass[tid * kBinsPerThread + q];
+    const unsigned long long pre = block_excl(local);
+    if (tid == 0) s_hit = INT32_MAX;
+    __syncthreads();
+    unsigned long long run = pre;
+    for (int q = 0; q < kBinsPerThread; ++q) {
+      const unsigned long long m = bmass[tid * kBinsPerThread + q];
+      if (run + m > thr) {
+        atomicMin(&s_hit, tid * kBinsPerThread + q);
+        break;
+      }
+      run += m;
+    }
+    __syncthreads();
+    const int b = s_hit;
+    if (b != INT32_MAX && tid == b / kBinsPerThread) {
+      unsigned long long r = pre;
+      for (int q = 0; q < b % kBinsPerThread; ++q) r += bmass[tid * kBinsPerThread + q];
+      s_u64 = r;
+    }
+    __syncthreads();
+    before = s_u64;
+    __syncthreads();
+    return b == INT32_MAX ? -1 : b;
+  };
+
+  // ---- the tokens of bin b into cand, sorted by value (descending) then
+  // index (ascending); their count, or -1 when they do not fit
+  auto collect = [&](int bin) -> int {
+    if (tid == 0) s_n = 0;
+    // raw values of the bin, widened by a whole bin on either side and a
+    // relative 1e-5 (the scaling rounds by half an ulp): only tokens in there
+    // are divided and binned exactly
+    const float xl = smax - (float)(bin + 2) / inv_w, xh = smax - (float)(bin - 1) / inv_w;
+    const float rl = xl * t - 1e-5f * fabsf(xl * t) - 1e-30f, rh = xh * t + 1e-5f * fabsf(xh * t) + 1e-30f;
+    __syncthreads();
+    for (int b0 = tid * kVec; b0 < V; b0 += kStep) {
+      float x[kVec];
+      fetch_raw(b0, x);
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) {
+        if (b0 + j < V && x[j] >= rl && x[j] <= rh && bin_of(x[j] = __fdiv_rn(x[j], t)) == bin) {
+          const int pos = atomicAdd(&s_n, 1);
+          if (pos < kCand)
+            cand[pos] = ((unsigned long long)order_key(x[j]) << 32) | (uint32_t)(0xffffffffu - (uint32_t)(b0 + j));
+        }
+      }
+    }
+    __syncthreads();
+    const int n = s_n;
+    if (n > kCand) return -1;
+    int np = 2;
+    while (np < n) np <<= 1;
+    for (int i = n + tid; i < np; i += kSampleThreads) cand[i] = 0ull;
+    __syncthreads();
+    for (int k = 2; k <= np; k <<= 1) {
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        for (int i = tid; i < np; i += kSampleThreads) {
+          const int p = i ^ j;
+          if (p > i) {
+            const unsigned long long u = cand[i], w = cand[p];
+            if ((i & k) == 0 ? u < w : u > w) {
+              cand[i] = w;
+              cand[p] = u;
+            }
+          }
+        }
+        __syncthreads();
+      }
+    }
+    return n;
+  };
+
+  // ---- walk the n sorted tokens from `base` (the mass before them): the
+  // first whose running mass (inclusive) exceeds thr, its group (equal values)
+  // [gs, ge], the mass before the group and its per-token mass. False when
+  // none does.
+  constexpr int kPerThread = kCand / kSampleThreads;
+  auto walk = [&](int n, unsigned long long base, unsigned long long thr, int &gs, int &ge,
+                  unsigned long long &gbefore, unsigned long long &per) -> bool {
+    unsigned long long m[kPerThread], local = 0;
+#pragma unroll
+    for (int q = 0; q < kPerThread; ++q) {
+      const int i = tid * kPerThread + q;
+      m[q] = i < n ? pfix(expf(key_value((uint32_t)(cand[i] >> 32)) - smax)) : 0ull;
+      local += m[q];
+    }
+    const unsigned long long pre = base + block_excl(local);
+    if (tid == 0) s_hit = INT32_MAX;
+    __syncthreads();
+    unsigned long long run = pre;
+#pragma unroll
+    for (int q = 0; q < kPerThread; ++q) {
+      run += m[q];
+      const int i = tid * kPerThread + q;
+      if (i < n && run > thr) {
+        atomicMin(&s_hit, i);
+        break;
+      }
+    }
+    __syncthreads();
+    const int hit = s_hit;
+    if (hit == INT32_MAX) return false;
+    const uint32_t key = (uint32_t)(cand[hit] >> 32);
+    int lo = 0, hi = hit;  // first index with this key (keys descending)
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if ((uint32_t)(cand[mid] >> 32) > key) lo = mid + 1; else hi = mid;
+    }
+    gs = lo;
+    lo = hit;
+    hi = n - 1;  // last index with this key
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if ((uint32_t)(cand[mid] >> 32) < key) hi = mid - 1; else lo = mid;
+    }
+    ge = lo;
+    per = pfix(expf(key_value(key) - smax));
+    if (tid == hit / kPerThread) {  // the running mass through the hit: every token of a group weighs the same
+      unsigned long long r = pre;
+      for (int q = 0; q <= hit % kPerThread; ++q) r += m[q];
+      s_u64 = r;
+    }
+    __syncthreads();
+    gbefore = s_u64 - (unsigned long long)(hit - gs + 1) * per;
+    __syncthreads();
+    return true;
+  };
+  auto token_of = [&](int i) { return (int)(0xffffffffu - (uint32_t)(cand[i] & 0xffffffffu)); };
+
+  // ---- 3. the cut
+  const unsigned long long top_p = (unsigned long long)fmin((double)a.top_p * (double)total, 4.0 * (double)total);
+  const bool found = total > top_p;
+  int cbin = -1, cgs = 0, cge = -1, n_ties = 0, keep_ties = 0, ncand = 0;
+  unsigned long long above = total, pc = 0;
+  if (found) {
+    unsigned long long bbefore = 0;
+    cbin = first_bin_over(top_p, bbefore);
+    ncand = cbin >= 0 ? collect(cbin) : -1;
+    if (ncand < 0 || !walk(ncand, bbefore, top_p, cgs, cge, above, pc)) {
+      radix_top_p<float, 32>(a, sample_smem);
+      return;
+    }
+    n_ties = cge - cgs + 1;
+    if (pc > 0 && top_p > above) {
+      const unsigned long long nk = (top_p - above) / pc;
+      keep_ties = nk >= (unsigned long long)V ? V : (int)nk;
+    }
+    if (above == 0 && keep_ties == 0) keep_ties = 1;  // the most likely token always stays
+  }
+  const unsigned long long kept = above + (unsigned long long)min(n_ties, keep_ties) * pc;
+
+  // ---- 4. the draw
+  const unsigned long long target = (unsigned long long)((double)a.uniforms[blockIdx.x] * (double)kept);
+  int token;
+  if (found && target >= above) {  // in the cut group
+    const unsigned long long r = pc > 0 ? (target - above) / pc : 0;
+    token = token_of(cgs + (int)min(r, (unsigned long long)(n_ties - 1)));
+  } else {
+    unsigned long long bbefore = 0;
+    const int tbin = first_bin_over(target, bbefore);
+    int n = ncand;
+    if (tbin != cbin) n = tbin >= 0 ? collect(tbin) : -1;
+    int gs = 0, ge = -1;
+    unsigned long long gb = 0, per = 0;
+    if (n < 0 || !walk(n, bbefore, target, gs, ge, gb, per)) {
+      radix_top_p<float, 32>(a, sample_smem);
+      return;
+    }
+    const unsigned long long r = per > 0 ? (target - gb) / per : 0;
+    token = token_of(gs + (int)min(r, (unsigned long long)(ge - gs)));
+  }
+  if (tid == 0) a.out[blockIdx.x] = token;
+}
+
 }  // namespace
 }  // namespace pkv
 
@@ -873,10 +1194,10 @@ extern "C" int pkv_sample_top_p(const void *logits, int32_t dtype, int32_t batch
       top_p16_kernel<__half, 24><<<batch, kSampleThreads, kHistBytes + kTableBytes, st>>>(a);
       break;
     default:
-      if (cudaFuncSetAttribute(top_p_kernel<float, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               kHistBytes) != cudaSuccess)
+      if (cudaFuncSetAttribute(top_p32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kHistBytes + kTableBytes) != cudaSuccess)
         return check_launch("cudaFuncSetAttribute(top_p)");
-      top_p_kernel<float, 32><<<batch, kSampleThreads, kHistBytes, st>>>(a);
+      top_p32_kernel<<<batch, kSampleThreads, kHistBytes + kTableBytes, st>>>(a);
       break;
   }
   return check_launch("pkv_sample_top_p");

@@ -99,12 +99,14 @@ def _both_paths(logits, temperature, top_p, seed=0):
     return fast, radix
 
 
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("kind", ["normal", "coarse", "flat", "masked", "peaked"])
 def test_count_path_equals_radix_path(dtype, kind):
-    """16-bit logits: the per-pattern count path and the radix-select path use the
-    same fixed-point masses, cut and target, so every row gives the same token --
-    near-ties included, no margin."""
+    """The count paths (per 16-bit pattern; for fp32 per value bin, with the cut's
+    bin sorted) and the radix-select path use the same fixed-point masses, cut
+    and target, so every row gives the same token -- near-ties included, no
+    margin. For fp32 the coarse (thousands of ties per value) and flat rows
+    overflow the bin buffer and take the radix path inside the kernel."""
     g = torch.Generator().manual_seed(21)
     vocab = 151936
     if kind == "normal":
@@ -128,7 +130,7 @@ def test_count_path_equals_radix_path(dtype, kind):
 @pytest.mark.parametrize("vocab", [7, 1000, 50257])
 def test_count_path_equals_radix_path_small_vocab(vocab):
     g = torch.Generator().manual_seed(vocab)
-    for dtype in (torch.bfloat16, torch.float16):
+    for dtype in (torch.bfloat16, torch.float16, torch.float32):
         logits = (torch.randn(48, vocab, generator=g) * 3).to(dtype).to(DEV)
         for seed, (temperature, top_p) in enumerate([(0.7, 0.9), (1.0, 1.0), (2.0, 0.3)]):
             fast, radix = _both_paths(logits, temperature, top_p, seed)
@@ -151,3 +153,21 @@ def test_rows_outside_the_count_window_take_the_radix_path():
     assert torch.equal(fast, radix)
     # no finite softmax there (the reference's probabilities are NaN): a valid index, token 0 for all -inf
     assert 0 <= int(fast[1]) < 5000 and int(fast[2]) == 0
+
+
+def test_fp32_bin_path_ties_and_spans():
+    """fp32 rows with a few hundred exact ties near the top (inside one bin),
+    rows spanning many binades, rows of tiny values (one bin holds them all:
+    the radix path), and temperatures that merge neighbouring values: the
+    value-bin path against the radix path."""
+    g = torch.Generator().manual_seed(11)
+    vocab = 151936
+    ties = torch.randn(16, vocab, generator=g) * 2
+    ties[:, :400] = 1.25
+    wide = torch.randn(16, vocab, generator=g) * 12
+    tiny = torch.randn(16, vocab, generator=g) * 1e-3
+    for x in (ties, wide, tiny):
+        logits = x.to(DEV)
+        for seed, (temperature, top_p) in enumerate([(0.7, 0.9), (1.0, 0.5), (3.0, 0.95), (0.5, 0.02)]):
+            fast, radix = _both_paths(logits, temperature, top_p, seed)
+            assert torch.equal(fast, radix), (temperature, top_p, (fast != radix).nonzero()[:4])
