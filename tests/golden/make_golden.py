@@ -30,6 +30,12 @@ Two more parts pin the steps around the decode in the rollout step:
             output bits (rmsnorm_<case>.npz).
 
     python tests/golden/make_golden.py <reference checkout> [--only decode,sampling,rmsnorm]
+
+`--time` instead prints the seconds per call of the reference's append + decode
+kernels on the config-1 case under the interpreter (the reference's own code on
+the host CPU):
+
+    python tests/golden/make_golden.py <reference checkout> --time
 """
 
 from __future__ import annotations
@@ -99,6 +105,74 @@ def rmsnorm_fixtures(torch) -> None:
         print(case["name"], tuple(y.shape))
 
 
+def reference_append_decode(ref, torch, case: dict, t: dict):
+    """One layer of the reference's step on a case: its update kernel appends the
+    new token (when the case has one), then its decode kernel attends over the
+    post-append lengths, with the launch arguments and heuristics of the
+    reference drivers (paged_kv.py:730-783). Returns the head-replicated caches,
+    the block tables, the fp32 output and the head-dim block used."""
+    G = case["hq"] // case["hkv"]
+    B, bs = case["batch"], case["block_size"]
+    D = case["head_dim"]
+    # replicate the cache to query heads (reference model-path layout)
+    kc = t["k_cache"].repeat_interleave(G, dim=1).contiguous()
+    vc = t["v_cache"].repeat_interleave(G, dim=1).contiguous()
+    bt = t["block_tables"]
+    ctx_pre = t["context_lens"]
+    block_d = ref._select_block_d(D)
+    max_context = bt.shape[1] * bs
+    if case["append"]:
+        k_new = t["k_new"].repeat_interleave(G, dim=1).contiguous()
+        v_new = t["v_new"].repeat_interleave(G, dim=1).contiguous()
+        ref._paged_kv_update_kernel[(B, case["hq"])](
+            k_new, v_new, kc, vc, bt, ctx_pre,
+            k_new.stride(0), k_new.stride(1), k_new.stride(2),
+            kc.stride(0), kc.stride(1), kc.stride(2), kc.stride(3),
+            bt.stride(0), bt.stride(1), bs,
+            D=D, BLOCK_D=block_d, num_warps=ref._select_num_warps_update(D), num_stages=1,
+        )
+        ctx = ctx_pre + 1
+    else:
+        ctx = ctx_pre
+    q = t["q"]
+    out = torch.empty((B, case["hq"], D), dtype=torch.float32)
+    block_ctx = ref._select_block_ctx(max_context)
+    ref._paged_attention_decode_kernel[(B, case["hq"])](
+        q, kc, vc, bt, ctx, out,
+        q.stride(0), q.stride(1), q.stride(2),
+        kc.stride(0), kc.stride(1), kc.stride(2), kc.stride(3),
+        bt.stride(0), bt.stride(1),
+        out.stride(0), out.stride(1), out.stride(2),
+        bs, 1.0 / np.sqrt(D),
+        D=D, BLOCK_CTX=block_ctx, BLOCK_D=block_d, MAX_CONTEXT=max_context,
+        num_warps=ref._select_num_warps_decode(block_d, block_ctx), num_stages=1,
+    )
+    return kc, vc, bt, out, block_d
+
+
+def time_reference(ref_root: str, calls: int = 3) -> None:
+    """Seconds per call of the reference's append + decode kernels on the
+    config-1 case (1.5B head geometry, fp32, contexts 37/128/300/511 + 1) under
+    the Triton interpreter on this machine's CPU: the reference's own code on
+    the host, stated beside the CPU baselines."""
+    import time
+
+    os.environ["TRITON_INTERPRET"] = "1"
+    sys.path.insert(0, ref_root)
+    import torch
+    from src.triton_kernels import paged_kv as ref  # the reference module
+
+    case = cases.BY_NAME["config1_fp32"]
+    times = []
+    for _ in range(calls + 1):  # the first call compiles nothing but warms the interpreter's caches
+        t = cases.to_torch(cases.make_inputs(case), case["dtype"])
+        t0 = time.perf_counter()
+        reference_append_decode(ref, torch, case, t)
+        times.append(time.perf_counter() - t0)
+    print(json.dumps({"case": case["name"], "seconds_per_call": [round(x, 2) for x in times[1:]],
+                      "first_call_s": round(times[0], 2), "cpus": os.cpu_count()}))
+
+
 def main(ref_root: str, parts=("decode", "sampling", "rmsnorm")) -> None:
     os.environ["TRITON_INTERPRET"] = "1"
     sys.path.insert(0, ref_root)
@@ -115,39 +189,7 @@ def main(ref_root: str, parts=("decode", "sampling", "rmsnorm")) -> None:
         G = case["hq"] // case["hkv"]
         B, bs = case["batch"], case["block_size"]
         D = case["head_dim"]
-        # replicate the cache to query heads (reference model-path layout)
-        kc = t["k_cache"].repeat_interleave(G, dim=1).contiguous()
-        vc = t["v_cache"].repeat_interleave(G, dim=1).contiguous()
-        bt = t["block_tables"]
-        ctx_pre = t["context_lens"]
-        block_d = ref._select_block_d(D)
-        max_context = bt.shape[1] * bs
-        if case["append"]:
-            k_new = t["k_new"].repeat_interleave(G, dim=1).contiguous()
-            v_new = t["v_new"].repeat_interleave(G, dim=1).contiguous()
-            ref._paged_kv_update_kernel[(B, case["hq"])](
-                k_new, v_new, kc, vc, bt, ctx_pre,
-                k_new.stride(0), k_new.stride(1), k_new.stride(2),
-                kc.stride(0), kc.stride(1), kc.stride(2), kc.stride(3),
-                bt.stride(0), bt.stride(1), bs,
-                D=D, BLOCK_D=block_d, num_warps=ref._select_num_warps_update(D), num_stages=1,
-            )
-            ctx = ctx_pre + 1
-        else:
-            ctx = ctx_pre
-        q = t["q"]
-        out = torch.empty((B, case["hq"], D), dtype=torch.float32)
-        block_ctx = ref._select_block_ctx(max_context)
-        ref._paged_attention_decode_kernel[(B, case["hq"])](
-            q, kc, vc, bt, ctx, out,
-            q.stride(0), q.stride(1), q.stride(2),
-            kc.stride(0), kc.stride(1), kc.stride(2), kc.stride(3),
-            bt.stride(0), bt.stride(1),
-            out.stride(0), out.stride(1), out.stride(2),
-            bs, 1.0 / np.sqrt(D),
-            D=D, BLOCK_CTX=block_ctx, BLOCK_D=block_d, MAX_CONTEXT=max_context,
-            num_warps=ref._select_num_warps_decode(block_d, block_ctx), num_stages=1,
-        )
+        kc, vc, bt, out, block_d = reference_append_decode(ref, torch, case, t)
         # the un-replicated cache after the reference append: head kvh*G of the replica
         kc_gqa = kc[:, ::G].contiguous()
         vc_gqa = vc[:, ::G].contiguous()
@@ -187,10 +229,14 @@ def main(ref_root: str, parts=("decode", "sampling", "rmsnorm")) -> None:
 if __name__ == "__main__":
     args = sys.argv[1:]
     parts = ("decode", "sampling", "rmsnorm")
+    if "--time" in args:
+        args.remove("--time")
+        time_reference(args[0])
+        sys.exit(0)
     if "--only" in args:
         i = args.index("--only")
         parts = tuple(args[i + 1].split(","))
         del args[i:i + 2]
     if len(args) != 1:
-        sys.exit("usage: python tests/golden/make_golden.py <reference checkout> [--only decode,sampling,rmsnorm]")
+        sys.exit("usage: python tests/golden/make_golden.py <reference checkout> [--only decode,sampling,rmsnorm] | --time")
     main(args[0], parts)
