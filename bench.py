@@ -904,6 +904,51 @@ def run_linear(args):
                       "graph; fastest of 3 replays / calls", "shapes": out}), flush=True)
 
 
+# ----------------------------------------------------------------------------- sampling
+def run_sample(args):
+    """ops.sample_top_p on 128 rows of the 151,936-token vocabulary (temperature 0.7, top-p 0.9),
+    bf16 and fp32 logits of three kinds (N(0, 9), N(0, 1), one peaked block over a low bulk): the
+    default kernel path against the radix-select path (PKV_SAMPLE_FORCE_RADIX), CUDA events around
+    one call (the draw of the uniforms included), median of --steps calls after --warmup; the two
+    paths must give the same tokens."""
+    from grpo_training_engine_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    rows, vocab = 128, 151936
+    kinds = {"normal_sd3": torch.randn(rows, vocab, device=dev, generator=g) * 3,
+             "normal_sd1": torch.randn(rows, vocab, device=dev, generator=g),
+             "peaked": torch.randn(rows, vocab, device=dev, generator=g) * 2 - 10}
+    kinds["peaked"][:, :50] += torch.randn(rows, 50, device=dev, generator=g) * 3 + 20
+
+    def median_us(fn, n):
+        ts = []
+        for i in range(args.warmup + n):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                ts.append(e0.elapsed_time(e1) * 1e3)
+        return statistics.median(ts)
+
+    out = []
+    for name, x in kinds.items():
+        for dt in (torch.bfloat16, torch.float32):
+            logits = x.to(dt)
+            fast = median_us(lambda: ops.sample_top_p(logits, 0.7, 0.9), args.steps)
+            radix = median_us(lambda: ops.sample_top_p(logits, 0.7, 0.9, force_radix=True), max(3, args.steps // 4))
+            a = ops.sample_top_p(logits, 0.7, 0.9, generator=torch.Generator(device=dev).manual_seed(2))
+            b = ops.sample_top_p(logits, 0.7, 0.9, generator=torch.Generator(device=dev).manual_seed(2),
+                                 force_radix=True)
+            out.append({"logits": name, "dtype": str(dt).split(".")[1], "us": round(fast, 1),
+                        "radix_us": round(radix, 1), "same_tokens": bool(torch.equal(a, b))})
+    print(json.dumps({"metric": "top-p sampling of 128 x 151,936 logits (T 0.7, top-p 0.9): us per call",
+                      "unit": "us", "timing": "CUDA events around one ops.sample_top_p call, median",
+                      "results": out}), flush=True)
+
+
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args, rank, world):
     """CPU restatement of the reference algorithm on the host cores (the reference is
@@ -1028,6 +1073,8 @@ def main():
                     help="time the model-level rollout step (eager vs CUDA graph) instead of the decode path")
     ap.add_argument("--linear", action="store_true",
                     help="time the projection GEMM (pkv_linear) against cuBLAS on the rollout step's shapes")
+    ap.add_argument("--sample", action="store_true",
+                    help="time the top-p sampling kernels (bf16 and fp32 logits) against the radix path")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
@@ -1042,6 +1089,9 @@ def main():
         return
     if args.linear:
         run_linear(args)
+        return
+    if args.sample:
+        run_sample(args)
         return
     rank, world, local = dist_setup(args)
     if args.impl == "reference":
