@@ -24,9 +24,10 @@
 //   warp 1             : allocates the TMEM accumulator; one thread issues
 //                        tcgen05.mma (M 128, N BN, K 16) per 16 K and commits
 //                        each stage back to the producer
-//   warps 2-5          : epilogue: tcgen05.ld of the accumulator (warp w reads
-//                        TMEM lanes 32 (w % 4) ...), bias / activation, bf16
-//                        stores.
+//   warps 2-9          : epilogue: tcgen05.ld of the accumulator (warp w reads
+//                        TMEM lanes 32 (w % 4) ..., two warps per lane group
+//                        on alternate 32-column chunks), bias / activation,
+//                        bf16 stores.
 // Narrow matrices (N of a few thousand) are split along K so that ~148 CTAs
 // stream every weight matrix. The splits of a tile are the CTAs of one thread-
 // block cluster: each leaves its fp32 partial tile in its own shared memory,
@@ -53,8 +54,13 @@ namespace {
 
 constexpr int kLinBM = 128;      // rows of the MMA (all activation rows)
 constexpr int kLinBK = 64;       // K elements per stage: one 128-byte swizzle row of 16-bit values
-constexpr int kLinThreads = 192; // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
-constexpr int kLinEpiThreads = 128;
+// warp 0 TMA, warp 1 MMA, warps 2-9 epilogue: two warps per 32-lane TMEM
+// group, each taking every other 32-column chunk (with one warp per group the
+// epilogue's dependent convert / SiLU chains took ~5 us of a gate/up launch)
+constexpr int kLinEpiWarps = 8;
+constexpr int kLinEpiParts = kLinEpiWarps / 4;  // warps per TMEM lane group
+constexpr int kLinThreads = 64 + 32 * kLinEpiWarps;
+constexpr int kLinEpiThreads = 32 * kLinEpiWarps;
 constexpr int kLinEpiBarrier = 1;  // named barrier of the epilogue warps
 constexpr int kLinMaxSplits = 8;   // K splits of a tile: the CTAs of one (portable) cluster
 
@@ -146,7 +152,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Barrier of the 128 epilogue threads. One lane may arrive later than the
+// Barrier of the epilogue threads. One lane may arrive later than the
 // rest of its warp (it waited on an mbarrier alone), so the warp reconverges
 // first and the barrier is the non-aligned form.
 __device__ __forceinline__ void epi_sync() {
@@ -396,6 +402,7 @@ linear_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CU
   } else {
     // ============================ epilogue ================================
     const int lg = warp & 3;  // TMEM lanes 32 lg .. 32 lg + 31 are readable by this warp
+    const int part = (warp - 2) >> 2;  // which of the group's warps: its 32-column chunks
     const int row = lg * 32 + lane;
     if (threadIdx.x == 64) *flag = mbar_wait_bounded(acc_full, 0, a.max_polls) ? 1 : 0;
     epi_sync();
@@ -407,7 +414,7 @@ linear_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CU
       tc_fence_after();
       const uint32_t trow = tmem + ((uint32_t)(lg * 32) << 16);
       if (a.splits == 1) {
-        for (int c0 = 0; c0 < kCols; c0 += 32) {
+        for (int c0 = 32 * part; c0 < kCols; c0 += 32 * kLinEpiParts) {
           uint32_t r[32];
           float v[32], u[32];
           tmem_ld32(trow + c0, r);
@@ -425,7 +432,7 @@ linear_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CU
         // (the stage buffers are idle once every MMA has completed), summed
         // across the cluster below
         float *tile_s = reinterpret_cast<float *>(smem) + row * (BN + 4);
-        for (int c0 = 0; c0 < BN; c0 += 32) {
+        for (int c0 = 32 * part; c0 < BN; c0 += 32 * kLinEpiParts) {
           uint32_t r[32];
           tmem_ld32(trow + c0, r);
 #pragma unroll
