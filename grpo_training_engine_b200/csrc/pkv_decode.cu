@@ -785,9 +785,6 @@ __device__ __forceinline__ uint32_t slab_chunk_offset(int c) {
   return (cc >> 3) * kBoxBytes + r * 128 + (((cc & 7) ^ (r & 7)) << 4);
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
 // 16-byte copy of which only the first src_bytes are read; the rest are zero
 __device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void *src, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");

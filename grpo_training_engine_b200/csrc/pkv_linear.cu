@@ -24,10 +24,10 @@
 //   warp 1             : allocates the TMEM accumulator; one thread issues
 //                        tcgen05.mma (M 128, N BN, K 16) per 16 K and commits
 //                        each stage back to the producer
-//   warps 2-9          : epilogue: tcgen05.ld of the accumulator (warp w reads
-//                        TMEM lanes 32 (w % 4) ..., two warps per lane group
-//                        on alternate 32-column chunks), bias / activation,
-//                        bf16 stores.
+//   warps 2-17 / 2-9   : epilogue: tcgen05.ld of the accumulator (warp w reads
+//                        TMEM lanes 32 (w % 4) ..., four (two with a K split)
+//                        warps per lane group on interleaved 16- (32-) column
+//                        chunks), bias / activation, bf16 stores.
 // Narrow matrices (N of a few thousand) are split along K so that ~148 CTAs
 // stream every weight matrix. The splits of a tile are the CTAs of one thread-
 // block cluster: each leaves its fp32 partial tile in its own shared memory,
@@ -54,13 +54,21 @@ namespace {
 
 constexpr int kLinBM = 128;      // rows of the MMA (all activation rows)
 constexpr int kLinBK = 64;       // K elements per stage: one 128-byte swizzle row of 16-bit values
-// warp 0 TMA, warp 1 MMA, warps 2-9 epilogue: two warps per 32-lane TMEM
-// group, each taking every other 32-column chunk (with one warp per group the
-// epilogue's dependent convert / SiLU chains took ~5 us of a gate/up launch)
-constexpr int kLinEpiWarps = 8;
-constexpr int kLinEpiParts = kLinEpiWarps / 4;  // warps per TMEM lane group
-constexpr int kLinThreads = 64 + 32 * kLinEpiWarps;
-constexpr int kLinEpiThreads = 32 * kLinEpiWarps;
+// Warp 0 TMA, warp 1 MMA, warps 2 .. 2 + EW - 1 epilogue: EW / 4 warps per
+// 32-lane TMEM group, each taking every (EW / 4)-th chunk of accumulator
+// columns. With one warp per group the epilogue's dependent convert / SiLU
+// chains took ~5 us of a gate/up launch; tiles stored straight from TMEM use
+// 16 warps on 16-column chunks (3.6 -> 3.0 us), split-K tiles, whose partials
+// go to shared memory and whose cluster reduction uses every thread, 8 warps
+// on 32-column chunks (16 measured slower there).
+template <int EW>
+struct LinEpi {
+  static constexpr int kParts = EW / 4;              // warps per TMEM lane group
+  static constexpr int kChunk = EW >= 16 ? 16 : 32;  // accumulator columns per tcgen05.ld
+  static constexpr int kThreads = 64 + 32 * EW;      // threads of the CTA
+  static constexpr int kEpiThreads = 32 * EW;
+  static_assert(EW % 4 == 0 && 64 + 32 * EW <= 1024, "epilogue warps: a multiple of 4, at most 30");
+};
 constexpr int kLinEpiBarrier = 1;  // named barrier of the epilogue warps
 constexpr int kLinMaxSplits = 8;   // K splits of a tile: the CTAs of one (portable) cluster
 
@@ -138,26 +146,37 @@ __host__ __device__ constexpr uint32_t mma_idesc(bool bf16, int n) {
          ((uint32_t)(kLinBM >> 4) << 24);
 }
 
-// 32 consecutive fp32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
-        "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
-        "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
-        "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-      : "r"(taddr));
+// NC (16 or 32) consecutive fp32 columns of this thread's TMEM lane.
+template <int NC>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&v)[NC]) {
+  static_assert(NC == 16 || NC == 32, "tcgen05.ld 32x32b .x16 or .x32");
+  if constexpr (NC == 16) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+  } else {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+          "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
+          "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
+          "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+  }
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 // Barrier of the epilogue threads. One lane may arrive later than the
 // rest of its warp (it waited on an mbarrier alone), so the warp reconverges
 // first and the barrier is the non-aligned form.
+template <int NT>
 __device__ __forceinline__ void epi_sync() {
   __syncwarp();
-  asm volatile("barrier.sync %0, %1;" ::"n"(kLinEpiBarrier), "n"(kLinEpiThreads) : "memory");
+  asm volatile("barrier.sync %0, %1;" ::"n"(kLinEpiBarrier), "n"(NT) : "memory");
 }
 
 // Barrier over every thread of every CTA of the cluster, with release /
@@ -221,16 +240,16 @@ template <int BN> struct TmemCols {
 __device__ __forceinline__ uint32_t bits16(__nv_bfloat16 v) { return __bfloat16_as_ushort(v); }
 __device__ __forceinline__ uint32_t bits16(__half v) { return __half_as_ushort(v); }
 
-// Final value of 32 columns of one row: bias / activation, rounding, store.
-template <typename T, int ACT>
-__device__ __forceinline__ void store_row32(const LinArgs &a, int row, int col0, const float (&v)[32],
-                                            const float (&up)[32]) {
+// Final value of NC columns of one row: bias / activation, rounding, store.
+template <typename T, int ACT, int NC>
+__device__ __forceinline__ void store_row(const LinArgs &a, int row, int col0, const float (&v)[NC],
+                                          const float (&up)[NC]) {
   using C = LinCvt<T>;
   T *out = reinterpret_cast<T *>(a.out) + row * a.out_stride;
   const T *bias = reinterpret_cast<const T *>(a.bias);
-  T o[32];
+  T o[NC];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
+  for (int j = 0; j < NC; ++j) {
     if constexpr (ACT == kActSiluGate) {
       // HF Qwen2MLP: gate and up rounded as GEMM outputs, silu rounded, product rounded
       const float g = C::f(C::t(v[j]));
@@ -241,9 +260,9 @@ __device__ __forceinline__ void store_row32(const LinArgs &a, int row, int col0,
       o[j] = C::t(bias != nullptr && c < a.n ? v[j] + C::f(bias[c]) : v[j]);
     }
   }
-  if (col0 + 32 <= a.n && (reinterpret_cast<uintptr_t>(out + col0) & 15) == 0) {
+  if (col0 + NC <= a.n && (reinterpret_cast<uintptr_t>(out + col0) & 15) == 0) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < NC / 8; ++q) {
       uint4 w;
       w.x = bits16(o[8 * q + 0]) | (bits16(o[8 * q + 1]) << 16);
       w.y = bits16(o[8 * q + 2]) | (bits16(o[8 * q + 3]) << 16);
@@ -253,7 +272,7 @@ __device__ __forceinline__ void store_row32(const LinArgs &a, int row, int col0,
     }
   } else {
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
+    for (int j = 0; j < NC; ++j)
       if (col0 + j < a.n) out[col0 + j] = o[j];
   }
 }
@@ -279,11 +298,12 @@ __device__ __forceinline__ void store_4(const LinArgs &a, int row, int col, floa
   }
 }
 
-template <typename T, int BN, int S, int ACT>
-__global__ void __launch_bounds__(kLinThreads, 1)
+template <typename T, int BN, int S, int ACT, int EW>
+__global__ void __launch_bounds__(LinEpi<EW>::kThreads, 1)
 linear_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw,
               const __grid_constant__ CUtensorMap tu, LinArgs a) {
   using L = LinSmem<BN, S>;
+  using E = LinEpi<EW>;
   extern __shared__ uint8_t lin_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(lin_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t *sa = smem;           // S x tiles (1024-byte aligned: kA is a multiple of 1024)
@@ -402,41 +422,41 @@ linear_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CU
   } else {
     // ============================ epilogue ================================
     const int lg = warp & 3;  // TMEM lanes 32 lg .. 32 lg + 31 are readable by this warp
-    const int part = (warp - 2) >> 2;  // which of the group's warps: its 32-column chunks
+    const int part = (warp - 2) >> 2;  // which of the group's warps: its column chunks
     const int row = lg * 32 + lane;
     if (threadIdx.x == 64) *flag = mbar_wait_bounded(acc_full, 0, a.max_polls) ? 1 : 0;
-    epi_sync();
+    epi_sync<E::kEpiThreads>();
     const bool ready = *flag != 0;
-    epi_sync();  // every epilogue thread has read the flag before it is reused
+    epi_sync<E::kEpiThreads>();  // every epilogue thread has read the flag before it is reused
     if (!ready) {
       if (threadIdx.x == 64) flag_status(a.status, PKV_DEV_WAIT_TIMEOUT);
     } else {
       tc_fence_after();
       const uint32_t trow = tmem + ((uint32_t)(lg * 32) << 16);
       if (a.splits == 1) {
-        for (int c0 = 32 * part; c0 < kCols; c0 += 32 * kLinEpiParts) {
-          uint32_t r[32];
-          float v[32], u[32];
-          tmem_ld32(trow + c0, r);
+        for (int c0 = E::kChunk * part; c0 < kCols; c0 += E::kChunk * E::kParts) {
+          uint32_t r[E::kChunk];
+          float v[E::kChunk], u[E::kChunk];
+          tmem_ld<E::kChunk>(trow + c0, r);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          for (int j = 0; j < E::kChunk; ++j) v[j] = __uint_as_float(r[j]);
           if constexpr (ACT == kActSiluGate) {
-            tmem_ld32(trow + BN / 2 + c0, r);
+            tmem_ld<E::kChunk>(trow + BN / 2 + c0, r);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) u[j] = __uint_as_float(r[j]);
+            for (int j = 0; j < E::kChunk; ++j) u[j] = __uint_as_float(r[j]);
           }
-          if (row < a.rows && n0 + c0 < a.n) store_row32<T, ACT>(a, row, n0 + c0, v, u);
+          if (row < a.rows && n0 + c0 < a.n) store_row<T, ACT, E::kChunk>(a, row, n0 + c0, v, u);
         }
       } else {
         // split-K: this split's fp32 partial tile into its own shared memory
         // (the stage buffers are idle once every MMA has completed), summed
         // across the cluster below
         float *tile_s = reinterpret_cast<float *>(smem) + row * (BN + 4);
-        for (int c0 = 32 * part; c0 < BN; c0 += 32 * kLinEpiParts) {
-          uint32_t r[32];
-          tmem_ld32(trow + c0, r);
+        for (int c0 = E::kChunk * part; c0 < BN; c0 += E::kChunk * E::kParts) {
+          uint32_t r[E::kChunk];
+          tmem_ld<E::kChunk>(trow + c0, r);
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
+          for (int q = 0; q < E::kChunk / 4; ++q)
             reinterpret_cast<float4 *>(tile_s + c0)[q] =
                 make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
                             __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
@@ -458,7 +478,7 @@ linear_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CU
     const uint32_t base = smem_u32(smem);
     constexpr int kC4 = kCols / 4;
     const int my_rows = (kLinBM - split + a.splits - 1) / a.splits;
-    for (int it = threadIdx.x; it < my_rows * kC4; it += kLinThreads) {
+    for (int it = threadIdx.x; it < my_rows * kC4; it += E::kThreads) {
       const int row = split + (it / kC4) * a.splits, c4 = it % kC4;
       if (row >= a.rows || n0 + 4 * c4 >= a.n) continue;
       const uint32_t off = (uint32_t)((row * (BN + 4) + 4 * c4) * sizeof(float));
@@ -578,18 +598,18 @@ LinPlan lin_plan(int32_t n, int32_t k, int32_t act, int sms) {
   return p;
 }
 
-template <typename T, int BN, int S, int ACT>
+template <typename T, int BN, int S, int ACT, int EW>
 int lin_launch(const CUtensorMap &tx, const CUtensorMap &tw, const CUtensorMap &tu, const LinArgs &a,
                cudaStream_t st) {
   using L = LinSmem<BN, S>;
   static_assert(L::kBytes <= 227 * 1024, "linear kernel exceeds 227 KB of shared memory");
   static_assert(kLinBM * (BN + 4) * sizeof(float) <= L::kFull, "the split-K partial tile fits the ring");
-  auto kern = linear_kernel<T, BN, S, ACT>;
+  auto kern = linear_kernel<T, BN, S, ACT, EW>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kBytes) != cudaSuccess)
     return check_launch("cudaFuncSetAttribute(linear)");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(a.tiles * a.splits));
-  cfg.blockDim = dim3(kLinThreads);
+  cfg.blockDim = dim3(LinEpi<EW>::kThreads);
   cfg.dynamicSmemBytes = L::kBytes;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
@@ -608,10 +628,15 @@ int lin_launch(const CUtensorMap &tx, const CUtensorMap &tw, const CUtensorMap &
 template <typename T>
 int lin_dispatch(const CUtensorMap &tx, const CUtensorMap &tw, const CUtensorMap &tu, const LinArgs &a, int bn,
                  int act, cudaStream_t st) {
-  if (act == kActSiluGate) return lin_launch<T, 128, 6, kActSiluGate>(tx, tw, tu, a, st);
-  if (bn == 256) return lin_launch<T, 256, 4, kActNone>(tx, tw, tu, a, st);
-  if (bn == 128) return lin_launch<T, 128, 6, kActNone>(tx, tw, tu, a, st);
-  return lin_launch<T, 64, 8, kActNone>(tx, tw, tu, a, st);
+  // 16 epilogue warps where tiles are stored from TMEM, 8 where they are summed
+  // across a K-split cluster (the plan never splits gate/up or 256-column tiles)
+  if (act == kActSiluGate) return lin_launch<T, 128, 6, kActSiluGate, 16>(tx, tw, tu, a, st);
+  if (bn == 256) return lin_launch<T, 256, 4, kActNone, 16>(tx, tw, tu, a, st);
+  if (bn == 128)
+    return a.splits > 1 ? lin_launch<T, 128, 6, kActNone, 8>(tx, tw, tu, a, st)
+                        : lin_launch<T, 128, 6, kActNone, 16>(tx, tw, tu, a, st);
+  return a.splits > 1 ? lin_launch<T, 64, 8, kActNone, 8>(tx, tw, tu, a, st)
+                      : lin_launch<T, 64, 8, kActNone, 16>(tx, tw, tu, a, st);
 }
 
 }  // namespace
