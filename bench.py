@@ -949,6 +949,71 @@ def run_sample(args):
                       "results": out}), flush=True)
 
 
+# ----------------------------------------------------------------------------- host cost of eager calls
+def run_host(args):
+    """Host-to-host cost of eager calls through the public API on a launch-bound case (8 sequences of
+    64 tokens, 12q/2kv, D 128, bf16 cache, block size 16), where the GPU work of a call is a few µs:
+    wall-clock time (time.perf_counter) around --steps x 100 back-to-back calls with one synchronize
+    at the end, after --warmup x 100 calls; median of 5 such runs. Cases: the fused append + decode
+    with a plan made once, the same with the plan made by the call, the decode alone, one step of the
+    reference-facing low-level driver paged_kv_decode (fused append + decode, greedy pick, its per-step
+    finished check; projections and logits precomputed), and a torch.add of two 8-element tensors for
+    the scale of one torch launch."""
+    from grpo_training_engine_b200 import paged_attention_decode, plan_decode
+    from grpo_training_engine_b200.paged_kv import paged_kv_decode  # the low-level driver
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    b, hq, hkv, d, bs, ctx_len, new = 8, 12, 2, 128, 16, 64, 32
+    max_blocks = (ctx_len + new) // bs + 1
+    nblk = b * max_blocks
+    kc = torch.randn(nblk, hkv, bs, d, device=dev, generator=g).to(torch.bfloat16)
+    vc = torch.randn(nblk, hkv, bs, d, device=dev, generator=g).to(torch.bfloat16)
+    bt = torch.arange(nblk, device=dev, dtype=torch.int32).reshape(b, max_blocks)
+    ctx = torch.full((b,), ctx_len, dtype=torch.int32, device=dev)
+    q = torch.randn(b, hq, d, device=dev, generator=g).to(torch.bfloat16)
+    kn = torch.randn(b, hkv, d, device=dev, generator=g).to(torch.bfloat16)
+    vn = torch.randn(b, hkv, d, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty(b, hq, d, device=dev)
+    plan = plan_decode(ctx, hq, hkv, d, bs, max_blocks)
+    logits = torch.randn(b, 1000, device=dev, generator=g)
+    ids = torch.randint(0, 1000, (b, 1), device=dev, generator=g)
+    s8 = torch.ones(8, device=dev)
+    s8o = torch.empty(8, device=dev)
+
+    def driver_step():
+        paged_kv_decode(ids, kc, vc, bt, ctx, lambda t: (q, kn, vn), lambda a: logits, max_new_tokens=new,
+                        do_sample=False)
+
+    cases = [
+        ("append_decode_plan_reused", 1, lambda: paged_attention_decode(q, kc, vc, bt, ctx, out=out, plan=plan,
+                                                                         k_new=kn, v_new=vn)),
+        ("append_decode_plan_per_call", 1, lambda: paged_attention_decode(q, kc, vc, bt, ctx, out=out,
+                                                                           k_new=kn, v_new=vn)),
+        ("decode_plan_reused", 1, lambda: paged_attention_decode(q, kc, vc, bt, ctx, out=out, plan=plan)),
+        ("paged_kv_decode_step", new, driver_step),
+        ("torch_add_8", 1, lambda: torch.add(s8, s8, out=s8o)),
+    ]
+    res = {}
+    for name, per_call, fn in cases:
+        calls = max(1, 100 // per_call)
+        for _ in range(args.warmup * calls):
+            fn()
+        torch.cuda.synchronize()
+        runs = []
+        for _ in range(5):
+            t0 = time.perf_counter()
+            for _ in range(args.steps * calls):
+                fn()
+            torch.cuda.synchronize()
+            runs.append((time.perf_counter() - t0) * 1e6 / (args.steps * calls * per_call))
+        res[name] = round(statistics.median(runs), 2)
+    print(json.dumps({"metric": "host-to-host time per eager call (launch-bound case), us", "unit": "us",
+                      "case": f"{b} seqs x {ctx_len} tokens, {hq}q/{hkv}kv, D {d}, bf16, bs {bs}",
+                      "timing": "perf_counter around back-to-back calls, one synchronize, median of 5",
+                      "results": res}), flush=True)
+
+
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args, rank, world):
     """CPU restatement of the reference algorithm on the host cores (the reference is
@@ -1075,6 +1140,8 @@ def main():
                     help="time the projection GEMM (pkv_linear) against cuBLAS on the rollout step's shapes")
     ap.add_argument("--sample", action="store_true",
                     help="time the top-p sampling kernels (bf16 and fp32 logits) against the radix path")
+    ap.add_argument("--host", action="store_true",
+                    help="host-to-host time per eager call of the decode API on a launch-bound case")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
@@ -1092,6 +1159,9 @@ def main():
         return
     if args.sample:
         run_sample(args)
+        return
+    if args.host:
+        run_host(args)
         return
     rank, world, local = dist_setup(args)
     if args.impl == "reference":
