@@ -173,12 +173,15 @@ def paged_kv_decode(
     scale = 1.0 / math.sqrt(head_dim)
 
     any_finished = False
+    # without an EOS id no row ever finishes, so the reference's per-step
+    # finished.all() check (a host sync) always reads False and is skipped
+    track_finished = eos >= 0
     for step in range(max_new_tokens):
-        # one host sync per step, as the reference's finished.all() check
-        all_done, any_finished = (
-            torch.stack([finished.all(), finished.any()]).tolist() if step else (False, False))
-        if all_done:
-            break
+        if step and track_finished:
+            # one host sync per step, as the reference's finished.all() check
+            all_done, any_finished = torch.stack([finished.all(), finished.any()]).tolist()
+            if all_done:
+                break
         q, k_new, v_new = qkv_proj_fn(last_tokens)
         if q.ndim != 3 or q.shape[0] != batch_size or q.shape[2] != head_dim or q.shape[1] % num_heads != 0:
             raise ValueError("qkv_proj_fn must return [B, H, D] tensors.")
@@ -204,10 +207,11 @@ def paged_kv_decode(
         if logits.ndim != 2 or logits.shape[0] != batch_size:
             raise ValueError("logits_fn must return [B, vocab] logits.")
         next_tokens = _sample_tokens(logits, do_sample, temperature, top_p, generator)
-        next_tokens = torch.where(finished, input_ids[:, 0], next_tokens)
+        if track_finished:
+            next_tokens = torch.where(finished, input_ids[:, 0], next_tokens)
         generated[:, step] = next_tokens
         last_tokens = next_tokens
-        if eos >= 0:
+        if track_finished:
             finished = finished | (next_tokens == eos)
     return generated
 
