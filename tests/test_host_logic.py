@@ -52,6 +52,68 @@ def test_low_level_rejects_nonpositive_tokens():
                                  a["context_lens"], lambda x: x, lambda x: x, max_new_tokens=0)
 
 
+def _fake_low_level(monkeypatch, script, vocab=16):
+    """The low-level driver with its kernels replaced by fakes that record the
+    lengths they get, and logits_fn replaced by a script of greedy tokens (one
+    row of tokens per step). Returns (run, calls)."""
+    calls = []
+
+    def fake_decode(q, k_cache, v_cache, block_tables, context_lens, scale=None, k_new=None, v_new=None, **kw):
+        calls.append(("fused" if k_new is not None else "decode", context_lens.tolist()))
+        return torch.zeros(q.shape, dtype=torch.float32)
+
+    def fake_append(k_new, v_new, k_cache, v_cache, block_tables, context_lens):
+        calls.append(("append", context_lens.tolist()))
+
+    monkeypatch.setattr(paged_kv.ops, "paged_attention_decode", fake_decode)
+    monkeypatch.setattr(paged_kv.ops, "paged_kv_append", fake_append)
+    monkeypatch.setattr(paged_kv, "_validate_inputs", lambda *a: (2, 4, 8, 64))
+    step = iter(script)
+
+    def logits_fn(attn):
+        return torch.nn.functional.one_hot(torch.tensor(next(step)), vocab).float()
+
+    def run(ctx, eos, new):
+        a = _args()
+        ids = torch.tensor([[13, 1], [14, 2]])
+        q = torch.zeros(2, 2, 8, dtype=torch.bfloat16)
+        return paged_kv.paged_kv_decode(ids, a["k_cache"], a["v_cache"], a["block_tables"],
+                                        torch.tensor(ctx, dtype=torch.int32), lambda t: (q, q, q), logits_fn,
+                                        max_new_tokens=new, do_sample=False, eos_token_id=eos, pad_token_id=15)
+
+    return run, calls
+
+
+def test_low_level_steps_without_eos(monkeypatch):
+    """No EOS id: every row advances one position per step through the fused
+    append + decode, for max_new_tokens steps (paged_kv.py:840-985)."""
+    run, calls = _fake_low_level(monkeypatch, [[1, 2], [3, 4], [5, 6]])
+    out = run([10, 20], None, 3)
+    assert out.tolist() == [[1, 3, 5], [2, 4, 6]]
+    assert calls == [("fused", [11, 21]), ("fused", [12, 22]), ("fused", [13, 23])]
+
+
+def test_low_level_steps_with_eos(monkeypatch):
+    """Row 1 emits EOS (9) at step 1: from step 2 it keeps its length (append at
+    the unchanged length, then decode over the others' new lengths) and
+    re-emits input_ids[1, 0]; row 0 keeps advancing."""
+    run, calls = _fake_low_level(monkeypatch, [[5, 6], [7, 9], [8, 10], [11, 12]])
+    out = run([10, 20], 9, 4)
+    assert out.tolist() == [[5, 7, 8, 11], [6, 9, 14, 14]]
+    assert calls == [("fused", [11, 21]), ("fused", [12, 22]),
+                     ("append", [12, 22]), ("decode", [13, 22]),
+                     ("append", [13, 22]), ("decode", [14, 22])]
+
+
+def test_low_level_stops_when_every_row_finished(monkeypatch):
+    """Both rows emit EOS by step 1: the loop stops before step 2, whose column
+    stays pad_token_id; row 0 re-emits input_ids[0, 0] at step 1."""
+    run, calls = _fake_low_level(monkeypatch, [[9, 6], [1, 9], [2, 3]])
+    out = run([10, 20], 9, 3)
+    assert out.tolist() == [[9, 13, 15], [6, 9, 15]]
+    assert [c[0] for c in calls] == ["fused", "append", "decode"]
+
+
 # ----------------------------------------------------------------------- façade
 def test_facade_routes_low_level(monkeypatch):
     seen = {}
